@@ -1,0 +1,36 @@
+// Launchers shared between the library's translation units.  Every pointer
+// is a device pointer; descriptor arrays hold device addresses as uint64.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace cb {
+
+int launch_sha256(const uint64_t *d_ptrs, const uint64_t *d_sizes, int n,
+                  uint8_t *d_digests, cudaStream_t s);
+
+int launch_minmax(const uint64_t *d_ptrs, const uint64_t *d_sizes, int n,
+                  uint64_t max_size, int2 *d_mnmx, cudaStream_t s);
+
+// header_inline=1: the reference layout (8-byte header, then codes) at
+// d_dsts[b]; header_inline=0: codes at d_dsts[b], header at d_headers+8*b.
+int launch_quantize(const uint64_t *d_ptrs, const uint64_t *d_sizes, int n,
+                    uint64_t max_size, const int2 *d_mnmx,
+                    const uint64_t *d_dsts, uint8_t *d_headers,
+                    int header_inline, cudaStream_t s);
+
+int launch_dequantize(const uint64_t *d_srcs, const uint8_t *d_headers,
+                      int header_inline, const uint64_t *d_out_sizes, int n,
+                      uint64_t max_out_size, const uint64_t *d_dsts,
+                      cudaStream_t s);
+
+int launch_copy(const uint64_t *d_srcs, const uint64_t *d_dsts,
+                const uint64_t *d_sizes, int n, uint64_t max_size,
+                cudaStream_t s);
+
+// out[i] = in[i] + delta
+int launch_offset_ptrs(const uint64_t *d_in, uint64_t delta, uint64_t *d_out,
+                       int n, cudaStream_t s);
+
+}  // namespace cb
