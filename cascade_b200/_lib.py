@@ -42,6 +42,7 @@ _SIGS = {
     "cascade_kv_decompress_batch": (_int, [_vp, _vp, _vp, _sz, _u64, _vp]),
     "cascade_copy_batch": (_int, [_vp, _vp, _vp, _sz, _u64, _vp]),
     "cascade_compute_block_id": (_int, [_vp, _u64, ctypes.c_char_p]),
+    "cascade_diag_launch_count": (ctypes.c_uint64, []),
     "cascade_diag_sha_peak": (_int, [_int, ctypes.c_uint32,
                                      ctypes.POINTER(ctypes.c_double),
                                      ctypes.POINTER(ctypes.c_double)]),

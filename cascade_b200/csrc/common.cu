@@ -1,5 +1,6 @@
 // Error reporting, small utility kernels and the device diagnostics behind
 // the C-ABI.
+#include <atomic>
 #include <cstdio>
 #include <cstring>
 #include <string>
@@ -12,6 +13,7 @@ namespace cb {
 
 namespace {
 thread_local std::string g_error;
+std::atomic<uint64_t> g_launches{0};
 
 __global__ void offset_ptrs_kernel(const uint64_t *in, uint64_t delta,
                                    uint64_t *out, int n) {
@@ -37,6 +39,8 @@ __global__ void __launch_bounds__(256)
 }
 }  // namespace
 
+void count_launches(int k) { g_launches.fetch_add((uint64_t)k); }
+
 void set_error(const std::string &msg) { g_error = msg; }
 void clear_error() { g_error.clear(); }
 const char *last_error() { return g_error.c_str(); }
@@ -50,6 +54,7 @@ int launch_offset_ptrs(const uint64_t *d_in, uint64_t delta, uint64_t *d_out,
                        int n, cudaStream_t s) {
   if (n <= 0) return CASCADE_OK;
   offset_ptrs_kernel<<<(n + 255) / 256, 256, 0, s>>>(d_in, delta, d_out, n);
+  count_launches(1);
   CB_CUDA(cudaGetLastError());
   return CASCADE_OK;
 }
@@ -59,6 +64,10 @@ int launch_offset_ptrs(const uint64_t *d_in, uint64_t delta, uint64_t *d_out,
 extern "C" const char *cascade_last_error(void) { return cb::last_error(); }
 
 extern "C" int cascade_abi_version(void) { return CASCADE_ABI_VERSION; }
+
+extern "C" uint64_t cascade_diag_launch_count(void) {
+  return cb::g_launches.load();
+}
 
 extern "C" int cascade_diag_sha_peak(int device, uint32_t chunks_per_thread,
                                      double *gbps, double *ms) {

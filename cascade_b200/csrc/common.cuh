@@ -15,6 +15,9 @@ void set_error(const std::string &msg);
 void clear_error();
 const char *last_error();
 
+// Kernel launches made by this library since load (cascade_diag_launch_count).
+void count_launches(int k);
+
 // Records `what` + the CUDA error text and returns CASCADE_ERR_CUDA.
 int cuda_fail(cudaError_t e, const char *what);
 

@@ -252,10 +252,12 @@ int launch_minmax(const uint64_t *d_ptrs, const uint64_t *d_sizes, int n,
                   uint64_t max_size, int2 *d_mnmx, cudaStream_t s) {
   if (n <= 0) return CASCADE_OK;
   init_minmax_kernel<<<(n + 255) / 256, 256, 0, s>>>(d_mnmx, n);
+  count_launches(1);
   CB_CUDA(cudaGetLastError());
   const int tiles = (int)std::max<uint64_t>(1, div_up(max_size / 2, kTileElems));
   const int grid = grid_for((uint64_t)n * tiles, 1, 4);
   minmax_kernel<<<grid, kThreads, 0, s>>>(d_ptrs, d_sizes, n, tiles, d_mnmx);
+  count_launches(1);
   CB_CUDA(cudaGetLastError());
   return CASCADE_OK;
 }
@@ -269,6 +271,7 @@ int launch_quantize(const uint64_t *d_ptrs, const uint64_t *d_sizes, int n,
   const int grid = grid_for((uint64_t)n * tiles, 1, 4);
   quantize_kernel<<<grid, kThreads, 0, s>>>(d_ptrs, d_sizes, n, tiles, d_mnmx,
                                             d_dsts, d_headers, header_inline);
+  count_launches(1);
   CB_CUDA(cudaGetLastError());
   return CASCADE_OK;
 }
@@ -283,6 +286,7 @@ int launch_dequantize(const uint64_t *d_srcs, const uint8_t *d_headers,
   const int grid = grid_for((uint64_t)n * tiles, 1, 4);
   dequantize_kernel<<<grid, kThreads, 0, s>>>(d_srcs, d_headers, header_inline,
                                               d_out_sizes, n, tiles, d_dsts);
+  count_launches(1);
   CB_CUDA(cudaGetLastError());
   return CASCADE_OK;
 }
@@ -294,6 +298,7 @@ int launch_copy(const uint64_t *d_srcs, const uint64_t *d_dsts,
   const int tiles = (int)std::max<uint64_t>(1, div_up(max_size, kCopyTile));
   const int grid = grid_for((uint64_t)n * tiles, 1, 4);
   copy_kernel<<<grid, kThreads, 0, s>>>(d_srcs, d_dsts, d_sizes, n, tiles);
+  count_launches(1);
   CB_CUDA(cudaGetLastError());
   return CASCADE_OK;
 }

@@ -116,6 +116,7 @@ int launch_sha256(const uint64_t *d_ptrs, const uint64_t *d_sizes, int n,
   int blocks = (n + threads - 1) / threads;
   sha256_lane_per_block<<<blocks, threads, 0, s>>>(
       d_ptrs, d_sizes, n, reinterpret_cast<uint32_t *>(d_digests));
+  count_launches(1);
   CB_CUDA(cudaGetLastError());
   return CASCADE_OK;
 }

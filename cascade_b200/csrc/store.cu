@@ -1,0 +1,1272 @@
+// CascadeStore on a B200: host orchestration over the device index, the HBM
+// pool and the pinned DRAM tier.  Block bytes never pass through host code
+// except when a caller hands over host buffers (staged through pinned
+// memory) or a block lives in the DRAM tier.
+//
+// Reference: CascadeStore (cascade.hpp:420-502, cascade_core.cpp:960-1303),
+// GPUBackend (gpu_backend.cu:166-528), ShmBackend (cascade_core.cpp:237-569).
+#include <algorithm>
+#include <cstring>
+#include <memory>
+#include <mutex>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "common.cuh"
+#include "dram.cuh"
+#include "kernels.cuh"
+#include "store_dev.cuh"
+
+namespace cb {
+
+namespace {
+
+// ------------------------------------------------------------ helpers
+struct DeviceGuard {
+  int prev = -1;
+  explicit DeviceGuard(int dev) {
+    cudaGetDevice(&prev);
+    if (prev != dev) cudaSetDevice(dev);
+  }
+  ~DeviceGuard() {
+    int cur = -1;
+    cudaGetDevice(&cur);
+    if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+  }
+};
+
+inline uint64_t pow2_at_least(uint64_t x) {
+  uint64_t p = 1;
+  while (p < x) p <<= 1;
+  return p;
+}
+
+inline bool is_hex_id(const char *s, size_t len) {
+  if (len != 32) return false;
+  for (size_t i = 0; i < 32; ++i) {
+    char c = s[i];
+    if (!((c >= '0' && c <= '9') || (c >= 'a' && c <= 'f'))) return false;
+  }
+  return true;
+}
+
+inline int hexval(char c) { return c <= '9' ? c - '0' : c - 'a' + 10; }
+
+// Little-endian load of 8 key bytes.
+inline uint64_t le64(const uint8_t *b) {
+  uint64_t v = 0;
+  for (int i = 7; i >= 0; --i) v = (v << 8) | b[i];
+  return v;
+}
+
+// After the pool allocation: final offsets, payload destinations and the
+// per-format byte counts the payload kernels consume (0 = skip block).
+__global__ void prepare_kernel(int n, const uint64_t *__restrict__ req,
+                               uint64_t *__restrict__ off,
+                               const uint64_t *__restrict__ off_host,
+                               const uint64_t *__restrict__ dst_host,
+                               const uint32_t *__restrict__ flags,
+                               const uint64_t *__restrict__ sizes,
+                               uint64_t pool_base, uint64_t *__restrict__ dst,
+                               uint64_t *__restrict__ eff_raw,
+                               uint64_t *__restrict__ eff_q8) {
+  int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  uint64_t d = 0, o;
+  if (req[i] != kNoRequest) {  // an HBM placement
+    o = off[i];
+    if (o != kInvalidOffset) d = pool_base + o;
+  } else {  // a DRAM placement (offset chosen on the host) or nothing
+    o = off_host[i];
+    d = dst_host[i];
+  }
+  off[i] = o;
+  dst[i] = d;
+  const bool q8 = (flags[i] & kFlagQ8) != 0;
+  eff_q8[i] = (d && q8) ? sizes[i] : 0;
+  eff_raw[i] = (d && !q8) ? sizes[i] : 0;
+}
+
+}  // namespace
+
+// ------------------------------------------------------------- scratch
+// Per-batch device arrays and their pinned host mirrors, carved from two
+// blobs with the same layout.
+struct Scratch {
+  size_t cap = 0;
+  uint8_t *dblob = nullptr, *hblob = nullptr;
+  // arrays: device pointer, host mirror
+  uint64_t *ptrs, *h_ptrs, *sizes, *h_sizes, *seqs, *h_seqs, *keys, *h_keys;
+  uint64_t *req, *h_req, *off, *h_off, *dst, *h_dst, *eff_raw, *eff_q8;
+  uint64_t *hoff, *hdst;  // device copies of h_off / h_dst
+  uint8_t *digests, *h_digests, *status, *h_status, *hdr, *h_hdr;
+  uint32_t *slot, *h_slot, *flags, *h_flags;
+  int2 *mnmx;
+  LookupInfo *info, *h_info;
+  int *err, *h_err;
+};
+
+struct Store {
+  cascade_config_t cfg;
+  std::string shm_path, lustre_path;
+  int dev = 0;
+  bool hbm = false, dram_tier = false;
+  cudaStream_t s = nullptr;
+  cudaEvent_t ev = nullptr;
+  uint8_t *pool = nullptr;
+  uint64_t pool_cap = 0;
+  PoolDev *d_pool = nullptr;
+  uint64_t *stack_ptr[kNumClasses] = {};
+  Slot *slots = nullptr;
+  uint64_t nslots = 0;
+  uint64_t claimed = 0;  // keys that own a slot (upper bound)
+  std::unique_ptr<DramArena> dram;
+  Scratch sc;
+  uint8_t *d_stage = nullptr;  // device staging for host buffers
+  size_t d_stage_cap = 0;
+  uint8_t *h_stage = nullptr;  // pinned staging for host buffers
+  size_t h_stage_cap = 0;
+  uint8_t *d_q8stage = nullptr;  // INT8 payloads on their way to DRAM
+  size_t d_q8stage_cap = 0;
+  std::mutex mu;
+  uint64_t next_seq = 1, next_epoch = 1, next_name = 1;
+  std::unordered_map<std::string, Key> names;
+  // CascadeStore::Stats counters (cascade.hpp:439-456)
+  uint64_t gpu_used = 0, shm_used = 0, gpu_hits = 0, shm_hits = 0,
+           misses = 0, dedup_hits = 0, gpu_evictions = 0,
+           promotions_to_gpu = 0, compression_savings = 0, shm_puts = 0;
+};
+
+namespace {
+
+template <typename T>
+T *carve(uint8_t *&p, size_t count) {
+  T *r = reinterpret_cast<T *>(p);
+  p += (count * sizeof(T) + 255) & ~size_t(255);
+  return r;
+}
+
+size_t scratch_bytes(size_t c) {
+  uint8_t *p = nullptr;
+  carve<uint64_t>(p, c); carve<uint64_t>(p, c); carve<uint64_t>(p, c);
+  carve<uint64_t>(p, 2 * c); carve<uint64_t>(p, c); carve<uint64_t>(p, c);
+  carve<uint64_t>(p, c); carve<uint64_t>(p, c); carve<uint64_t>(p, c);
+  carve<uint64_t>(p, c); carve<uint64_t>(p, c);
+  carve<uint8_t>(p, 32 * c); carve<uint8_t>(p, c); carve<uint8_t>(p, 8 * c);
+  carve<uint32_t>(p, c); carve<uint32_t>(p, c); carve<int2>(p, c);
+  carve<LookupInfo>(p, c); carve<int>(p, 1);
+  return (size_t)(p - (uint8_t *)nullptr);
+}
+
+void carve_all(Scratch &S, uint8_t *base, bool host) {
+  uint8_t *p = base;
+  uint64_t *ptrs = carve<uint64_t>(p, S.cap);
+  uint64_t *sizes = carve<uint64_t>(p, S.cap);
+  uint64_t *seqs = carve<uint64_t>(p, S.cap);
+  uint64_t *keys = carve<uint64_t>(p, 2 * S.cap);
+  uint64_t *req = carve<uint64_t>(p, S.cap);
+  uint64_t *off = carve<uint64_t>(p, S.cap);
+  uint64_t *dst = carve<uint64_t>(p, S.cap);
+  uint64_t *eff_raw = carve<uint64_t>(p, S.cap);
+  uint64_t *eff_q8 = carve<uint64_t>(p, S.cap);
+  uint64_t *hoff = carve<uint64_t>(p, S.cap);
+  uint64_t *hdst = carve<uint64_t>(p, S.cap);
+  uint8_t *digests = carve<uint8_t>(p, 32 * S.cap);
+  uint8_t *status = carve<uint8_t>(p, S.cap);
+  uint8_t *hdr = carve<uint8_t>(p, 8 * S.cap);
+  uint32_t *slot = carve<uint32_t>(p, S.cap);
+  uint32_t *flags = carve<uint32_t>(p, S.cap);
+  int2 *mnmx = carve<int2>(p, S.cap);
+  LookupInfo *info = carve<LookupInfo>(p, S.cap);
+  int *err = carve<int>(p, 1);
+  if (host) {
+    S.h_ptrs = ptrs; S.h_sizes = sizes; S.h_seqs = seqs; S.h_keys = keys;
+    S.h_req = req; S.h_off = off; S.h_dst = dst; S.h_digests = digests;
+    S.h_status = status; S.h_hdr = hdr; S.h_slot = slot; S.h_flags = flags;
+    S.h_info = info; S.h_err = err;
+    (void)eff_raw; (void)eff_q8; (void)mnmx; (void)hoff; (void)hdst;
+  } else {
+    S.ptrs = ptrs; S.sizes = sizes; S.seqs = seqs; S.keys = keys;
+    S.req = req; S.off = off; S.dst = dst; S.eff_raw = eff_raw;
+    S.eff_q8 = eff_q8; S.hoff = hoff; S.hdst = hdst; S.digests = digests; S.status = status; S.hdr = hdr;
+    S.slot = slot; S.flags = flags; S.mnmx = mnmx; S.info = info;
+    S.err = err;
+  }
+}
+
+int ensure_scratch(Store &st, size_t n) {
+  if (n <= st.sc.cap) return CASCADE_OK;
+  size_t cap = std::max<size_t>(n, std::max<size_t>(1024, 2 * st.sc.cap));
+  CB_CUDA(cudaStreamSynchronize(st.s));
+  if (st.sc.dblob) cudaFree(st.sc.dblob);
+  if (st.sc.hblob) cudaFreeHost(st.sc.hblob);
+  st.sc = Scratch();
+  size_t bytes = scratch_bytes(cap);
+  CB_CUDA(cudaMalloc(&st.sc.dblob, bytes));
+  CB_CUDA(cudaHostAlloc(&st.sc.hblob, bytes, cudaHostAllocDefault));
+  st.sc.cap = cap;
+  carve_all(st.sc, st.sc.dblob, false);
+  carve_all(st.sc, st.sc.hblob, true);
+  return CASCADE_OK;
+}
+
+int ensure_device_buf(uint8_t *&buf, size_t &cap, size_t need,
+                      cudaStream_t s) {
+  if (need <= cap) return CASCADE_OK;
+  CB_CUDA(cudaStreamSynchronize(s));
+  if (buf) CB_CUDA(cudaFree(buf));
+  buf = nullptr;
+  cap = 0;
+  size_t c = std::max<size_t>(need, 1 << 20);
+  CB_CUDA(cudaMalloc(&buf, c));
+  cap = c;
+  return CASCADE_OK;
+}
+
+int ensure_host_stage(Store &st, size_t need) {
+  if (need <= st.h_stage_cap) return CASCADE_OK;
+  CB_CUDA(cudaStreamSynchronize(st.s));
+  if (st.h_stage) CB_CUDA(cudaFreeHost(st.h_stage));
+  st.h_stage = nullptr;
+  st.h_stage_cap = 0;
+  size_t c = std::max<size_t>(need, 1 << 20);
+  CB_CUDA(cudaHostAlloc(&st.h_stage, c, cudaHostAllocDefault));
+  st.h_stage_cap = c;
+  return CASCADE_OK;
+}
+
+// Free stacks exist for every class an allocation may use.
+int ensure_stack(Store &st, int c) {
+  if (st.stack_ptr[c]) return CASCADE_OK;
+  uint64_t by_pool = st.pool_cap / class_bytes(c) + 1;
+  uint64_t by_index = 2 * st.nslots;
+  uint64_t cap = std::min(by_pool, by_index);
+  if (cap > 0xffffffffull) cap = 0xffffffffull;
+  uint64_t *d = nullptr;
+  CB_CUDA(cudaMalloc(&d, cap * sizeof(uint64_t)));
+  uint32_t cap32 = (uint32_t)cap;
+  CB_CUDA(cudaMemcpyAsync(&st.d_pool->stack[c], &d, sizeof(d),
+                          cudaMemcpyHostToDevice, st.s));
+  CB_CUDA(cudaMemcpyAsync(&st.d_pool->cap[c], &cap32, sizeof(cap32),
+                          cudaMemcpyHostToDevice, st.s));
+  CB_CUDA(cudaStreamSynchronize(st.s));  // the sources live on this stack
+  st.stack_ptr[c] = d;
+  return CASCADE_OK;
+}
+
+int reset_pool(Store &st) {
+  if (!st.hbm) return CASCADE_OK;
+  PoolDev h;
+  std::memset(&h, 0, sizeof(h));
+  h.capacity = st.pool_cap;
+  for (int c = 0; c < kNumClasses; ++c) {
+    h.stack[c] = st.stack_ptr[c];
+    if (st.stack_ptr[c]) {
+      uint64_t cap = std::min(st.pool_cap / class_bytes(c) + 1, 2 * st.nslots);
+      h.cap[c] = (uint32_t)std::min<uint64_t>(cap, 0xffffffffull);
+    }
+  }
+  CB_CUDA(cudaMemcpyAsync(st.d_pool, &h, sizeof(h), cudaMemcpyHostToDevice,
+                          st.s));
+  CB_CUDA(cudaStreamSynchronize(st.s));
+  return CASCADE_OK;
+}
+
+// Key of a block-id string (see cascade_store_key_of).  Synthetic keys live
+// in the region k1 == ~0; a hex id falling there (or on the one unstorable
+// key) is mapped through the name table as well, so no two ids share a key.
+int key_of(Store &st, const char *id, bool create, Key *out, bool *known) {
+  size_t len = std::strlen(id);
+  *known = true;
+  if (is_hex_id(id, len)) {
+    uint8_t b[16];
+    for (int i = 0; i < 16; ++i)
+      b[i] = (uint8_t)(hexval(id[2 * i]) << 4 | hexval(id[2 * i + 1]));
+    Key k{le64(b), le64(b + 8)};
+    bool reserved = (k.k1 == ~0ull) || (k.k0 == kKeyMask0 && k.k1 == kKeyMask1);
+    if (!reserved) { *out = k; return CASCADE_OK; }
+  }
+  std::string sid(id, len);
+  auto it = st.names.find(sid);
+  if (it != st.names.end()) { *out = it->second; return CASCADE_OK; }
+  if (!create) { *known = false; return CASCADE_OK; }
+  Key k{st.next_name++, ~0ull};
+  st.names.emplace(std::move(sid), k);
+  *out = k;
+  return CASCADE_OK;
+}
+
+// Copies the kernel-side error word; non-zero aborts the operation.
+int check_device_err(Store &st) {
+  if (*st.sc.h_err) {
+    set_error("device index is full: raise index_slots");
+    return CASCADE_ERR_FULL;
+  }
+  return CASCADE_OK;
+}
+
+inline bool q8_eligible(const Store &st, uint64_t size, bool to_dram) {
+  if (!st.cfg.kv_compression || size < 64) return false;
+  return to_dram || st.cfg.gpu_q8;
+}
+
+inline uint64_t payload_bytes(uint64_t size, bool q8) {
+  return q8 ? size / 2 : size;
+}
+
+// What the reference's ShmBackend accounts for a stored block: the
+// compressed form is 8 + size/2 bytes (KVCompressor::compressed_size,
+// cascade.hpp:357-359).
+inline uint64_t dram_accounted(uint64_t size, bool q8) {
+  return q8 ? 8 + size / 2 : size;
+}
+
+// Doubles the index and re-inserts every live slot.
+int grow_index(Store &st);
+
+}  // namespace
+
+// ----------------------------------------------------------------- put
+// Core of every put: the inputs (device addresses, sizes, sequence numbers,
+// keys or digests) are already in st.sc on the device.
+//   use_digests: keys are sc.digests (stride 4) instead of sc.keys.
+//   h_prefix: per-block is_prefix or null.
+// On return st.sc.h_status holds the final per-block status.
+static int put_placed(Store &st, size_t n, bool use_digests,
+                      const uint8_t *h_prefix, uint64_t max_size) {
+  cudaStream_t s = st.s;
+  const uint64_t *keys = use_digests
+                             ? reinterpret_cast<const uint64_t *>(st.sc.digests)
+                             : st.sc.keys;
+  const int stride = use_digests ? 4 : 2;
+  if (st.claimed + n > st.nslots / 2) {
+    int rc = grow_index(st);
+    if (rc) return rc;
+  }
+  CB_CUDA(cudaMemsetAsync(st.sc.err, 0, sizeof(int), s));
+  int rc = launch_index_claim(st.slots, st.nslots - 1, keys, stride,
+                              st.sc.seqs, (int)n, st.sc.slot, st.sc.err, s);
+  if (!rc) rc = launch_index_resolve(st.slots, st.sc.slot, st.sc.seqs, (int)n,
+                                     st.sc.status, s);
+  if (rc) return rc;
+  CB_CUDA(cudaMemcpyAsync(st.sc.h_status, st.sc.status, n,
+                          cudaMemcpyDeviceToHost, s));
+  CB_CUDA(cudaMemcpyAsync(st.sc.h_err, st.sc.err, sizeof(int),
+                          cudaMemcpyDeviceToHost, s));
+  CB_CUDA(cudaStreamSynchronize(s));
+  if ((rc = check_device_err(st))) return rc;
+
+  // Placement, in sequence order as the reference's serial puts would:
+  // HBM while used + size fits the GPU capacity (CascadeStore::put,
+  // cascade_core.cpp:1097-1105), else the DRAM tier while its capacity
+  // holds (1108-1118), else the block fails (the Lustre tier of
+  // 1121-1124 is not part of this library).
+  uint64_t hbm_proj = st.gpu_used, dram_proj = st.shm_used;
+  uint64_t q8stage_bytes = 0;
+  std::vector<size_t> dram_raw, dram_q8;
+  std::vector<uint64_t> q8stage_off;
+  bool any_hbm = false, any_hbm_raw = false, any_q8 = false;
+  for (size_t i = 0; i < n; ++i) {
+    st.sc.h_req[i] = kNoRequest;
+    st.sc.h_off[i] = kInvalidOffset;
+    st.sc.h_dst[i] = 0;
+    const uint64_t size = st.sc.h_sizes[i];
+    uint32_t prefix =
+        (h_prefix && h_prefix[i] && st.cfg.dedup_enabled) ? kFlagPrefix : 0;
+    st.sc.h_flags[i] = prefix;
+    if (st.sc.h_status[i] != CASCADE_PUT_STORED) continue;
+    const bool hq8 = st.hbm && q8_eligible(st, size, false);
+    if (st.hbm && hbm_proj + payload_bytes(size, hq8) <= st.pool_cap) {
+      const bool q8 = hq8;
+      st.sc.h_req[i] = payload_bytes(size, q8);
+      st.sc.h_flags[i] |= kTierHbm | (q8 ? kFlagQ8 : 0);
+      hbm_proj += payload_bytes(size, q8);
+      any_hbm = true;
+      any_q8 |= q8;
+      any_hbm_raw |= !q8;
+      continue;
+    }
+    if (st.dram_tier) {
+      bool q8 = q8_eligible(st, size, true);
+      uint64_t acc = dram_accounted(size, q8);
+      if (dram_proj + acc <= st.dram->capacity()) {
+        uint64_t pay = payload_bytes(size, q8);
+        uint64_t off = st.dram->alloc(pay);
+        if (off != DramArena::kNone) {
+          st.sc.h_off[i] = off;
+          st.sc.h_flags[i] |= kTierDram | (q8 ? kFlagQ8 : 0);
+          dram_proj += acc;
+          if (q8) {
+            any_q8 = true;
+            dram_q8.push_back(i);
+            q8stage_off.push_back(q8stage_bytes);
+            q8stage_bytes += (pay + 255) & ~uint64_t(255);
+          } else {
+            dram_raw.push_back(i);
+          }
+          continue;
+        }
+      }
+    }
+    // No room anywhere: left with req = none and no offset -> FAILED.
+  }
+  if (!dram_q8.empty()) {
+    if ((rc = ensure_device_buf(st.d_q8stage, st.d_q8stage_cap, q8stage_bytes,
+                                s)))
+      return rc;
+    for (size_t k = 0; k < dram_q8.size(); ++k)
+      st.sc.h_dst[dram_q8[k]] = (uint64_t)(uintptr_t)(st.d_q8stage + q8stage_off[k]);
+  }
+  if (any_hbm) {
+    for (size_t i = 0; i < n; ++i)
+      if (st.sc.h_req[i] != kNoRequest)
+        if ((rc = ensure_stack(st, size_class(std::max<uint64_t>(st.sc.h_req[i], 1)))))
+          return rc;
+  }
+  // Host decisions to the device: requests, DRAM offsets, staging
+  // destinations and flags.
+  CB_CUDA(cudaMemcpyAsync(st.sc.req, st.sc.h_req, n * 8, cudaMemcpyHostToDevice, s));
+  CB_CUDA(cudaMemcpyAsync(st.sc.hoff, st.sc.h_off, n * 8, cudaMemcpyHostToDevice, s));
+  CB_CUDA(cudaMemcpyAsync(st.sc.hdst, st.sc.h_dst, n * 8, cudaMemcpyHostToDevice, s));
+  CB_CUDA(cudaMemcpyAsync(st.sc.flags, st.sc.h_flags, n * 4, cudaMemcpyHostToDevice, s));
+  const int nb = (int)((n + 255) / 256);
+  if (any_hbm) {
+    rc = launch_pool_alloc(st.d_pool, st.sc.req, (int)n, st.sc.off, s);
+    if (rc) return rc;
+  }
+  prepare_kernel<<<nb, 256, 0, s>>>((int)n, st.sc.req, st.sc.off, st.sc.hoff,
+                                    st.sc.hdst, st.sc.flags, st.sc.sizes,
+                                    (uint64_t)(uintptr_t)st.pool, st.sc.dst,
+                                    st.sc.eff_raw, st.sc.eff_q8);
+  count_launches(1);
+  CB_CUDA(cudaGetLastError());
+  // Payloads.  INT8: min/max then quantise with the header kept apart (it
+  // goes into the index slot).  Raw HBM: one batched copy.
+  if (any_q8) {
+    rc = launch_minmax(st.sc.ptrs, st.sc.eff_q8, (int)n, max_size, st.sc.mnmx, s);
+    if (!rc) rc = launch_quantize(st.sc.ptrs, st.sc.eff_q8, (int)n, max_size,
+                                  st.sc.mnmx, st.sc.dst, st.sc.hdr, 0, s);
+  }
+  if (!rc && any_hbm_raw)
+    rc = launch_copy(st.sc.ptrs, st.sc.dst, st.sc.eff_raw, (int)n, max_size, s);
+  if (rc) return rc;
+  // DRAM placements leave the device by DMA into the pinned arena.
+  for (size_t k = 0; k < dram_q8.size(); ++k) {
+    size_t i = dram_q8[k];
+    uint64_t pay = payload_bytes(st.sc.h_sizes[i], true);
+    if (pay)
+      CB_CUDA(cudaMemcpyAsync(st.dram->ptr(st.sc.h_off[i]),
+                              st.d_q8stage + q8stage_off[k], pay,
+                              cudaMemcpyDeviceToHost, s));
+  }
+  for (size_t i : dram_raw) {
+    uint64_t size = st.sc.h_sizes[i];
+    if (size)
+      CB_CUDA(cudaMemcpyAsync(st.dram->ptr(st.sc.h_off[i]),
+                              reinterpret_cast<const void *>(st.sc.h_ptrs[i]),
+                              size, cudaMemcpyDeviceToHost, s));
+  }
+  const uint64_t epoch = st.next_epoch;
+  st.next_epoch += n;
+  rc = launch_index_commit(st.slots, st.sc.slot, st.sc.status, st.sc.off,
+                           st.sc.sizes, st.sc.flags, st.sc.hdr, epoch, (int)n, s);
+  if (!rc) rc = launch_index_finalize(st.slots, st.sc.slot, st.sc.off,
+                                      st.sc.status, (int)n, s);
+  if (rc) return rc;
+  CB_CUDA(cudaMemcpyAsync(st.sc.h_status, st.sc.status, n,
+                          cudaMemcpyDeviceToHost, s));
+  CB_CUDA(cudaMemcpyAsync(st.sc.h_off, st.sc.off, n * 8,
+                          cudaMemcpyDeviceToHost, s));
+  CB_CUDA(cudaStreamSynchronize(s));
+
+  // Statistics and tier accounting, per CascadeStore::put.
+  for (size_t i = 0; i < n; ++i) {
+    const uint8_t r = st.sc.h_status[i];
+    const uint64_t size = st.sc.h_sizes[i];
+    const bool hit = (r == CASCADE_PUT_DUP_KNOWN || r == CASCADE_PUT_DUP_BATCH);
+    if (hit && st.cfg.dedup_enabled) ++st.dedup_hits;
+    // With dedup off a repeated id reaches the tier, whose put answers true
+    // for an id it holds; the reference counts that as an SHM put when the
+    // DRAM tier is the only tier (cascade_core.cpp:1108-1111).
+    if (hit && !st.cfg.dedup_enabled && !st.hbm) ++st.shm_puts;
+    // The reference compresses every block that passes the dedup check,
+    // whatever tier then takes it (cascade_core.cpp:1086-1092).
+    if (st.cfg.kv_compression && size >= 64 && !(hit && st.cfg.dedup_enabled))
+      st.compression_savings += size - (8 + size / 2);
+    if (r != CASCADE_PUT_STORED) {
+      // A DRAM placement that did not become live gives its space back.
+      if ((st.sc.h_flags[i] & kTierDram) && st.sc.h_off[i] != kInvalidOffset) {
+        bool q8 = (st.sc.h_flags[i] & kFlagQ8) != 0;
+        st.dram->free(st.sc.h_off[i], payload_bytes(size, q8));
+      }
+      continue;
+    }
+    ++st.claimed;
+    if (st.sc.h_flags[i] & kTierHbm) {
+      st.gpu_used += payload_bytes(size, (st.sc.h_flags[i] & kFlagQ8) != 0);
+    } else {
+      bool q8 = (st.sc.h_flags[i] & kFlagQ8) != 0;
+      st.shm_used += dram_accounted(size, q8);
+      ++st.shm_puts;
+    }
+  }
+  return CASCADE_OK;
+}
+
+// Uploads the batch description and runs the put.  When h_keys is null the
+// blocks are content-addressed: SHA-256 runs first and its digests are the
+// keys.  h_ptrs are device addresses.
+static int put_batch_locked(Store &st, size_t n, const uint64_t *h_ptrs,
+                            const uint64_t *h_sizes, const uint8_t *h_keys,
+                            const uint8_t *h_prefix, uint8_t *h_status,
+                            uint8_t *h_digests, uint64_t *n_stored) {
+  int rc = ensure_scratch(st, n);
+  if (rc) return rc;
+  cudaStream_t s = st.s;
+  uint64_t max_size = 0;
+  for (size_t i = 0; i < n; ++i) {
+    st.sc.h_ptrs[i] = h_ptrs[i];
+    st.sc.h_sizes[i] = h_sizes[i];
+    st.sc.h_seqs[i] = st.next_seq + i;
+    max_size = std::max(max_size, h_sizes[i]);
+    if (h_keys) {
+      uint64_t k0 = le64(h_keys + 16 * i), k1 = le64(h_keys + 16 * i + 8);
+      CB_CHECK(!(k0 == kKeyMask0 && k1 == kKeyMask1), CASCADE_ERR_INVALID,
+               "key equals the index's reserved mask value");
+      st.sc.h_keys[2 * i] = k0;
+      st.sc.h_keys[2 * i + 1] = k1;
+    }
+  }
+  st.next_seq += n;
+  CB_CUDA(cudaMemcpyAsync(st.sc.ptrs, st.sc.h_ptrs, n * 8, cudaMemcpyHostToDevice, s));
+  CB_CUDA(cudaMemcpyAsync(st.sc.sizes, st.sc.h_sizes, n * 8, cudaMemcpyHostToDevice, s));
+  CB_CUDA(cudaMemcpyAsync(st.sc.seqs, st.sc.h_seqs, n * 8, cudaMemcpyHostToDevice, s));
+  if (h_keys) {
+    CB_CUDA(cudaMemcpyAsync(st.sc.keys, st.sc.h_keys, n * 16, cudaMemcpyHostToDevice, s));
+  } else {
+    rc = launch_sha256(st.sc.ptrs, st.sc.sizes, (int)n, st.sc.digests, s);
+    if (rc) return rc;
+  }
+  rc = put_placed(st, n, h_keys == nullptr, h_prefix, max_size);
+  if (rc) return rc;
+  if (h_digests && !h_keys) {
+    CB_CUDA(cudaMemcpyAsync(st.sc.h_digests, st.sc.digests, 32 * n,
+                            cudaMemcpyDeviceToHost, s));
+    CB_CUDA(cudaStreamSynchronize(s));
+    std::memcpy(h_digests, st.sc.h_digests, 32 * n);
+  }
+  uint64_t ok = 0;
+  for (size_t i = 0; i < n; ++i) {
+    if (st.sc.h_status[i] != CASCADE_PUT_FAILED) ++ok;
+    if (h_status) h_status[i] = st.sc.h_status[i];
+  }
+  if (n_stored) *n_stored = ok;
+  return CASCADE_OK;
+}
+
+// ----------------------------------------------------------------- get
+// Looks the keys up (touching LRU epochs when `touch`); infos land in
+// st.sc.h_info.  Keys must already be in st.sc.keys on the device.
+static int lookup_locked(Store &st, size_t n, bool touch) {
+  cudaStream_t s = st.s;
+  const uint64_t epoch = st.next_epoch;
+  if (touch) st.next_epoch += n;
+  int rc = launch_index_lookup(st.slots, st.nslots - 1, st.sc.keys, 2, (int)n,
+                               touch ? 1 : 0, epoch, st.sc.info, s);
+  if (rc) return rc;
+  CB_CUDA(cudaMemcpyAsync(st.sc.h_info, st.sc.info, n * sizeof(LookupInfo),
+                          cudaMemcpyDeviceToHost, s));
+  CB_CUDA(cudaStreamSynchronize(s));
+  return CASCADE_OK;
+}
+
+static int upload_keys(Store &st, size_t n, const uint8_t *h_keys) {
+  for (size_t i = 0; i < n; ++i) {
+    st.sc.h_keys[2 * i] = le64(h_keys + 16 * i);
+    st.sc.h_keys[2 * i + 1] = le64(h_keys + 16 * i + 8);
+  }
+  CB_CUDA(cudaMemcpyAsync(st.sc.keys, st.sc.h_keys, n * 16,
+                          cudaMemcpyHostToDevice, st.s));
+  return CASCADE_OK;
+}
+
+// Moves the found blocks (h_info) into device buffers out[i], decoding INT8
+// payloads.  deliver[i] = 0 skips a block.  Updates hit/miss counters and
+// promotes DRAM hits to HBM when the configuration asks for it.
+static int deliver_locked(Store &st, size_t n, const uint64_t *out,
+                          const uint8_t *deliver) {
+  cudaStream_t s = st.s;
+  // Copy jobs and dequantise jobs, packed into the scratch arrays:
+  //   copies:  ptrs (src) / dst / eff_raw (bytes)
+  //   decodes: req (src codes) / off (dst) / eff_q8 (out bytes) / hdr
+  size_t nc = 0, nd = 0;
+  uint64_t max_c = 0, max_d = 0, stage_bytes = 0;
+  std::vector<size_t> dram_q8;
+  for (size_t i = 0; i < n; ++i) {
+    const LookupInfo &f = st.sc.h_info[i];
+    if (!f.found || !deliver[i]) continue;
+    const bool q8 = (f.flags & kFlagQ8) != 0;
+    if ((f.flags & kTierDram) && q8) {
+      dram_q8.push_back(i);
+      stage_bytes += (payload_bytes(f.size, true) + 255) & ~uint64_t(255);
+    }
+  }
+  if (stage_bytes) {
+    int rc = ensure_device_buf(st.d_q8stage, st.d_q8stage_cap, stage_bytes, s);
+    if (rc) return rc;
+  }
+  uint64_t stage_off = 0;
+  for (size_t i = 0; i < n; ++i) {
+    const LookupInfo &f = st.sc.h_info[i];
+    if (!f.found || !deliver[i]) continue;
+    const bool q8 = (f.flags & kFlagQ8) != 0;
+    uint64_t src;
+    if (f.flags & kTierHbm) {
+      src = (uint64_t)(uintptr_t)st.pool + f.offset;
+    } else {  // DRAM: bring the payload up first
+      uint64_t pay = payload_bytes(f.size, q8);
+      if (!q8) {
+        if (f.size)
+          CB_CUDA(cudaMemcpyAsync(reinterpret_cast<void *>(out[i]),
+                                  st.dram->ptr(f.offset), f.size,
+                                  cudaMemcpyHostToDevice, s));
+        continue;
+      }
+      src = (uint64_t)(uintptr_t)(st.d_q8stage + stage_off);
+      if (pay)
+        CB_CUDA(cudaMemcpyAsync(st.d_q8stage + stage_off, st.dram->ptr(f.offset),
+                                pay, cudaMemcpyHostToDevice, s));
+      stage_off += (pay + 255) & ~uint64_t(255);
+    }
+    if (q8) {
+      st.sc.h_req[nd] = src;
+      st.sc.h_off[nd] = out[i];
+      st.sc.h_seqs[nd] = 2 * (f.size / 2);  // decoded bytes (2 per code)
+      uint8_t *h = st.sc.h_hdr + 8 * nd;
+      std::memcpy(h, &f.hdr_scale, 4);
+      h[4] = (uint8_t)f.hdr_zp;
+      h[5] = h[6] = h[7] = 0;
+      max_d = std::max<uint64_t>(max_d, f.size);
+      ++nd;
+    } else {
+      st.sc.h_ptrs[nc] = src;
+      st.sc.h_dst[nc] = out[i];
+      st.sc.h_sizes[nc] = f.size;
+      max_c = std::max<uint64_t>(max_c, f.size);
+      ++nc;
+    }
+  }
+  if (nc) {
+    CB_CUDA(cudaMemcpyAsync(st.sc.ptrs, st.sc.h_ptrs, nc * 8, cudaMemcpyHostToDevice, s));
+    CB_CUDA(cudaMemcpyAsync(st.sc.dst, st.sc.h_dst, nc * 8, cudaMemcpyHostToDevice, s));
+    CB_CUDA(cudaMemcpyAsync(st.sc.eff_raw, st.sc.h_sizes, nc * 8, cudaMemcpyHostToDevice, s));
+    int rc = launch_copy(st.sc.ptrs, st.sc.dst, st.sc.eff_raw, (int)nc, max_c, s);
+    if (rc) return rc;
+  }
+  if (nd) {
+    CB_CUDA(cudaMemcpyAsync(st.sc.req, st.sc.h_req, nd * 8, cudaMemcpyHostToDevice, s));
+    CB_CUDA(cudaMemcpyAsync(st.sc.off, st.sc.h_off, nd * 8, cudaMemcpyHostToDevice, s));
+    CB_CUDA(cudaMemcpyAsync(st.sc.eff_q8, st.sc.h_seqs, nd * 8, cudaMemcpyHostToDevice, s));
+    CB_CUDA(cudaMemcpyAsync(st.sc.hdr, st.sc.h_hdr, nd * 8, cudaMemcpyHostToDevice, s));
+    int rc = launch_dequantize(st.sc.req, st.sc.hdr, 0, st.sc.eff_q8, (int)nd,
+                               max_d, st.sc.off, s);
+    if (rc) return rc;
+  }
+  // Counters: CascadeStore::get (cascade_core.cpp:1138-1189).
+  for (size_t i = 0; i < n; ++i) {
+    const LookupInfo &f = st.sc.h_info[i];
+    if (!deliver[i]) continue;
+    if (!f.found) ++st.misses;
+    else if (f.flags & kTierHbm) ++st.gpu_hits;
+    else ++st.shm_hits;
+  }
+  CB_CUDA(cudaStreamSynchronize(s));
+  // Promotion of DRAM hits (promote_to_gpu, cascade_core.cpp:1039-1056):
+  // the decoded block, now in out[i], is stored in HBM and its DRAM space
+  // released.
+  if (!(st.cfg.promotion_enabled && st.hbm)) return CASCADE_OK;
+  std::vector<size_t> promo;
+  uint64_t proj = st.gpu_used;
+  for (size_t i = 0; i < n; ++i) {
+    const LookupInfo &f = st.sc.h_info[i];
+    if (!f.found || !deliver[i] || !(f.flags & kTierDram)) continue;
+    const uint64_t size = (f.flags & kFlagQ8) ? 2 * (f.size / 2) : f.size;
+    const uint64_t need = payload_bytes(size, q8_eligible(st, size, false));
+    if (proj + need > st.pool_cap) continue;  // no eviction on promotion yet
+    proj += need;
+    promo.push_back(i);
+  }
+  if (promo.empty()) return CASCADE_OK;
+  // Build a placement batch over the scratch arrays: one request each.
+  const size_t m = promo.size();
+  std::vector<LookupInfo> infos(m);
+  uint64_t max_size = 0;
+  for (size_t k = 0; k < m; ++k) {
+    const size_t i = promo[k];
+    const LookupInfo &f = st.sc.h_info[i];
+    infos[k] = f;
+    const bool was_q8 = (f.flags & kFlagQ8) != 0;
+    const uint64_t size = was_q8 ? 2 * (f.size / 2) : f.size;
+    const bool q8 = q8_eligible(st, size, false);
+    st.sc.h_ptrs[k] = out[i];
+    st.sc.h_sizes[k] = size;
+    st.sc.h_req[k] = payload_bytes(size, q8);
+    st.sc.h_flags[k] = (f.flags & kFlagPrefix) | kTierHbm | (q8 ? kFlagQ8 : 0);
+    st.sc.h_slot[k] = f.slot;
+    max_size = std::max(max_size, size);
+    int rc = ensure_stack(st, size_class(std::max<uint64_t>(st.sc.h_req[k], 1)));
+    if (rc) return rc;
+  }
+  CB_CUDA(cudaMemcpyAsync(st.sc.ptrs, st.sc.h_ptrs, m * 8, cudaMemcpyHostToDevice, s));
+  CB_CUDA(cudaMemcpyAsync(st.sc.sizes, st.sc.h_sizes, m * 8, cudaMemcpyHostToDevice, s));
+  CB_CUDA(cudaMemcpyAsync(st.sc.req, st.sc.h_req, m * 8, cudaMemcpyHostToDevice, s));
+  CB_CUDA(cudaMemcpyAsync(st.sc.flags, st.sc.h_flags, m * 4, cudaMemcpyHostToDevice, s));
+  CB_CUDA(cudaMemcpyAsync(st.sc.slot, st.sc.h_slot, m * 4, cudaMemcpyHostToDevice, s));
+  int rc = launch_pool_alloc(st.d_pool, st.sc.req, (int)m, st.sc.off, s);
+  if (rc) return rc;
+  CB_CUDA(cudaMemcpyAsync(st.sc.h_off, st.sc.off, m * 8, cudaMemcpyDeviceToHost, s));
+  CB_CUDA(cudaStreamSynchronize(s));
+  // Only the allocations that succeeded move.
+  size_t good = 0;
+  for (size_t k = 0; k < m; ++k) {
+    if (st.sc.h_off[k] == kInvalidOffset) continue;
+    st.sc.h_ptrs[good] = st.sc.h_ptrs[k];
+    st.sc.h_sizes[good] = st.sc.h_sizes[k];
+    st.sc.h_flags[good] = st.sc.h_flags[k];
+    st.sc.h_slot[good] = st.sc.h_slot[k];
+    st.sc.h_dst[good] = (uint64_t)(uintptr_t)st.pool + st.sc.h_off[k];
+    st.sc.h_req[good] = st.sc.h_off[k];  // keep the offset for relocate
+    infos[good] = infos[k];
+    ++good;
+  }
+  if (!good) return CASCADE_OK;
+  std::vector<uint64_t> eff_q8(good), eff_raw(good);
+  for (size_t k = 0; k < good; ++k) {
+    bool q8 = (st.sc.h_flags[k] & kFlagQ8) != 0;
+    eff_q8[k] = q8 ? st.sc.h_sizes[k] : 0;
+    eff_raw[k] = q8 ? 0 : st.sc.h_sizes[k];
+  }
+  std::memcpy(st.sc.h_seqs, eff_q8.data(), good * 8);
+  CB_CUDA(cudaMemcpyAsync(st.sc.ptrs, st.sc.h_ptrs, good * 8, cudaMemcpyHostToDevice, s));
+  CB_CUDA(cudaMemcpyAsync(st.sc.dst, st.sc.h_dst, good * 8, cudaMemcpyHostToDevice, s));
+  CB_CUDA(cudaMemcpyAsync(st.sc.eff_q8, st.sc.h_seqs, good * 8, cudaMemcpyHostToDevice, s));
+  CB_CUDA(cudaStreamSynchronize(s));
+  std::memcpy(st.sc.h_seqs, eff_raw.data(), good * 8);
+  CB_CUDA(cudaMemcpyAsync(st.sc.eff_raw, st.sc.h_seqs, good * 8, cudaMemcpyHostToDevice, s));
+  CB_CUDA(cudaMemcpyAsync(st.sc.off, st.sc.h_req, good * 8, cudaMemcpyHostToDevice, s));
+  CB_CUDA(cudaMemcpyAsync(st.sc.flags, st.sc.h_flags, good * 4, cudaMemcpyHostToDevice, s));
+  CB_CUDA(cudaMemcpyAsync(st.sc.slot, st.sc.h_slot, good * 4, cudaMemcpyHostToDevice, s));
+  rc = launch_minmax(st.sc.ptrs, st.sc.eff_q8, (int)good, max_size, st.sc.mnmx, s);
+  if (!rc) rc = launch_quantize(st.sc.ptrs, st.sc.eff_q8, (int)good, max_size,
+                                st.sc.mnmx, st.sc.dst, st.sc.hdr, 0, s);
+  if (!rc) rc = launch_copy(st.sc.ptrs, st.sc.dst, st.sc.eff_raw, (int)good,
+                            max_size, s);
+  if (!rc) rc = launch_index_relocate(st.slots, st.sc.slot, st.sc.off,
+                                      st.sc.flags, st.sc.hdr, (int)good, s);
+  if (rc) return rc;
+  CB_CUDA(cudaStreamSynchronize(s));
+  for (size_t k = 0; k < good; ++k) {
+    const LookupInfo &f = infos[k];
+    const bool was_q8 = (f.flags & kFlagQ8) != 0;
+    st.dram->free(f.offset, payload_bytes(f.size, was_q8));
+    st.shm_used -= dram_accounted(f.size, was_q8);
+    st.gpu_used += payload_bytes(st.sc.h_sizes[k],
+                                 (st.sc.h_flags[k] & kFlagQ8) != 0);
+    ++st.promotions_to_gpu;
+  }
+  return CASCADE_OK;
+}
+
+static int get_batch_locked(Store &st, size_t n, const uint8_t *h_keys,
+                            const uint64_t *h_out, const uint64_t *h_caps,
+                            uint64_t *h_sizes, uint8_t *h_found,
+                            uint64_t *n_found) {
+  int rc = ensure_scratch(st, n);
+  if (!rc) rc = upload_keys(st, n, h_keys);
+  if (!rc) rc = lookup_locked(st, n, true);
+  if (rc) return rc;
+  std::vector<uint8_t> deliver(n);
+  std::vector<uint64_t> out(h_out, h_out + n);
+  uint64_t found = 0;
+  for (size_t i = 0; i < n; ++i) {
+    const LookupInfo &f = st.sc.h_info[i];
+    uint64_t size = f.found ? ((f.flags & kFlagQ8) ? 2 * (f.size / 2) : f.size) : 0;
+    if (h_sizes) h_sizes[i] = size;
+    if (h_found) h_found[i] = f.found ? 1 : 0;
+    found += f.found ? 1 : 0;
+    deliver[i] = (!f.found || size <= h_caps[i]) ? 1 : 0;
+  }
+  if (n_found) *n_found = found;
+  return deliver_locked(st, n, out.data(), deliver.data());
+}
+
+// ---------------------------------------------------------- index growth
+namespace {
+
+__global__ void rehash_kernel(const Slot *__restrict__ old_slots,
+                              uint64_t old_n, Slot *new_slots,
+                              uint64_t new_mask, int *err) {
+  for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x;
+       i < old_n; i += (uint64_t)gridDim.x * blockDim.x) {
+    const Slot &o = old_slots[i];
+    if (o.state != kLive) continue;
+    const uint64_t z = slot_hash(o.k0, o.k1);
+    bool placed = false;
+    for (int p = 0; p < kMaxProbe && !placed; ++p) {
+      Slot *t = new_slots + ((z + (uint64_t)p) & new_mask);
+      uint64_t a, b;
+      cas128(&t->k0, 0, 0, o.k0, o.k1, a, b);
+      if (a == 0 && b == 0) {  // the key is unique: the slot is ours
+        t->claim = 0;
+        t->state = o.state;
+        t->flags = o.flags;
+        t->offset = o.offset;
+        t->size = o.size;
+        t->hdr_scale = o.hdr_scale;
+        t->hdr_zp = o.hdr_zp;
+        t->epoch = o.epoch;
+        placed = true;
+      }
+    }
+    if (!placed) atomicExch(err, CASCADE_ERR_FULL);
+  }
+}
+
+int grow_index(Store &st) {
+  uint64_t want = pow2_at_least(2 * (st.claimed + st.sc.cap) + 1);
+  if (want <= st.nslots) want = st.nslots * 2;
+  Slot *fresh = nullptr;
+  CB_CUDA(cudaMalloc(&fresh, want * sizeof(Slot)));
+  CB_CUDA(cudaMemsetAsync(fresh, 0, want * sizeof(Slot), st.s));
+  CB_CUDA(cudaMemsetAsync(st.sc.err, 0, sizeof(int), st.s));
+  const int grid = grid_for(st.nslots, 256, 8);
+  rehash_kernel<<<grid, 256, 0, st.s>>>(st.slots, st.nslots, fresh, want - 1,
+                                        st.sc.err);
+  count_launches(1);
+  CB_CUDA(cudaGetLastError());
+  CB_CUDA(cudaMemcpyAsync(st.sc.h_err, st.sc.err, sizeof(int),
+                          cudaMemcpyDeviceToHost, st.s));
+  CB_CUDA(cudaStreamSynchronize(st.s));
+  if (*st.sc.h_err) {
+    cudaFree(fresh);
+    set_error("index rehash failed");
+    return CASCADE_ERR_FULL;
+  }
+  CB_CUDA(cudaFree(st.slots));
+  st.slots = fresh;
+  st.nslots = want;
+  return CASCADE_OK;
+}
+
+}  // namespace
+
+// ------------------------------------------------------------- lifecycle
+static int create_store(const cascade_config_t *cfg, Store **out) {
+  int count = 0;
+  if (cudaGetDeviceCount(&count) != cudaSuccess || count == 0) {
+    cudaGetLastError();
+    set_error("no CUDA device: the block store runs only on the GPU");
+    return CASCADE_ERR_NODEVICE;
+  }
+  CB_CHECK(cfg->gpu_device_id >= 0 && cfg->gpu_device_id < count,
+           CASCADE_ERR_INVALID, "gpu_device_id out of range");
+  std::unique_ptr<Store> st(new Store());
+  st->cfg = *cfg;
+  st->shm_path = cfg->shm_path ? cfg->shm_path : "";
+  st->lustre_path = cfg->lustre_path ? cfg->lustre_path : "";
+  st->cfg.shm_path = st->shm_path.c_str();
+  st->cfg.lustre_path = st->lustre_path.c_str();
+  st->dev = cfg->gpu_device_id;
+  DeviceGuard g(st->dev);
+  CB_CUDA(cudaStreamCreateWithFlags(&st->s, cudaStreamNonBlocking));
+  CB_CUDA(cudaEventCreateWithFlags(&st->ev, cudaEventDisableTiming));
+  st->hbm = cfg->use_gpu && cfg->gpu_capacity_bytes > 0;
+  st->dram_tier = cfg->shm_capacity_bytes > 0;
+  if (st->hbm) {
+    st->pool_cap = cfg->gpu_capacity_bytes;
+    cudaError_t e = cudaMalloc(&st->pool, st->pool_cap);
+    if (e != cudaSuccess) {
+      cudaGetLastError();
+      set_error("cannot allocate the HBM pool of gpu_capacity_bytes");
+      return CASCADE_ERR_NOMEM;
+    }
+    CB_CUDA(cudaMalloc(&st->d_pool, sizeof(PoolDev)));
+  }
+  uint64_t slots = cfg->index_slots;
+  if (!slots) {
+    uint64_t blocks = (cfg->gpu_capacity_bytes * (st->hbm ? 1 : 0) +
+                       cfg->shm_capacity_bytes) / (256ull << 10);
+    slots = std::min<uint64_t>(std::max<uint64_t>(2 * blocks, 1ull << 16),
+                               1ull << 22);
+  }
+  st->nslots = pow2_at_least(std::max<uint64_t>(slots, 1024));
+  CB_CUDA(cudaMalloc(&st->slots, st->nslots * sizeof(Slot)));
+  CB_CUDA(cudaMemsetAsync(st->slots, 0, st->nslots * sizeof(Slot), st->s));
+  if (st->dram_tier) {
+    uint64_t chunk = cfg->dram_chunk_bytes ? cfg->dram_chunk_bytes : (1ull << 30);
+    st->dram.reset(new DramArena(cfg->shm_capacity_bytes, chunk));
+  }
+  int rc = ensure_scratch(*st, 1024);
+  if (!rc) rc = reset_pool(*st);
+  if (rc) return rc;
+  CB_CUDA(cudaStreamSynchronize(st->s));
+  *out = st.release();
+  return CASCADE_OK;
+}
+
+static void destroy_store(Store *st) {
+  DeviceGuard g(st->dev);
+  if (st->s) cudaStreamSynchronize(st->s);
+  st->dram.reset();
+  for (int c = 0; c < kNumClasses; ++c)
+    if (st->stack_ptr[c]) cudaFree(st->stack_ptr[c]);
+  if (st->pool) cudaFree(st->pool);
+  if (st->d_pool) cudaFree(st->d_pool);
+  if (st->slots) cudaFree(st->slots);
+  if (st->sc.dblob) cudaFree(st->sc.dblob);
+  if (st->sc.hblob) cudaFreeHost(st->sc.hblob);
+  if (st->d_stage) cudaFree(st->d_stage);
+  if (st->h_stage) cudaFreeHost(st->h_stage);
+  if (st->d_q8stage) cudaFree(st->d_q8stage);
+  if (st->ev) cudaEventDestroy(st->ev);
+  if (st->s) cudaStreamDestroy(st->s);
+  delete st;
+}
+
+static int clear_store(Store &st) {
+  CB_CUDA(cudaStreamSynchronize(st.s));
+  CB_CUDA(cudaMemsetAsync(st.slots, 0, st.nslots * sizeof(Slot), st.s));
+  int rc = reset_pool(st);
+  if (rc) return rc;
+  if (st.dram) st.dram->reset();
+  st.names.clear();
+  st.claimed = 0;
+  st.gpu_used = st.shm_used = st.gpu_hits = st.shm_hits = st.misses = 0;
+  st.dedup_hits = st.gpu_evictions = st.promotions_to_gpu = 0;
+  st.compression_savings = st.shm_puts = 0;
+  CB_CUDA(cudaStreamSynchronize(st.s));
+  return CASCADE_OK;
+}
+
+// Host-buffer put of one block: staged to the device, then the batch path.
+static int put_host_locked(Store &st, const Key &k, const uint8_t *data,
+                           uint64_t size, int is_prefix, int *stored) {
+  int rc = ensure_device_buf(st.d_stage, st.d_stage_cap, size, st.s);
+  if (!rc) rc = ensure_host_stage(st, size);
+  if (rc) return rc;
+  if (size) {
+    std::memcpy(st.h_stage, data, size);
+    CB_CUDA(cudaMemcpyAsync(st.d_stage, st.h_stage, size,
+                            cudaMemcpyHostToDevice, st.s));
+  }
+  uint8_t key[16];
+  for (int i = 0; i < 8; ++i) {
+    key[i] = (uint8_t)(k.k0 >> (8 * i));
+    key[8 + i] = (uint8_t)(k.k1 >> (8 * i));
+  }
+  uint64_t ptr = (uint64_t)(uintptr_t)st.d_stage;
+  uint8_t pf = is_prefix ? 1 : 0, status = 0;
+  uint64_t ok = 0;
+  rc = put_batch_locked(st, 1, &ptr, &size, key, &pf, &status, nullptr, &ok);
+  if (rc) return rc;
+  *stored = ok ? 1 : 0;
+  return CASCADE_OK;
+}
+
+static int get_host_locked(Store &st, const Key &k, uint8_t *out,
+                           uint64_t cap, int *found, uint64_t *size) {
+  int rc = ensure_scratch(st, 1);
+  if (rc) return rc;
+  st.sc.h_keys[0] = k.k0;
+  st.sc.h_keys[1] = k.k1;
+  CB_CUDA(cudaMemcpyAsync(st.sc.keys, st.sc.h_keys, 16, cudaMemcpyHostToDevice,
+                          st.s));
+  if ((rc = lookup_locked(st, 1, true))) return rc;
+  LookupInfo f = st.sc.h_info[0];
+  if (!f.found) {
+    ++st.misses;
+    *found = 0;
+    *size = 0;
+    return CASCADE_OK;
+  }
+  const uint64_t bytes = (f.flags & kFlagQ8) ? 2 * (f.size / 2) : f.size;
+  *found = 1;
+  *size = bytes;
+  if (bytes > cap) return CASCADE_OK;  // caller retries with a larger buffer
+  if ((f.flags & kTierDram) && !(f.flags & kFlagQ8) &&
+      !(st.cfg.promotion_enabled && st.hbm)) {
+    // A raw DRAM block goes straight from the arena to the caller.
+    if (bytes) std::memcpy(out, st.dram->ptr(f.offset), bytes);
+    ++st.shm_hits;
+    return CASCADE_OK;
+  }
+  if ((rc = ensure_device_buf(st.d_stage, st.d_stage_cap, bytes, st.s)) ||
+      (rc = ensure_host_stage(st, bytes)))
+    return rc;
+  uint64_t dst = (uint64_t)(uintptr_t)st.d_stage;
+  uint8_t deliver = 1;
+  if ((rc = deliver_locked(st, 1, &dst, &deliver))) return rc;
+  if (bytes) {
+    CB_CUDA(cudaMemcpyAsync(st.h_stage, st.d_stage, bytes,
+                            cudaMemcpyDeviceToHost, st.s));
+    CB_CUDA(cudaStreamSynchronize(st.s));
+    std::memcpy(out, st.h_stage, bytes);
+  }
+  return CASCADE_OK;
+}
+
+// Host blocks for the batched put: copied into one device staging area
+// (directly when the host memory is pinned), then the device batch path.
+static int put_batch_host_locked(Store &st, size_t n,
+                                 const uint8_t *const *blocks,
+                                 const uint64_t *sizes, const uint8_t *keys,
+                                 const uint8_t *prefix, uint8_t *status,
+                                 uint8_t *digests, uint64_t *n_stored) {
+  uint64_t total = 0;
+  std::vector<uint64_t> offs(n);
+  for (size_t i = 0; i < n; ++i) {
+    offs[i] = total;
+    total += (sizes[i] + 255) & ~uint64_t(255);
+  }
+  int rc = ensure_device_buf(st.d_stage, st.d_stage_cap, total, st.s);
+  if (rc) return rc;
+  size_t pinned_need = 0;
+  std::vector<uint8_t> pinned(n);
+  for (size_t i = 0; i < n; ++i) {
+    cudaPointerAttributes a;
+    pinned[i] = (sizes[i] && cudaPointerGetAttributes(&a, blocks[i]) == cudaSuccess &&
+                 a.type == cudaMemoryTypeHost) ? 1 : 0;
+    cudaGetLastError();
+    if (!pinned[i]) pinned_need = std::max<size_t>(pinned_need, sizes[i]);
+  }
+  if (pinned_need && (rc = ensure_host_stage(st, pinned_need))) return rc;
+  std::vector<uint64_t> ptrs(n);
+  for (size_t i = 0; i < n; ++i) {
+    ptrs[i] = (uint64_t)(uintptr_t)(st.d_stage + offs[i]);
+    if (!sizes[i]) continue;
+    if (pinned[i]) {
+      CB_CUDA(cudaMemcpyAsync(st.d_stage + offs[i], blocks[i], sizes[i],
+                              cudaMemcpyHostToDevice, st.s));
+    } else {  // through the pinned stage, one block at a time
+      CB_CUDA(cudaStreamSynchronize(st.s));
+      std::memcpy(st.h_stage, blocks[i], sizes[i]);
+      CB_CUDA(cudaMemcpyAsync(st.d_stage + offs[i], st.h_stage, sizes[i],
+                              cudaMemcpyHostToDevice, st.s));
+    }
+  }
+  return put_batch_locked(st, n, ptrs.data(), sizes, keys, prefix, status,
+                          digests, n_stored);
+}
+
+}  // namespace cb
+
+// ------------------------------------------------------------------ C-ABI
+struct cascade_store {
+  cb::Store *impl;
+};
+
+#define STORE_ENTRY(s)                                                       \
+  cb::clear_error();                                                         \
+  CB_CHECK((s) && (s)->impl, CASCADE_ERR_INVALID, "null store");             \
+  cb::Store &st = *(s)->impl;                                                \
+  std::lock_guard<std::mutex> lock(st.mu);                                   \
+  cb::DeviceGuard guard(st.dev)
+
+extern "C" void cascade_struct_sizes(size_t *config_bytes,
+                                     size_t *stats_bytes) {
+  if (config_bytes) *config_bytes = sizeof(cascade_config_t);
+  if (stats_bytes) *stats_bytes = sizeof(cascade_stats_t);
+}
+
+extern "C" void cascade_config_init(cascade_config_t *c) {
+  if (!c) return;
+  std::memset(c, 0, sizeof(*c));
+  c->gpu_capacity_bytes = 32ull << 30;
+  c->gpu_device_id = 0;
+  c->use_gpu = 1;
+  c->shm_capacity_bytes = 64ull << 30;
+  c->shm_path = "/dev/shm/cascade";
+  c->lustre_path = "cascade_store";
+  c->lustre_stripe_size = 1ull << 20;
+  c->lustre_stripe_count = 16;
+  c->dedup_enabled = 1;
+  c->compression_enabled = 1;
+  c->num_io_threads = 8;
+  c->semantic_eviction = 1;
+  c->promotion_enabled = 1;
+  c->prefetch_enabled = 1;
+  c->prefetch_threads = 2;
+  c->prefetch_queue_size = 64;
+  c->kv_compression = 0;
+  c->aggregated_lustre = 0;
+  c->agg_file_size = 256ull << 20;
+}
+
+extern "C" int cascade_store_create(const cascade_config_t *cfg,
+                                    cascade_store_t **out) {
+  cb::clear_error();
+  CB_CHECK(cfg && out, CASCADE_ERR_INVALID, "null argument");
+  cb::Store *impl = nullptr;
+  int rc = cb::create_store(cfg, &impl);
+  if (rc) return rc;
+  *out = new cascade_store{impl};
+  return CASCADE_OK;
+}
+
+extern "C" int cascade_store_destroy(cascade_store_t *s) {
+  cb::clear_error();
+  if (!s) return CASCADE_OK;
+  if (s->impl) cb::destroy_store(s->impl);
+  delete s;
+  return CASCADE_OK;
+}
+
+extern "C" int cascade_store_put(cascade_store_t *s, const char *block_id,
+                                 const uint8_t *data, uint64_t size,
+                                 int is_prefix, int *stored) {
+  STORE_ENTRY(s);
+  CB_CHECK(block_id && stored && (data || !size), CASCADE_ERR_INVALID,
+           "null argument");
+  cb::Key k;
+  bool known;
+  int rc = cb::key_of(st, block_id, true, &k, &known);
+  if (rc) return rc;
+  return cb::put_host_locked(st, k, data, size, is_prefix, stored);
+}
+
+extern "C" int cascade_store_get(cascade_store_t *s, const char *block_id,
+                                 uint8_t *out, uint64_t out_capacity,
+                                 int *found, uint64_t *size) {
+  STORE_ENTRY(s);
+  CB_CHECK(block_id && found && size && (out || !out_capacity),
+           CASCADE_ERR_INVALID, "null argument");
+  cb::Key k;
+  bool known;
+  int rc = cb::key_of(st, block_id, false, &k, &known);
+  if (rc) return rc;
+  if (!known) {
+    ++st.misses;
+    *found = 0;
+    *size = 0;
+    return CASCADE_OK;
+  }
+  return cb::get_host_locked(st, k, out, out_capacity, found, size);
+}
+
+extern "C" int cascade_store_contains(cascade_store_t *s, const char *block_id,
+                                      int *present) {
+  STORE_ENTRY(s);
+  CB_CHECK(block_id && present, CASCADE_ERR_INVALID, "null argument");
+  cb::Key k;
+  bool known;
+  int rc = cb::key_of(st, block_id, false, &k, &known);
+  if (rc) return rc;
+  *present = 0;
+  if (!known) return CASCADE_OK;
+  if ((rc = cb::ensure_scratch(st, 1))) return rc;
+  st.sc.h_keys[0] = k.k0;
+  st.sc.h_keys[1] = k.k1;
+  CB_CUDA(cudaMemcpyAsync(st.sc.keys, st.sc.h_keys, 16, cudaMemcpyHostToDevice,
+                          st.s));
+  if ((rc = cb::lookup_locked(st, 1, false))) return rc;
+  *present = st.sc.h_info[0].found ? 1 : 0;
+  return CASCADE_OK;
+}
+
+extern "C" int cascade_store_get_stats(cascade_store_t *s,
+                                       cascade_stats_t *o) {
+  STORE_ENTRY(s);
+  CB_CHECK(o, CASCADE_ERR_INVALID, "null argument");
+  std::memset(o, 0, sizeof(*o));
+  o->gpu_used = st.gpu_used;
+  o->shm_used = st.shm_used;
+  o->gpu_hits = st.gpu_hits;
+  o->shm_hits = st.shm_hits;
+  o->misses = st.misses;
+  o->dedup_hits = st.dedup_hits;
+  o->gpu_evictions = st.gpu_evictions;
+  o->promotions_to_gpu = st.promotions_to_gpu;
+  o->compression_savings_bytes = st.compression_savings;
+  o->shm_puts = st.shm_puts;
+  return CASCADE_OK;
+}
+
+extern "C" int cascade_store_clear(cascade_store_t *s) {
+  STORE_ENTRY(s);
+  return cb::clear_store(st);
+}
+
+extern "C" int cascade_store_flush(cascade_store_t *s) {
+  STORE_ENTRY(s);
+  CB_CUDA(cudaStreamSynchronize(st.s));
+  return CASCADE_OK;
+}
+
+extern "C" int cascade_store_key_of(cascade_store_t *s, const char *block_id,
+                                    uint8_t key_out[16]) {
+  STORE_ENTRY(s);
+  CB_CHECK(block_id && key_out, CASCADE_ERR_INVALID, "null argument");
+  cb::Key k;
+  bool known;
+  int rc = cb::key_of(st, block_id, true, &k, &known);
+  if (rc) return rc;
+  for (int i = 0; i < 8; ++i) {
+    key_out[i] = (uint8_t)(k.k0 >> (8 * i));
+    key_out[8 + i] = (uint8_t)(k.k1 >> (8 * i));
+  }
+  return CASCADE_OK;
+}
+
+extern "C" int cascade_store_put_batch(cascade_store_t *s, size_t n,
+                                       const uint64_t *h_ptrs,
+                                       const uint64_t *h_sizes,
+                                       const uint8_t *h_keys,
+                                       const uint8_t *h_prefix,
+                                       uint8_t *h_status, uint8_t *h_digests,
+                                       void *stream, uint64_t *n_stored) {
+  STORE_ENTRY(s);
+  if (n_stored) *n_stored = 0;
+  if (n == 0) return CASCADE_OK;
+  CB_CHECK(h_ptrs && h_sizes, CASCADE_ERR_INVALID, "null argument");
+  CB_CHECK(n <= (size_t)INT32_MAX, CASCADE_ERR_INVALID, "batch too large");
+  if (stream) {  // the caller's producer work comes first
+    CB_CUDA(cudaEventRecord(st.ev, static_cast<cudaStream_t>(stream)));
+    CB_CUDA(cudaStreamWaitEvent(st.s, st.ev, 0));
+  }
+  return cb::put_batch_locked(st, n, h_ptrs, h_sizes, h_keys, h_prefix,
+                              h_status, h_digests, n_stored);
+}
+
+extern "C" int cascade_store_put_batch_host(
+    cascade_store_t *s, size_t n, const uint8_t *const *h_blocks,
+    const uint64_t *h_sizes, const uint8_t *h_keys, const uint8_t *h_prefix,
+    uint8_t *h_status, uint8_t *h_digests, uint64_t *n_stored) {
+  STORE_ENTRY(s);
+  if (n_stored) *n_stored = 0;
+  if (n == 0) return CASCADE_OK;
+  CB_CHECK(h_blocks && h_sizes, CASCADE_ERR_INVALID, "null argument");
+  CB_CHECK(n <= (size_t)INT32_MAX, CASCADE_ERR_INVALID, "batch too large");
+  return cb::put_batch_host_locked(st, n, h_blocks, h_sizes, h_keys, h_prefix,
+                                   h_status, h_digests, n_stored);
+}
+
+extern "C" int cascade_store_get_batch(cascade_store_t *s, size_t n,
+                                       const uint8_t *h_keys,
+                                       const uint64_t *h_out_ptrs,
+                                       const uint64_t *h_out_caps,
+                                       uint64_t *h_sizes, uint8_t *h_found,
+                                       void *stream, uint64_t *n_found) {
+  STORE_ENTRY(s);
+  if (n_found) *n_found = 0;
+  if (n == 0) return CASCADE_OK;
+  CB_CHECK(h_keys && h_out_ptrs && h_out_caps, CASCADE_ERR_INVALID,
+           "null argument");
+  CB_CHECK(n <= (size_t)INT32_MAX, CASCADE_ERR_INVALID, "batch too large");
+  if (stream) {
+    CB_CUDA(cudaEventRecord(st.ev, static_cast<cudaStream_t>(stream)));
+    CB_CUDA(cudaStreamWaitEvent(st.s, st.ev, 0));
+  }
+  return cb::get_batch_locked(st, n, h_keys, h_out_ptrs, h_out_caps, h_sizes,
+                              h_found, n_found);
+}

@@ -1,0 +1,339 @@
+// Batched kernels over the device block index and the HBM pool allocator.
+//
+// Put protocol for a batch (each step one launch, stream-ordered):
+//   claim    every request finds or inserts its key (128-bit CAS on the key)
+//            and lowers the slot's claim to its own sequence number;
+//   resolve  the request holding the slot's smallest sequence number wins
+//            (the reference's "first put stores, later puts are dedup hits",
+//            CascadeStore::put, cascade_core.cpp:1077-1080), a live slot
+//            means the key is already stored;
+//   (alloc + payload kernels for the winners)
+//   commit   winners publish location/size/header and turn the slot live;
+//   finalize duplicates of a winner that failed fail too.
+// No kernel here waits on another thread: every conflict is settled by one
+// atomic, so nothing can spin.
+#include "common.cuh"
+#include "store_dev.cuh"
+
+namespace cb {
+
+namespace {
+
+__device__ __forceinline__ void ld_key(const Slot *s, uint64_t &a,
+                                       uint64_t &b) {
+  asm volatile("ld.global.cg.v2.u64 {%0, %1}, [%2];"
+               : "=l"(a), "=l"(b)
+               : "l"(&s->k0));
+}
+
+__global__ void claim_kernel(Slot *slots, uint64_t mask,
+                             const uint64_t *__restrict__ keys, int stride,
+                             const uint64_t *__restrict__ seqs, int n,
+                             uint32_t *__restrict__ slot_idx, int *err) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const uint64_t s0 = keys[(size_t)i * stride] ^ kKeyMask0;
+  const uint64_t s1 = keys[(size_t)i * stride + 1] ^ kKeyMask1;
+  const uint64_t h = slot_hash(s0, s1);
+  for (int p = 0; p < kMaxProbe; ++p) {
+    const uint64_t idx = (h + (uint64_t)p) & mask;
+    Slot *sl = slots + idx;
+    uint64_t a, b;
+    ld_key(sl, a, b);
+    if ((a | b) != 0) {  // keys are never rewritten: a non-empty read is final
+      if (a != s0 || b != s1) continue;
+    } else {
+      cas128(&sl->k0, 0, 0, s0, s1, a, b);
+      if (!((a == 0 && b == 0) || (a == s0 && b == s1))) continue;
+    }
+    atomicMax(reinterpret_cast<unsigned long long *>(&sl->claim),
+              (unsigned long long)~seqs[i]);
+    slot_idx[i] = (uint32_t)idx;
+    return;
+  }
+  slot_idx[i] = kNoSlot;
+  atomicExch(err, CASCADE_ERR_FULL);
+}
+
+__global__ void resolve_kernel(const Slot *__restrict__ slots,
+                               const uint32_t *__restrict__ slot_idx,
+                               const uint64_t *__restrict__ seqs, int n,
+                               uint8_t *__restrict__ status) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const uint32_t idx = slot_idx[i];
+  if (idx == kNoSlot) { status[i] = CASCADE_PUT_FAILED; return; }
+  const Slot &sl = slots[idx];
+  if (sl.state == kLive) status[i] = CASCADE_PUT_DUP_KNOWN;
+  else if (sl.claim == ~seqs[i]) status[i] = CASCADE_PUT_STORED;
+  else status[i] = CASCADE_PUT_DUP_BATCH;
+}
+
+__global__ void commit_kernel(Slot *slots, const uint32_t *__restrict__ slot_idx,
+                              const uint8_t *__restrict__ status,
+                              const uint64_t *__restrict__ offsets,
+                              const uint64_t *__restrict__ sizes,
+                              const uint32_t *__restrict__ flags,
+                              const uint8_t *__restrict__ headers,
+                              uint64_t epoch_base, int n) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n || status[i] != CASCADE_PUT_STORED) return;
+  Slot &sl = slots[slot_idx[i]];
+  if (offsets[i] != kInvalidOffset) {
+    const uint8_t *h = headers + 8 * (size_t)i;
+    sl.offset = offsets[i];
+    sl.size = sizes[i];
+    sl.flags = flags[i];
+    sl.hdr_scale = (uint32_t)h[0] | ((uint32_t)h[1] << 8) |
+                   ((uint32_t)h[2] << 16) | ((uint32_t)h[3] << 24);
+    sl.hdr_zp = h[4];
+    sl.epoch = epoch_base + (uint64_t)i;
+    sl.state = kLive;
+  }
+  sl.claim = 0;
+}
+
+__global__ void finalize_kernel(const Slot *__restrict__ slots,
+                                const uint32_t *__restrict__ slot_idx,
+                                const uint64_t *__restrict__ offsets,
+                                uint8_t *__restrict__ status, int n) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const uint8_t st = status[i];
+  if (st == CASCADE_PUT_STORED && offsets[i] == kInvalidOffset)
+    status[i] = CASCADE_PUT_FAILED;
+  else if (st == CASCADE_PUT_DUP_BATCH && slots[slot_idx[i]].state != kLive)
+    status[i] = CASCADE_PUT_FAILED;
+}
+
+__global__ void lookup_kernel(Slot *slots, uint64_t mask,
+                              const uint64_t *__restrict__ keys, int stride,
+                              int n, int touch, uint64_t epoch_base,
+                              LookupInfo *__restrict__ out) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const uint64_t s0 = keys[(size_t)i * stride] ^ kKeyMask0;
+  const uint64_t s1 = keys[(size_t)i * stride + 1] ^ kKeyMask1;
+  const uint64_t h = slot_hash(s0, s1);
+  LookupInfo r = {};
+  r.slot = kNoSlot;
+  for (int p = 0; p < kMaxProbe; ++p) {
+    const uint64_t idx = (h + (uint64_t)p) & mask;
+    Slot *sl = slots + idx;
+    uint64_t a, b;
+    ld_key(sl, a, b);
+    if ((a | b) == 0) break;
+    if (a != s0 || b != s1) continue;
+    if (sl->state == kLive) {
+      r.found = 1;
+      r.flags = sl->flags;
+      r.offset = sl->offset;
+      r.size = sl->size;
+      r.hdr_scale = sl->hdr_scale;
+      r.hdr_zp = sl->hdr_zp;
+      r.slot = (uint32_t)idx;
+      if (touch) sl->epoch = epoch_base + (uint64_t)i;
+    }
+    break;
+  }
+  out[i] = r;
+}
+
+__global__ void relocate_kernel(Slot *slots, const uint32_t *__restrict__ idx,
+                                const uint64_t *__restrict__ offsets,
+                                const uint32_t *__restrict__ flags,
+                                const uint8_t *__restrict__ headers, int n) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  Slot &sl = slots[idx[i]];
+  const uint8_t *h = headers + 8 * (size_t)i;
+  sl.offset = offsets[i];
+  sl.flags = flags[i];
+  sl.hdr_scale = (uint32_t)h[0] | ((uint32_t)h[1] << 8) |
+                 ((uint32_t)h[2] << 16) | ((uint32_t)h[3] << 24);
+  sl.hdr_zp = h[4];
+}
+
+__global__ void scan_kernel(const Slot *__restrict__ slots, uint64_t nslots,
+                            uint32_t tier_flag, uint32_t *count,
+                            ScanRec *__restrict__ out, uint32_t max_out) {
+  for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x;
+       i < nslots; i += (uint64_t)gridDim.x * blockDim.x) {
+    const Slot &sl = slots[i];
+    if (sl.state != kLive || !(sl.flags & tier_flag)) continue;
+    const uint32_t k = atomicAdd(count, 1u);
+    if (k < max_out) {
+      ScanRec r;
+      r.slot = (uint32_t)i;
+      r.flags = sl.flags;
+      r.size = sl.size;
+      r.offset = sl.offset;
+      r.epoch = sl.epoch;
+      out[k] = r;
+    }
+  }
+}
+
+__global__ void pool_alloc_kernel(PoolDev *pool, const uint64_t *__restrict__ req,
+                                  int n, uint64_t *__restrict__ offsets) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const uint64_t want = req[i];
+  if (want == kNoRequest) { offsets[i] = kInvalidOffset; return; }
+  const int c = size_class(want);
+  const uint64_t bytes = class_bytes(c);
+  const uint32_t k = atomicAdd(&pool->taken[c], 1u);
+  const uint32_t top = pool->top[c];  // not written by this kernel
+  if (k < top) {
+    offsets[i] = pool->stack[c][top - 1 - k];
+    return;
+  }
+  unsigned long long off =
+      atomicAdd(reinterpret_cast<unsigned long long *>(&pool->bump),
+                (unsigned long long)bytes);
+  if (off + bytes > pool->capacity) {
+    atomicAdd(reinterpret_cast<unsigned long long *>(&pool->bump),
+              (unsigned long long)(0ull - bytes));
+    offsets[i] = kInvalidOffset;
+    return;
+  }
+  offsets[i] = off;
+}
+
+__global__ void pool_alloc_finish_kernel(PoolDev *pool) {
+  for (int c = threadIdx.x; c < kNumClasses; c += blockDim.x) {
+    const uint32_t t = pool->taken[c];
+    if (t) {
+      const uint32_t top = pool->top[c];
+      pool->top[c] = top - (t < top ? t : top);
+      pool->taken[c] = 0;
+    }
+  }
+}
+
+__global__ void pool_free_kernel(PoolDev *pool, const uint64_t *__restrict__ req,
+                                 const uint64_t *__restrict__ offsets,
+                                 const uint8_t *__restrict__ release, int n) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n || !release[i]) return;
+  const uint64_t off = offsets[i];
+  if (off == kInvalidOffset || req[i] == kNoRequest) return;
+  const int c = size_class(req[i]);
+  const uint32_t k = atomicAdd(&pool->top[c], 1u);
+  if (k < pool->cap[c] && pool->stack[c] != nullptr) {
+    pool->stack[c][k] = off;
+  } else {
+    atomicSub(&pool->top[c], 1u);
+    atomicAdd(reinterpret_cast<unsigned long long *>(&pool->overflow), 1ull);
+  }
+}
+
+inline int blocks_for(int n) { return (n + 255) / 256; }
+
+}  // namespace
+
+int launch_index_claim(Slot *slots, uint64_t mask, const uint64_t *keys,
+                       int key_stride_u64, const uint64_t *seqs, int n,
+                       uint32_t *slot_idx, int *err, cudaStream_t s) {
+  if (n <= 0) return CASCADE_OK;
+  claim_kernel<<<blocks_for(n), 256, 0, s>>>(slots, mask, keys, key_stride_u64,
+                                             seqs, n, slot_idx, err);
+  count_launches(1);
+  CB_CUDA(cudaGetLastError());
+  return CASCADE_OK;
+}
+
+int launch_index_resolve(const Slot *slots, const uint32_t *slot_idx,
+                         const uint64_t *seqs, int n, uint8_t *status,
+                         cudaStream_t s) {
+  if (n <= 0) return CASCADE_OK;
+  resolve_kernel<<<blocks_for(n), 256, 0, s>>>(slots, slot_idx, seqs, n,
+                                               status);
+  count_launches(1);
+  CB_CUDA(cudaGetLastError());
+  return CASCADE_OK;
+}
+
+int launch_index_commit(Slot *slots, const uint32_t *slot_idx,
+                        const uint8_t *status, const uint64_t *offsets,
+                        const uint64_t *sizes, const uint32_t *flags,
+                        const uint8_t *headers, uint64_t epoch_base, int n,
+                        cudaStream_t s) {
+  if (n <= 0) return CASCADE_OK;
+  commit_kernel<<<blocks_for(n), 256, 0, s>>>(slots, slot_idx, status, offsets,
+                                              sizes, flags, headers,
+                                              epoch_base, n);
+  count_launches(1);
+  CB_CUDA(cudaGetLastError());
+  return CASCADE_OK;
+}
+
+int launch_index_finalize(const Slot *slots, const uint32_t *slot_idx,
+                          const uint64_t *offsets, uint8_t *status, int n,
+                          cudaStream_t s) {
+  if (n <= 0) return CASCADE_OK;
+  finalize_kernel<<<blocks_for(n), 256, 0, s>>>(slots, slot_idx, offsets,
+                                                status, n);
+  count_launches(1);
+  CB_CUDA(cudaGetLastError());
+  return CASCADE_OK;
+}
+
+int launch_index_lookup(Slot *slots, uint64_t mask, const uint64_t *keys,
+                        int key_stride_u64, int n, int touch,
+                        uint64_t epoch_base, LookupInfo *out, cudaStream_t s) {
+  if (n <= 0) return CASCADE_OK;
+  lookup_kernel<<<blocks_for(n), 256, 0, s>>>(slots, mask, keys, key_stride_u64,
+                                              n, touch, epoch_base, out);
+  count_launches(1);
+  CB_CUDA(cudaGetLastError());
+  return CASCADE_OK;
+}
+
+int launch_index_relocate(Slot *slots, const uint32_t *slot_idx,
+                          const uint64_t *offsets, const uint32_t *flags,
+                          const uint8_t *headers, int n, cudaStream_t s) {
+  if (n <= 0) return CASCADE_OK;
+  relocate_kernel<<<blocks_for(n), 256, 0, s>>>(slots, slot_idx, offsets,
+                                                flags, headers, n);
+  count_launches(1);
+  CB_CUDA(cudaGetLastError());
+  return CASCADE_OK;
+}
+
+int launch_index_scan(const Slot *slots, uint64_t nslots, uint32_t tier_flag,
+                      uint32_t *count, ScanRec *out, uint32_t max_out,
+                      cudaStream_t s) {
+  CB_CUDA(cudaMemsetAsync(count, 0, sizeof(uint32_t), s));
+  const int grid = grid_for(nslots, 256, 8);
+  scan_kernel<<<grid, 256, 0, s>>>(slots, nslots, tier_flag, count, out,
+                                   max_out);
+  count_launches(1);
+  CB_CUDA(cudaGetLastError());
+  return CASCADE_OK;
+}
+
+int launch_pool_alloc(PoolDev *pool, const uint64_t *req, int n,
+                      uint64_t *offsets, cudaStream_t s) {
+  if (n <= 0) return CASCADE_OK;
+  pool_alloc_kernel<<<blocks_for(n), 256, 0, s>>>(pool, req, n, offsets);
+  count_launches(1);
+  CB_CUDA(cudaGetLastError());
+  pool_alloc_finish_kernel<<<1, 256, 0, s>>>(pool);
+  count_launches(1);
+  CB_CUDA(cudaGetLastError());
+  return CASCADE_OK;
+}
+
+int launch_pool_free(PoolDev *pool, const uint64_t *req,
+                     const uint64_t *offsets, const uint8_t *release, int n,
+                     cudaStream_t s) {
+  if (n <= 0) return CASCADE_OK;
+  pool_free_kernel<<<blocks_for(n), 256, 0, s>>>(pool, req, offsets, release,
+                                                 n);
+  count_launches(1);
+  CB_CUDA(cudaGetLastError());
+  return CASCADE_OK;
+}
+
+}  // namespace cb

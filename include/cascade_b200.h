@@ -87,6 +87,142 @@ int cascade_compute_block_id(const uint8_t *data, uint64_t size,
 int cascade_diag_sha_peak(int device, uint32_t chunks_per_thread,
                           double *gbps, double *ms);
 
+/* Diagnostics: kernels this library has launched since it was loaded
+ * (all devices, all threads). */
+uint64_t cascade_diag_launch_count(void);
+
+/* ------------------------------------------------------------------ */
+/* The block store (CascadeStore, cascade.hpp:420-502).                 */
+
+/* CascadeConfig (cascade.hpp:25-60; the 18 fields bound at
+ * bindings.cpp:15-35, plus num_io_threads), followed by B200 extensions.
+ * cascade_config_init() sets the reference defaults.  Fields the reference
+ * never reads on this path (compression_enabled, num_io_threads) and the
+ * cold-tier / prefetch fields (lustre_*, prefetch_*, aggregated_lustre,
+ * agg_file_size) are accepted and ignored: the Lustre tier and the
+ * prefetch pipeline are not part of this library. */
+typedef struct cascade_config {
+  uint64_t gpu_capacity_bytes;  /* 32 GiB: the HBM pool */
+  int32_t gpu_device_id;        /* 0 */
+  int32_t use_gpu;              /* 1: 0 = no HBM tier (kernels still run on
+                                   the GPU; blocks live in the DRAM tier) */
+  uint64_t shm_capacity_bytes;  /* 64 GiB: the pinned DRAM tier */
+  const char *shm_path;         /* "/dev/shm/cascade" (unused: the DRAM tier
+                                   is anonymous pinned memory) */
+  const char *lustre_path;      /* "cascade_store" */
+  uint64_t lustre_stripe_size;  /* 1 MiB */
+  int32_t lustre_stripe_count;  /* 16 */
+  int32_t dedup_enabled;        /* 1 */
+  int32_t compression_enabled;  /* 1 */
+  int32_t num_io_threads;       /* 8 */
+  int32_t semantic_eviction;    /* 1: demote non-prefix blocks first */
+  int32_t promotion_enabled;    /* 1: DRAM hits move back to HBM */
+  int32_t prefetch_enabled;     /* 1 */
+  int32_t prefetch_threads;     /* 2 */
+  uint64_t prefetch_queue_size; /* 64 */
+  int32_t kv_compression;       /* 0: 1 = DRAM tier holds KVCompressor's
+                                   INT8 form of blocks >= 64 bytes */
+  int32_t aggregated_lustre;    /* 0 */
+  uint64_t agg_file_size;       /* 256 MiB */
+  /* --- B200 extensions --- */
+  int32_t gpu_q8;               /* 0: HBM holds raw bytes, as the
+                                   reference's GPU tier; 1 = HBM also holds
+                                   the INT8 form when kv_compression is on
+                                   (gpu_used then counts those size/2
+                                   bytes) */
+  int32_t reserved0;
+  uint64_t index_slots;         /* device index capacity, a power of two;
+                                   0 = derived from the tier capacities */
+  uint64_t dram_chunk_bytes;    /* pinned-arena growth unit; 0 = 1 GiB */
+} cascade_config_t;
+
+/* CascadeStore::Stats (cascade.hpp:439-456), field for field. */
+typedef struct cascade_stats {
+  uint64_t gpu_used, shm_used, gpu_hits, shm_hits, lustre_hits, misses,
+      dedup_hits, gpu_evictions, shm_evictions, promotions_to_gpu,
+      promotions_to_shm, prefetch_completed, compression_savings_bytes,
+      shm_puts, lustre_puts;
+} cascade_stats_t;
+
+typedef struct cascade_store cascade_store_t;
+
+void cascade_config_init(cascade_config_t *cfg);
+/* sizeof(cascade_config_t) and sizeof(cascade_stats_t) as compiled, for
+ * bindings that lay the structs out themselves (ctypes, cgo, JNA). */
+void cascade_struct_sizes(size_t *config_bytes, size_t *stats_bytes);
+
+/* CascadeStore(cfg) (bindings.cpp:72, cascade_core.cpp:960-989).
+ * Fails with CASCADE_ERR_NODEVICE on a machine without a CUDA device. */
+int cascade_store_create(const cascade_config_t *cfg, cascade_store_t **out);
+int cascade_store_destroy(cascade_store_t *s);
+
+/* CascadeStore.put(block_id, data, is_prefix) (bindings.cpp:73-76,
+ * cascade_core.cpp:1074-1135) from a host buffer.  *stored = the
+ * reference's bool result.  Synchronous. */
+int cascade_store_put(cascade_store_t *s, const char *block_id,
+                      const uint8_t *data, uint64_t size, int is_prefix,
+                      int *stored);
+
+/* CascadeStore.get(block_id, out) (bindings.cpp:77-82,
+ * cascade_core.cpp:1138-1189) into a host buffer of out_capacity bytes.
+ * *found / *size as the reference's (found, size) tuple.  When the block
+ * is larger than out_capacity nothing is written, *found = 1 and *size is
+ * the size needed (the reference writes past the buffer instead).
+ * Synchronous. */
+int cascade_store_get(cascade_store_t *s, const char *block_id, uint8_t *out,
+                      uint64_t out_capacity, int *found, uint64_t *size);
+
+/* CascadeStore::contains (cascade_core.cpp:1192-1200). */
+int cascade_store_contains(cascade_store_t *s, const char *block_id,
+                           int *present);
+/* CascadeStore::get_stats (cascade_core.cpp:1238-1257). */
+int cascade_store_get_stats(cascade_store_t *s, cascade_stats_t *out);
+/* CascadeStore::clear (cascade_core.cpp:1259-1277). */
+int cascade_store_clear(cascade_store_t *s);
+/* CascadeStore::flush (cascade_core.cpp:1279-1282): waits for the store's
+ * device work; there is no file tier to flush. */
+int cascade_store_flush(cascade_store_t *s);
+
+/* The 16-byte key a block id names: the id's bytes when it is 32
+ * lowercase hex characters (compute_block_id's format), otherwise a key
+ * this store assigned to that string on first use. */
+int cascade_store_key_of(cascade_store_t *s, const char *block_id,
+                         uint8_t key_out[16]);
+
+/* Batched put of n device-resident blocks (the reference's OpenMP
+ * put_batch, cascade_core.cpp:1203-1218, not bound to Python there).
+ * h_ptrs/h_sizes: host arrays of device addresses and byte counts.
+ * h_keys: n x 16 key bytes, or NULL to content-address every block by
+ * SHA-256 (key = digest bytes 0..15, as compute_block_id).  h_prefix:
+ * n is_prefix flags or NULL.  h_status: n CASCADE_PUT_* codes or NULL.
+ * h_digests: n x 32 digest bytes (content-addressed only) or NULL.
+ * `stream` is waited on before the inputs are read.  Synchronous. */
+int cascade_store_put_batch(cascade_store_t *s, size_t n,
+                            const uint64_t *h_ptrs, const uint64_t *h_sizes,
+                            const uint8_t *h_keys, const uint8_t *h_prefix,
+                            uint8_t *h_status, uint8_t *h_digests,
+                            void *stream, uint64_t *n_stored);
+
+/* Batched put of n HOST blocks (pinned or pageable), content-addressed
+ * when h_keys is NULL.  The library moves the bytes to the GPU through its
+ * own staging in pipelined chunks.  Synchronous. */
+int cascade_store_put_batch_host(cascade_store_t *s, size_t n,
+                                 const uint8_t *const *h_blocks,
+                                 const uint64_t *h_sizes,
+                                 const uint8_t *h_keys,
+                                 const uint8_t *h_prefix, uint8_t *h_status,
+                                 uint8_t *h_digests, uint64_t *n_stored);
+
+/* Batched get (get_batch, cascade_core.cpp:1220-1235) into device
+ * buffers: h_out_ptrs[i] (device address) of h_out_caps[i] bytes.
+ * h_sizes[i] = stored size (also when it did not fit), h_found[i] = 1 when
+ * the key is stored.  Synchronous. */
+int cascade_store_get_batch(cascade_store_t *s, size_t n,
+                            const uint8_t *h_keys, const uint64_t *h_out_ptrs,
+                            const uint64_t *h_out_caps, uint64_t *h_sizes,
+                            uint8_t *h_found, void *stream,
+                            uint64_t *n_found);
+
 #ifdef __cplusplus
 }
 #endif
