@@ -39,6 +39,8 @@ _SIGS = {
     "cascade_abi_version": (_int, []),
     "cascade_sha256_batch": (_int, [_vp, _vp, _sz, _vp, _vp]),
     "cascade_kv_compress_batch": (_int, [_vp, _vp, _vp, _sz, _u64, _vp]),
+    "cascade_kv_compress_batch_noalloc": (_int, [_vp, _vp, _vp, _sz, _u64,
+                                                 _vp]),
     "cascade_kv_decompress_batch": (_int, [_vp, _vp, _vp, _sz, _u64, _vp]),
     "cascade_copy_batch": (_int, [_vp, _vp, _vp, _sz, _u64, _vp]),
     "cascade_compute_block_id": (_int, [_vp, _u64, ctypes.c_char_p]),

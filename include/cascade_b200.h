@@ -60,6 +60,27 @@ int cascade_kv_compress_batch(const uint64_t *d_src, const uint64_t *d_sizes,
                               const uint64_t *d_dst, size_t n,
                               uint64_t max_size, void *stream);
 
+/* No counterpart in the reference.  The same compression as
+ * cascade_kv_compress_batch (identical output bytes), for callers that
+ * cannot let a library allocate device memory: for example an inference
+ * engine that reserved nearly all of HBM for its own KV cache at start-up,
+ * or an ingest loop that cannot risk an allocator call stalling or failing
+ * mid-step.  It calls no cudaMalloc, cudaFree or other allocating routine;
+ * its per-block scratch is a fixed 512 KiB array built into the library,
+ * present on every GPU that loads the library until the process exits.
+ * Limits and rules:
+ *   - at most 65536 blocks per call; larger n fails with
+ *     CASCADE_ERR_INVALID and an explanatory cascade_last_error();
+ *   - all calls on a GPU share that one array, so calls whose work overlaps
+ *     on the same GPU race: keep them on one stream;
+ *   - the first call on each GPU looks up the array's device address (a
+ *     one-time set-up); make that first call before any stream capture;
+ *   - `stream` must belong to the current device. */
+int cascade_kv_compress_batch_noalloc(const uint64_t *d_src,
+                                      const uint64_t *d_sizes,
+                                      const uint64_t *d_dst, size_t n,
+                                      uint64_t max_size, void *stream);
+
 /* KVCompressor::decompress (cascade_core.cpp:851-872) as called by
  * CascadeStore::get (cascade_core.cpp:1149-1156): d_src[i] holds a
  * compressed block; d_out_sizes[i] (even) bytes are written to d_dst[i]. */
