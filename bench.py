@@ -44,6 +44,9 @@ def parse():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--blocks", type=int, default=N_BLOCKS)
+    ap.add_argument("--layers", type=int, default=32,
+                    help="layers per KV block (32 = 2 MiB; smaller for "
+                         "profiling captures)")
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args()
@@ -51,16 +54,20 @@ def parse():
 
 def workload_config(args, block_bytes):
     return {
-        "workload": f"llama3-8b-kv-{block_bytes >> 20}MiB-x{args.blocks}",
+        "workload": "llama3-8b-kv-" + (
+            f"{block_bytes >> 20}MiB" if block_bytes % (1 << 20) == 0
+            else f"{block_bytes >> 10}KiB") + f"-x{args.blocks}",
         "blocks_per_gpu": args.blocks,
         "block_bytes": block_bytes,
-        "block_shape": "[32 layers][K,V][8 heads][16 tokens][128 dim] fp16",
+        "block_shape": f"[{args.layers} layers][K,V][8 heads][16 tokens]"
+                       "[128 dim] fp16",
         "values": "N(0,1), 0.1% channels x20, seeded (synthetic)",
         "content_addressed": True,
         "kv_compression": True,
         "hbm_format": "int8 codes + per-block header in the index",
         "dedup": True,
-        "l2": "inputs (8 GiB/GPU) exceed the 126 MB L2; no flush needed",
+        "l2": f"inputs ({args.blocks * block_bytes / 2**30:.2f} GiB/GPU) "
+              "exceed the 126 MB L2; no flush needed",
         "parallelism": f"weak x{args.gpus} (each rank its own blocks)",
     }
 
@@ -210,7 +217,8 @@ def main_ours(args):
         return float(t.item())
 
     L = _lib.load()
-    blocks = workloads.kv_blocks_torch(args.blocks, SEED + rank, dev)
+    blocks = workloads.kv_blocks_torch(args.blocks, SEED + rank, dev,
+                                       layers=args.layers)
     n, bb = blocks.shape
     total = n * bb
     cfg = cc.CascadeConfig()
