@@ -356,12 +356,12 @@ def main_ours(args):
         "config": workload_config(args, bb),
         "blocks_per_s": world * args.steps * n / (ms * 1e-3),
         "roofline": {
-            "kernel": "sha256_lane_per_block", "bound": "int",
+            "kernel": "sha256_pipelined", "bound": "int",
             "achieved": sha_gbps, "peak": peak_gbps.value, "unit": "GB/s",
             "frac": sha_gbps / peak_gbps.value,
             "peak_source": "measured live: the same SHA-256 rounds from "
                            "registers with all 64 warp slots/SM busy",
-            "traffic": (traffic or {}).get("sha256_lane_per_block"),
+            "traffic": (traffic or {}).get("sha256_pipelined"),
             "note": f"{n} blocks = {n} serial chains = {(n + 31) // 32} "
                     "warps; per-chain issue latency, not the integer pipe, "
                     "bounds 2 MiB blocks"},

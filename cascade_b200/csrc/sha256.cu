@@ -2,9 +2,11 @@
 //
 // Replaces the per-block OpenSSL call of compute_block_id
 // (cascade_core.cpp:43-53) with one launch over a whole batch.  A lane owns
-// one block; 32 blocks share a warp, and CTAs are sized so the warps spread
-// over all 148 SMs before any SM gets a second warp (a chain is bound by its
-// own warp's issue rate, so spreading beats packing).
+// one block's chain; 32 blocks share a warp.  Merkle-Damgard chaining makes
+// a block's 64-byte chunks strictly sequential, so a batch of large blocks
+// is bound by how fast one warp can run the rounds of one chunk; the kernel
+// below takes everything else (loads, byte swaps, the message schedule) off
+// that warp.
 #include "common.cuh"
 #include "sha256.cuh"
 
@@ -26,99 +28,212 @@ __device__ __forceinline__ uint32_t ldg_u32(const uint32_t *p) {
   return v;
 }
 
-// Full chunks of a 16-byte aligned block, with the next chunk's loads issued
-// before the current chunk's rounds.
-__device__ __forceinline__ void chunks_aligned16(uint32_t st[8],
-                                                 const uint4 *q,
-                                                 uint64_t nfull) {
-  if (nfull == 0) return;
-  uint4 n0 = ldg_stream(q), n1 = ldg_stream(q + 1), n2 = ldg_stream(q + 2),
-        n3 = ldg_stream(q + 3);
-  for (uint64_t c = 0; c < nfull; ++c) {
-    uint32_t w[16] = {sha::bswap(n0.x), sha::bswap(n0.y), sha::bswap(n0.z),
-                      sha::bswap(n0.w), sha::bswap(n1.x), sha::bswap(n1.y),
-                      sha::bswap(n1.z), sha::bswap(n1.w), sha::bswap(n2.x),
-                      sha::bswap(n2.y), sha::bswap(n2.z), sha::bswap(n2.w),
-                      sha::bswap(n3.x), sha::bswap(n3.y), sha::bswap(n3.z),
-                      sha::bswap(n3.w)};
-    if (c + 1 < nfull) {
-      const uint4 *nq = q + 4 * (c + 1);
-      n0 = ldg_stream(nq);
-      n1 = ldg_stream(nq + 1);
-      n2 = ldg_stream(nq + 2);
-      n3 = ldg_stream(nq + 3);
+// ---------------------------------------------------------------------------
+// Producer/consumer SHA-256: a CTA of two warps hashes 32 blocks.  Warp 0
+// (the consumer) runs only the 64 rounds of each chunk; warp 1 (the
+// producer, on another scheduler) loads the message, expands the schedule
+// and hands K[t]+W[t] to the consumer through a ring of kStages chunk slots
+// in shared memory.  Named barriers order the ring: full[s] (producer ->
+// consumer) and empty[s] (consumer -> producer).  Both warps run the same
+// warp-uniform number of chunks, so every barrier is reached by all 64
+// threads; lanes whose block needs fewer chunks process padding and discard
+// the result.
+__device__ __forceinline__ void bar_sync(int id) {
+  asm volatile("bar.sync %0, 64;" ::"r"(id) : "memory");
+}
+__device__ __forceinline__ void bar_arrive(int id) {
+  asm volatile("bar.arrive %0, 64;" ::"r"(id) : "memory");
+}
+
+struct Lane {
+  const uint8_t *p;
+  uint64_t len, nfull;
+  uint32_t rem, nch;  // nch: chunks including padding
+  bool aligned;
+};
+
+__device__ __forceinline__ Lane lane_of(const uint64_t *ptrs,
+                                        const uint64_t *sizes, int n, int i) {
+  Lane l;
+  l.p = i < n ? reinterpret_cast<const uint8_t *>(ptrs[i]) : nullptr;
+  l.len = i < n ? sizes[i] : 0;
+  l.nfull = l.len >> 6;
+  l.rem = (uint32_t)(l.len & 63u);
+  l.nch = (uint32_t)l.nfull + (l.rem < 56 ? 1u : 2u);
+  l.aligned = ((uintptr_t)l.p & 15u) == 0;
+  return l;
+}
+
+// Big-endian message words of chunk c of a lane's padded message.
+__device__ __forceinline__ void message_words(const Lane &l, uint64_t c,
+                                              const uint4 *pre, uint32_t w[16]) {
+  if (c < l.nfull) {
+    if (l.aligned) {
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        w[4 * k] = sha::bswap(pre[k].x);
+        w[4 * k + 1] = sha::bswap(pre[k].y);
+        w[4 * k + 2] = sha::bswap(pre[k].z);
+        w[4 * k + 3] = sha::bswap(pre[k].w);
+      }
+    } else {
+      const uint32_t o = (uint32_t)((uintptr_t)l.p & 3u);
+      const uint32_t *cw = (const uint32_t *)(l.p - o) + 16 * c;
+      const uint32_t sel = (o << 12) | ((o + 1) << 8) | ((o + 2) << 4) | (o + 3);
+      uint32_t raw[17];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) raw[j] = ldg_u32(cw + j);
+      raw[16] = o ? ldg_u32(cw + 16) : 0u;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) w[j] = __byte_perm(raw[j], raw[j + 1], sel);
     }
-    sha::compress(st, w);
+    return;
+  }
+  // Padding: the tail bytes, 0x80, zeros, and the bit length in the last
+  // two words of the final chunk (FIPS 180-4 section 5.1.1).
+  const uint64_t extra = c - l.nfull;   // 0 or 1 for real lanes
+  const uint8_t *tail = l.p + (l.nfull << 6);
+  const bool first = extra == 0;
+  const bool last = c + 1 == l.nch;
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    uint32_t word = 0;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const uint32_t idx = 4 * j + k;
+      uint32_t byte = 0;
+      if (first && idx < l.rem) byte = tail[idx];
+      else if (first && idx == l.rem) byte = 0x80u;
+      word |= byte << (24 - 8 * k);
+    }
+    w[j] = word;
+  }
+  if (last) {
+    const uint64_t bits = l.len * 8u;
+    w[14] = (uint32_t)(bits >> 32);
+    w[15] = (uint32_t)bits;
   }
 }
 
-// Full chunks of a block at any address: aligned 32-bit loads of the words
-// that cover the chunk, then one byte permute per message word.  The
-// covering words stay inside the 4-byte-aligned span of the block, so no
-// load leaves the allocation's granule.
-__device__ __forceinline__ void chunks_unaligned(uint32_t st[8],
-                                                 const uint8_t *p,
-                                                 uint64_t nfull) {
-  const uint32_t o = (uint32_t)((uintptr_t)p & 3u);
-  const uint32_t *base = (const uint32_t *)(p - o);
-  // Selector picking bytes o..o+3 of the pair (x, y) in big-endian order.
-  const uint32_t sel = (o << 12) | ((o + 1) << 8) | ((o + 2) << 4) | (o + 3);
-  for (uint64_t c = 0; c < nfull; ++c) {
-    const uint32_t *cw = base + 16 * c;
-    uint32_t raw[17];
-#pragma unroll
-    for (int j = 0; j < 16; ++j) raw[j] = ldg_u32(cw + j);
-    // The 17th word is needed only when the chunk is misaligned.
-    raw[16] = o ? ldg_u32(cw + 16) : 0u;
-    uint32_t w[16];
-#pragma unroll
-    for (int j = 0; j < 16; ++j) w[j] = __byte_perm(raw[j], raw[j + 1], sel);
-    sha::compress(st, w);
-  }
-}
+// kGroups (consumer, producer) warp pairs per CTA: warp 2g consumes and
+// warp 2g+1 produces for group g.  Named barrier ids per group:
+// full = 1 + 2*kStages*g + s, empty = full + kStages (at most 15 ids).
+template <int kGroups, int kStages, int kRound>
+__global__ void __launch_bounds__(64 * kGroups)
+    sha256_pipelined(const uint64_t *__restrict__ ptrs,
+                     const uint64_t *__restrict__ sizes, int n,
+                     uint32_t *__restrict__ digests, uint32_t one,
+                     uint32_t neg_one) {
+  static_assert(2 * kGroups * kStages <= 15, "named barrier ids");
+  // ring[g][s][t/4][lane] holds K[t..t+3] + W[t..t+3] of one chunk.
+  __shared__ uint4 ring_all[kGroups][kStages][16][32];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int grp = warp >> 1;
+  uint4 (*ring)[16][32] = ring_all[grp];
+  const int full_bar = 1 + 2 * kStages * grp;
+  const int empty_bar = full_bar + kStages;
+  const int i = (blockIdx.x * kGroups + grp) * 32 + lane;
+  const Lane l = lane_of(ptrs, sizes, n, i);
+  const uint32_t nch = __reduce_max_sync(0xffffffffu, l.nch);
 
-__global__ void __launch_bounds__(256)
-    sha256_lane_per_block(const uint64_t *__restrict__ ptrs,
-                          const uint64_t *__restrict__ sizes, int n,
-                          uint32_t *__restrict__ digests) {
-  const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= n) return;
-  const uint8_t *p = reinterpret_cast<const uint8_t *>(ptrs[i]);
-  const uint64_t len = sizes[i];
-  const uint64_t nfull = len >> 6;
+  if (warp & 1) {  // -------------------------------------------- producer
+    uint4 pre[4] = {};
+    const uint4 *q = reinterpret_cast<const uint4 *>(l.p);
+    if (l.aligned && l.nfull > 0) {
+#pragma unroll
+      for (int k = 0; k < 4; ++k) pre[k] = ldg_stream(q + k);
+    }
+    for (uint32_t c = 0; c < nch; ++c) {
+      const int s = (int)(c % kStages);
+      uint32_t w[16];
+      message_words(l, c, pre, w);
+      if (l.aligned && c + 1 < l.nfull) {  // next chunk's loads in flight
+#pragma unroll
+        for (int k = 0; k < 4; ++k) pre[k] = ldg_stream(q + 4 * (c + 1) + k);
+      }
+      if (c >= kStages) bar_sync(empty_bar + s);
+#pragma unroll
+      for (int t = 0; t < 64; t += 4) {
+        uint32_t kw[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int tt = t + u;
+          uint32_t wt;
+          if (tt < 16) {
+            wt = w[tt];
+          } else {
+            wt = w[tt & 15] + sha::sig0(w[(tt - 15) & 15]) + w[(tt - 7) & 15] +
+                 sha::sig1(w[(tt - 2) & 15]);
+            w[tt & 15] = wt;
+          }
+          kw[u] = wt + sha::K(tt);
+        }
+        ring[s][t >> 2][lane] = make_uint4(kw[0], kw[1], kw[2], kw[3]);
+      }
+      bar_arrive(full_bar + s);
+    }
+    // Take the consumer's last releases so no arrival is left pending.
+    for (uint32_t c = nch > kStages ? nch - kStages : 0; c < nch; ++c)
+      bar_sync(empty_bar + (int)(c % kStages));
+    return;
+  }
+  // -------------------------------------------------------------- consumer
   uint32_t st[8];
   sha::init(st);
-  if (((uintptr_t)p & 15u) == 0)
-    chunks_aligned16(st, reinterpret_cast<const uint4 *>(p), nfull);
-  else
-    chunks_unaligned(st, p, nfull);
-  sha::finish(st, p + (nfull << 6), (uint32_t)(len & 63u), len);
-  uint32_t *out = digests + 8 * (size_t)i;
+  for (uint32_t c = 0; c < nch; ++c) {
+    const int s = (int)(c % kStages);
+    bar_sync(full_bar + s);
+    uint32_t a = st[0], b = st[1], cc = st[2], d = st[3];
+    uint32_t e = st[4], f = st[5], g = st[6], h = st[7];
 #pragma unroll
-  for (int k = 0; k < 8; ++k) out[k] = sha::bswap(st[k]);  // digest byte order
+    for (int t = 0; t < 64; t += 4) {
+      const uint4 kw = ring[s][t >> 2][lane];
+      const uint32_t kv[4] = {kw.x, kw.y, kw.z, kw.w};
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        if (kRound == 0)
+          sha::round_kw(a, b, cc, d, e, f, g, h, kv[u], one, neg_one);
+        else
+          sha::round_kw3(a, b, cc, d, e, f, g, h, kv[u], one, neg_one);
+      }
+    }
+    bar_arrive(empty_bar + s);
+    if (c < l.nch) {
+      st[0] += a; st[1] += b; st[2] += cc; st[3] += d;
+      st[4] += e; st[5] += f; st[6] += g; st[7] += h;
+    }
+  }
+  if (i < n) {
+    uint32_t *out = digests + 8 * (size_t)i;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) out[k] = sha::bswap(st[k]);
+  }
 }
 
 }  // namespace
 
-// Threads per CTA so that ceil(n/32) warps land on distinct SMs first.
-static int sha_cta_threads(int n) {
-  int warps = (n + 31) / 32;
-  int per_cta = (warps + kSmCount - 1) / kSmCount;
-  if (per_cta < 1) per_cta = 1;
-  if (per_cta > 8) per_cta = 8;
-  return 32 * per_cta;
+template <int G, int S, int R>
+int launch_sha256_pipelined(const uint64_t *d_ptrs, const uint64_t *d_sizes,
+                            int n, uint8_t *d_digests, cudaStream_t s) {
+  if (n <= 0) return CASCADE_OK;
+  const int blocks = (n + 32 * G - 1) / (32 * G);
+  sha256_pipelined<G, S, R><<<blocks, 64 * G, 0, s>>>(
+      d_ptrs, d_sizes, n, reinterpret_cast<uint32_t *>(d_digests), 1u,
+      0xffffffffu);
+  count_launches(1);
+  CB_CUDA(cudaGetLastError());
+  return CASCADE_OK;
 }
 
 int launch_sha256(const uint64_t *d_ptrs, const uint64_t *d_sizes, int n,
                   uint8_t *d_digests, cudaStream_t s) {
-  if (n <= 0) return CASCADE_OK;
-  int threads = sha_cta_threads(n);
-  int blocks = (n + threads - 1) / threads;
-  sha256_lane_per_block<<<blocks, threads, 0, s>>>(
-      d_ptrs, d_sizes, n, reinterpret_cast<uint32_t *>(d_digests));
-  count_launches(1);
-  CB_CUDA(cudaGetLastError());
-  return CASCADE_OK;
+  // While there are fewer producer/consumer pairs than SMs each chain runs
+  // alone on its SM and the latency-tuned round (both recurrences three
+  // operations deep) wins; once every scheduler has work, the ALU pipe is
+  // the limit and the round with the fewest ALU instructions wins.
+  if (n <= 32 * kSmCount)
+    return launch_sha256_pipelined<1, 4, 1>(d_ptrs, d_sizes, n, d_digests, s);
+  return launch_sha256_pipelined<2, 3, 0>(d_ptrs, d_sizes, n, d_digests, s);
 }
 
 }  // namespace cb

@@ -89,54 +89,57 @@ __device__ __forceinline__ void compress(uint32_t st[8], uint32_t w[16]) {
   st[4] += e; st[5] += f; st[6] += g; st[7] += h;
 }
 
-// The rounds only, for a chunk whose 64 schedule words (already added to
-// the round constants) were produced elsewhere.
-__device__ __forceinline__ void rounds_kw(uint32_t st[8], const uint32_t *kw) {
-  uint32_t a = st[0], b = st[1], c = st[2], d = st[3];
-  uint32_t e = st[4], f = st[5], g = st[6], h = st[7];
-#pragma unroll
-  for (int t = 0; t < 64; ++t) {
-    uint32_t t1 = h + Sig1(e) + ((e & f) ^ (~e & g)) + kw[t];
-    uint32_t t2 = Sig0(a) + ((a & b) | (c & (a | b)));
-    h = g; g = f; f = e; e = d + t1;
-    d = c; c = b; b = a; a = t1 + t2;
-  }
-  st[0] += a; st[1] += b; st[2] += c; st[3] += d;
-  st[4] += e; st[5] += f; st[6] += g; st[7] += h;
+// x*m + y as one IMAD.  With m a run-time 1 (or -1) the compiler cannot
+// fold the multiply away, so the add is issued to the FMA pipe instead of
+// the integer ALU pipe, which the rotates and logic ops already fill.
+__device__ __forceinline__ uint32_t mad(uint32_t x, uint32_t m, uint32_t y) {
+  uint32_t r;
+  asm("mad.lo.u32 %0, %1, %2, %3;" : "=r"(r) : "r"(x), "r"(m), "r"(y));
+  return r;
 }
 
-// Builds the final one or two chunks for a message of `len` bytes whose
-// last `rem` = len % 64 bytes start at `tail`, and compresses them.  Byte
-// loads only: the tail may end anywhere.
-__device__ __forceinline__ void finish(uint32_t st[8], const uint8_t *tail,
-                                       uint32_t rem, uint64_t len) {
-  uint32_t w[16];
-#pragma unroll
-  for (int j = 0; j < 16; ++j) {
-    uint32_t word = 0;
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      uint32_t idx = 4 * j + k;
-      uint32_t byte = 0;
-      if (idx < rem) byte = tail[idx];
-      else if (idx == rem) byte = 0x80u;
-      word |= byte << (24 - 8 * k);
-    }
-    w[j] = word;
-  }
-  const uint64_t bits = len * 8u;
-  if (rem < 56) {
-    w[14] = (uint32_t)(bits >> 32);
-    w[15] = (uint32_t)bits;
-    compress(st, w);
-  } else {
-    compress(st, w);
-#pragma unroll
-    for (int j = 0; j < 14; ++j) w[j] = 0;
-    w[14] = (uint32_t)(bits >> 32);
-    w[15] = (uint32_t)bits;
-    compress(st, w);
-  }
+// One round given kw = K[t] + W[t], with the seven additions on the FMA
+// pipe (10 ALU + 7 IMAD instructions) and arranged so the e-chain is three
+// operations deep (rotate, LOP3, IMAD):
+//   e' = Sig1(e) + (Ch(e,f,g) + (d + (h + kw)))
+//   a' = e' + (Sig0(a) + (Maj(a,b,c) - d))          [= T1 + T2]
+__device__ __forceinline__ void round_kw(uint32_t &a, uint32_t &b, uint32_t &c,
+                                         uint32_t &d, uint32_t &e, uint32_t &f,
+                                         uint32_t &g, uint32_t &h, uint32_t kw,
+                                         uint32_t one, uint32_t neg_one) {
+  const uint32_t hk = mad(h, one, kw);
+  const uint32_t dhk = mad(d, one, hk);
+  const uint32_t ch = (e & f) ^ (~e & g);
+  const uint32_t dhkc = mad(ch, one, dhk);
+  const uint32_t e_new = mad(Sig1(e), one, dhkc);
+  const uint32_t maj = (a & b) | (c & (a | b));
+  const uint32_t q = mad(d, neg_one, maj);
+  const uint32_t u = mad(Sig0(a), one, q);
+  const uint32_t a_new = mad(e_new, one, u);
+  h = g; g = f; f = e; e = e_new;
+  d = c; c = b; b = a; a = a_new;
+}
+
+// A round with both recurrences three operations deep (rotate, LOP3, add):
+//   e' = Sig1(e) + Ch(e,f,g) + (d + h + kw)      [IMAD, IMAD]
+//   a' = IADD3(e', Sig0(a), Maj(a,b,c) - d)      [one three-input ALU add]
+// 11 ALU + 5 IMAD instructions.
+__device__ __forceinline__ void round_kw3(uint32_t &a, uint32_t &b,
+                                          uint32_t &c, uint32_t &d,
+                                          uint32_t &e, uint32_t &f,
+                                          uint32_t &g, uint32_t &h,
+                                          uint32_t kw, uint32_t one,
+                                          uint32_t neg_one) {
+  const uint32_t hk = mad(h, one, kw);
+  const uint32_t dhk = mad(d, one, hk);
+  const uint32_t ch = (e & f) ^ (~e & g);
+  const uint32_t dhkc = mad(ch, one, dhk);
+  const uint32_t e_new = mad(Sig1(e), one, dhkc);
+  const uint32_t maj = (a & b) | (c & (a | b));
+  const uint32_t q = mad(d, neg_one, maj);
+  const uint32_t a_new = e_new + Sig0(a) + q;
+  h = g; g = f; f = e; e = e_new;
+  d = c; c = b; b = a; a = a_new;
 }
 
 }  // namespace sha
