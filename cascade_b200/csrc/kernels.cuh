@@ -10,6 +10,15 @@ namespace cb {
 int launch_sha256(const uint64_t *d_ptrs, const uint64_t *d_sizes, int n,
                   uint8_t *d_digests, cudaStream_t s);
 
+// Chunks [c_begin, c_end) of each block (64-byte chunks of the padded
+// message).  Blocks that end in the range get their digest; blocks that go
+// on get their running state in d_state (8 words per block), from which a
+// call starting at c_end resumes.  d_state may be null when c_begin == 0
+// and c_end covers every block.
+int launch_sha256_range(const uint64_t *d_ptrs, const uint64_t *d_sizes,
+                        int n, uint8_t *d_digests, uint32_t *d_state,
+                        uint64_t c_begin, uint64_t c_end, cudaStream_t s);
+
 int launch_minmax(const uint64_t *d_ptrs, const uint64_t *d_sizes, int n,
                   uint64_t max_size, int2 *d_mnmx, cudaStream_t s);
 

@@ -118,12 +118,18 @@ __device__ __forceinline__ void message_words(const Lane &l, uint64_t c,
 // kGroups (consumer, producer) warp pairs per CTA: warp 2g consumes and
 // warp 2g+1 produces for group g.  Named barrier ids per group:
 // full = 1 + 2*kStages*g + s, empty = full + kStages (at most 15 ids).
+// Chunks [c_begin, c_end) of every block are processed; a block whose last
+// chunk falls in that range gets its digest written, a block that goes on
+// beyond c_end gets its running state saved to `state` (and the next call
+// with c_begin = this c_end resumes from it).  c_begin = 0 starts from the
+// initial hash value.  One call with [0, ~0) hashes whole blocks.
 template <int kGroups, int kStages, int kRound>
 __global__ void __launch_bounds__(64 * kGroups)
     sha256_pipelined(const uint64_t *__restrict__ ptrs,
                      const uint64_t *__restrict__ sizes, int n,
                      uint32_t *__restrict__ digests, uint32_t one,
-                     uint32_t neg_one) {
+                     uint32_t neg_one, uint32_t *__restrict__ state,
+                     uint64_t c_begin, uint64_t c_end) {
   static_assert(2 * kGroups * kStages <= 15, "named barrier ids");
   // ring[g][s][t/4][lane] holds K[t..t+3] + W[t..t+3] of one chunk.
   __shared__ uint4 ring_all[kGroups][kStages][16][32];
@@ -134,24 +140,30 @@ __global__ void __launch_bounds__(64 * kGroups)
   const int empty_bar = full_bar + kStages;
   const int i = (blockIdx.x * kGroups + grp) * 32 + lane;
   const Lane l = lane_of(ptrs, sizes, n, i);
-  const uint32_t nch = __reduce_max_sync(0xffffffffu, l.nch);
+  const uint64_t nch_warp = __reduce_max_sync(0xffffffffu, l.nch);
+  const uint64_t c_stop = nch_warp < c_end ? nch_warp : c_end;
+  // iterations of this call (warp-uniform): chunks c_begin + 0 .. + iters-1
+  const uint32_t iters = c_stop > c_begin ? (uint32_t)(c_stop - c_begin) : 0u;
 
   if (warp & 1) {  // -------------------------------------------- producer
     uint4 pre[4] = {};
     const uint4 *q = reinterpret_cast<const uint4 *>(l.p);
-    if (l.aligned && l.nfull > 0) {
+    if (l.aligned && c_begin < l.nfull && iters > 0) {
 #pragma unroll
-      for (int k = 0; k < 4; ++k) pre[k] = ldg_stream(q + k);
+      for (int k = 0; k < 4; ++k) pre[k] = ldg_stream(q + 4 * c_begin + k);
     }
-    for (uint32_t c = 0; c < nch; ++c) {
-      const int s = (int)(c % kStages);
+    for (uint32_t it = 0; it < iters; ++it) {
+      const uint64_t c = c_begin + it;
+      const int s = (int)(it % kStages);
       uint32_t w[16];
       message_words(l, c, pre, w);
-      if (l.aligned && c + 1 < l.nfull) {  // next chunk's loads in flight
+      // the next chunk's loads in flight (never past this call's range: the
+      // bytes of later chunks may not have arrived yet)
+      if (l.aligned && c + 1 < l.nfull && it + 1 < iters) {
 #pragma unroll
         for (int k = 0; k < 4; ++k) pre[k] = ldg_stream(q + 4 * (c + 1) + k);
       }
-      if (c >= kStages) bar_sync(empty_bar + s);
+      if (it >= kStages) bar_sync(empty_bar + s);
 #pragma unroll
       for (int t = 0; t < 64; t += 4) {
         uint32_t kw[4];
@@ -173,15 +185,21 @@ __global__ void __launch_bounds__(64 * kGroups)
       bar_arrive(full_bar + s);
     }
     // Take the consumer's last releases so no arrival is left pending.
-    for (uint32_t c = nch > kStages ? nch - kStages : 0; c < nch; ++c)
-      bar_sync(empty_bar + (int)(c % kStages));
+    for (uint32_t it = iters > kStages ? iters - kStages : 0; it < iters; ++it)
+      bar_sync(empty_bar + (int)(it % kStages));
     return;
   }
   // -------------------------------------------------------------- consumer
   uint32_t st[8];
-  sha::init(st);
-  for (uint32_t c = 0; c < nch; ++c) {
-    const int s = (int)(c % kStages);
+  if (c_begin == 0) {
+    sha::init(st);
+  } else if (i < n) {
+#pragma unroll
+    for (int k = 0; k < 8; ++k) st[k] = state[8 * (size_t)i + k];
+  }
+  for (uint32_t it = 0; it < iters; ++it) {
+    const uint64_t c = c_begin + it;
+    const int s = (int)(it % kStages);
     bar_sync(full_bar + s);
     uint32_t a = st[0], b = st[1], cc = st[2], d = st[3];
     uint32_t e = st[4], f = st[5], g = st[6], h = st[7];
@@ -203,10 +221,15 @@ __global__ void __launch_bounds__(64 * kGroups)
       st[4] += e; st[5] += f; st[6] += g; st[7] += h;
     }
   }
-  if (i < n) {
-    uint32_t *out = digests + 8 * (size_t)i;
+  if (i < n && l.nch > c_begin) {
+    if (l.nch <= c_end) {  // finished in this call: the digest
+      uint32_t *out = digests + 8 * (size_t)i;
 #pragma unroll
-    for (int k = 0; k < 8; ++k) out[k] = sha::bswap(st[k]);
+      for (int k = 0; k < 8; ++k) out[k] = sha::bswap(st[k]);
+    } else {               // continues in the next call
+#pragma unroll
+      for (int k = 0; k < 8; ++k) state[8 * (size_t)i + k] = st[k];
+    }
   }
 }
 
@@ -214,26 +237,36 @@ __global__ void __launch_bounds__(64 * kGroups)
 
 template <int G, int S, int R>
 int launch_sha256_pipelined(const uint64_t *d_ptrs, const uint64_t *d_sizes,
-                            int n, uint8_t *d_digests, cudaStream_t s) {
+                            int n, uint8_t *d_digests, uint32_t *d_state,
+                            uint64_t c_begin, uint64_t c_end, cudaStream_t s) {
   if (n <= 0) return CASCADE_OK;
   const int blocks = (n + 32 * G - 1) / (32 * G);
   sha256_pipelined<G, S, R><<<blocks, 64 * G, 0, s>>>(
       d_ptrs, d_sizes, n, reinterpret_cast<uint32_t *>(d_digests), 1u,
-      0xffffffffu);
+      0xffffffffu, d_state, c_begin, c_end);
   count_launches(1);
   CB_CUDA(cudaGetLastError());
   return CASCADE_OK;
 }
 
-int launch_sha256(const uint64_t *d_ptrs, const uint64_t *d_sizes, int n,
-                  uint8_t *d_digests, cudaStream_t s) {
+int launch_sha256_range(const uint64_t *d_ptrs, const uint64_t *d_sizes,
+                        int n, uint8_t *d_digests, uint32_t *d_state,
+                        uint64_t c_begin, uint64_t c_end, cudaStream_t s) {
   // While there are fewer producer/consumer pairs than SMs each chain runs
   // alone on its SM and the latency-tuned round (both recurrences three
   // operations deep) wins; once every scheduler has work, the ALU pipe is
   // the limit and the round with the fewest ALU instructions wins.
   if (n <= 32 * kSmCount)
-    return launch_sha256_pipelined<1, 4, 1>(d_ptrs, d_sizes, n, d_digests, s);
-  return launch_sha256_pipelined<2, 3, 0>(d_ptrs, d_sizes, n, d_digests, s);
+    return launch_sha256_pipelined<1, 4, 1>(d_ptrs, d_sizes, n, d_digests,
+                                            d_state, c_begin, c_end, s);
+  return launch_sha256_pipelined<2, 3, 0>(d_ptrs, d_sizes, n, d_digests,
+                                          d_state, c_begin, c_end, s);
+}
+
+int launch_sha256(const uint64_t *d_ptrs, const uint64_t *d_sizes, int n,
+                  uint8_t *d_digests, cudaStream_t s) {
+  return launch_sha256_range(d_ptrs, d_sizes, n, d_digests, nullptr, 0, ~0ull,
+                             s);
 }
 
 }  // namespace cb

@@ -112,8 +112,12 @@ struct Store {
   std::string shm_path, lustre_path;
   int dev = 0;
   bool hbm = false, dram_tier = false;
-  cudaStream_t s = nullptr;
-  cudaEvent_t ev = nullptr;
+  cudaStream_t s = nullptr;   // main: index, allocation, payload kernels
+  cudaStream_t s2 = nullptr;  // hashing, overlapped with the main stream
+  cudaStream_t s3 = nullptr;  // host-to-device copies of host blocks
+  cudaEvent_t ev = nullptr, ev2 = nullptr, ev3 = nullptr;
+  uint32_t *sha_state = nullptr;  // running SHA-256 states (striped hashing)
+  size_t sha_state_cap = 0;       // blocks
   uint8_t *pool = nullptr;
   uint64_t pool_cap = 0;
   PoolDev *d_pool = nullptr;
@@ -327,6 +331,45 @@ int grow_index(Store &st);
 
 }  // namespace
 
+// Statistics and tier accounting for a finished put batch (sc.h_status,
+// h_sizes, h_flags, h_off on the host), per CascadeStore::put.
+constexpr uint8_t kRetry = 0xff;  // internal: placed again by a later pass
+
+static void tally_put(Store &st, size_t n) {
+  for (size_t i = 0; i < n; ++i) {
+    const uint8_t r = st.sc.h_status[i];
+    if (r == kRetry) continue;
+    const uint64_t size = st.sc.h_sizes[i];
+    const bool hit = (r == CASCADE_PUT_DUP_KNOWN || r == CASCADE_PUT_DUP_BATCH);
+    if (hit && st.cfg.dedup_enabled) ++st.dedup_hits;
+    // With dedup off a repeated id reaches the tier, whose put answers true
+    // for an id it holds; the reference counts that as an SHM put when the
+    // DRAM tier is the only tier (cascade_core.cpp:1108-1111).
+    if (hit && !st.cfg.dedup_enabled && !st.hbm) ++st.shm_puts;
+    // The reference compresses every block that passes the dedup check,
+    // whatever tier then takes it (cascade_core.cpp:1086-1092).
+    if (st.cfg.kv_compression && size >= 64 && !(hit && st.cfg.dedup_enabled))
+      st.compression_savings += size - (8 + size / 2);
+    if (r != CASCADE_PUT_STORED) {
+      // A DRAM placement that did not become live gives its space back.
+      if ((st.sc.h_flags[i] & kTierDram) && st.sc.h_off[i] != kInvalidOffset) {
+        bool q8 = (st.sc.h_flags[i] & kFlagQ8) != 0;
+        st.dram->free(st.sc.h_off[i], payload_bytes(size, q8));
+      }
+      continue;
+    }
+    ++st.claimed;
+    if (st.sc.h_flags[i] & kTierHbm) {
+      st.gpu_used += payload_bytes(size, (st.sc.h_flags[i] & kFlagQ8) != 0);
+    } else {
+      bool q8 = (st.sc.h_flags[i] & kFlagQ8) != 0;
+      st.shm_used += dram_accounted(size, q8);
+      ++st.shm_puts;
+    }
+  }
+}
+
+
 // ----------------------------------------------------------------- put
 // Core of every put: the inputs (device addresses, sizes, sequence numbers,
 // keys or digests) are already in st.sc on the device.
@@ -334,7 +377,8 @@ int grow_index(Store &st);
 //   h_prefix: per-block is_prefix or null.
 // On return st.sc.h_status holds the final per-block status.
 static int put_placed(Store &st, size_t n, bool use_digests,
-                      const uint8_t *h_prefix, uint64_t max_size) {
+                      const uint8_t *h_prefix, uint64_t max_size,
+                      bool allow_hbm) {
   cudaStream_t s = st.s;
   const uint64_t *keys = use_digests
                              ? reinterpret_cast<const uint64_t *>(st.sc.digests)
@@ -377,7 +421,8 @@ static int put_placed(Store &st, size_t n, bool use_digests,
     st.sc.h_flags[i] = prefix;
     if (st.sc.h_status[i] != CASCADE_PUT_STORED) continue;
     const bool hq8 = st.hbm && q8_eligible(st, size, false);
-    if (st.hbm && hbm_proj + payload_bytes(size, hq8) <= st.pool_cap) {
+    if (allow_hbm && st.hbm &&
+        hbm_proj + payload_bytes(size, hq8) <= st.pool_cap) {
       const bool q8 = hq8;
       st.sc.h_req[i] = payload_bytes(size, q8);
       st.sc.h_flags[i] |= kTierHbm | (q8 ? kFlagQ8 : 0);
@@ -479,57 +524,42 @@ static int put_placed(Store &st, size_t n, bool use_digests,
   CB_CUDA(cudaMemcpyAsync(st.sc.h_off, st.sc.off, n * 8,
                           cudaMemcpyDeviceToHost, s));
   CB_CUDA(cudaStreamSynchronize(s));
-
-  // Statistics and tier accounting, per CascadeStore::put.
-  for (size_t i = 0; i < n; ++i) {
-    const uint8_t r = st.sc.h_status[i];
-    const uint64_t size = st.sc.h_sizes[i];
-    const bool hit = (r == CASCADE_PUT_DUP_KNOWN || r == CASCADE_PUT_DUP_BATCH);
-    if (hit && st.cfg.dedup_enabled) ++st.dedup_hits;
-    // With dedup off a repeated id reaches the tier, whose put answers true
-    // for an id it holds; the reference counts that as an SHM put when the
-    // DRAM tier is the only tier (cascade_core.cpp:1108-1111).
-    if (hit && !st.cfg.dedup_enabled && !st.hbm) ++st.shm_puts;
-    // The reference compresses every block that passes the dedup check,
-    // whatever tier then takes it (cascade_core.cpp:1086-1092).
-    if (st.cfg.kv_compression && size >= 64 && !(hit && st.cfg.dedup_enabled))
-      st.compression_savings += size - (8 + size / 2);
-    if (r != CASCADE_PUT_STORED) {
-      // A DRAM placement that did not become live gives its space back.
-      if ((st.sc.h_flags[i] & kTierDram) && st.sc.h_off[i] != kInvalidOffset) {
-        bool q8 = (st.sc.h_flags[i] & kFlagQ8) != 0;
-        st.dram->free(st.sc.h_off[i], payload_bytes(size, q8));
-      }
-      continue;
-    }
-    ++st.claimed;
-    if (st.sc.h_flags[i] & kTierHbm) {
-      st.gpu_used += payload_bytes(size, (st.sc.h_flags[i] & kFlagQ8) != 0);
-    } else {
-      bool q8 = (st.sc.h_flags[i] & kFlagQ8) != 0;
-      st.shm_used += dram_accounted(size, q8);
-      ++st.shm_puts;
-    }
-  }
   return CASCADE_OK;
 }
 
-// Uploads the batch description and runs the put.  When h_keys is null the
-// blocks are content-addressed: SHA-256 runs first and its digests are the
-// keys.  h_ptrs are device addresses.
-static int put_batch_locked(Store &st, size_t n, const uint64_t *h_ptrs,
-                            const uint64_t *h_sizes, const uint8_t *h_keys,
-                            const uint8_t *h_prefix, uint8_t *h_status,
-                            uint8_t *h_digests, uint64_t *n_stored) {
+// Hands a finished batch's statuses (and digests) to the caller.
+static int finish_put(Store &st, size_t n, bool content_addressed,
+                      uint8_t *h_status, uint8_t *h_digests,
+                      uint64_t *n_stored) {
+  if (h_digests && content_addressed) {
+    CB_CUDA(cudaMemcpyAsync(st.sc.h_digests, st.sc.digests, 32 * n,
+                            cudaMemcpyDeviceToHost, st.s));
+    CB_CUDA(cudaStreamSynchronize(st.s));
+    std::memcpy(h_digests, st.sc.h_digests, 32 * n);
+  }
+  uint64_t ok = 0;
+  for (size_t i = 0; i < n; ++i) {
+    if (st.sc.h_status[i] != CASCADE_PUT_FAILED) ++ok;
+    if (h_status) h_status[i] = st.sc.h_status[i];
+  }
+  if (n_stored) *n_stored = ok;
+  return CASCADE_OK;
+}
+
+// Copies the batch description into the scratch arrays and to the device
+// (main stream): addresses, sizes, sequence numbers and, when given, keys.
+static int upload_batch(Store &st, size_t n, const uint64_t *h_ptrs,
+                        const uint64_t *h_sizes, const uint8_t *h_keys,
+                        uint64_t *max_size) {
   int rc = ensure_scratch(st, n);
   if (rc) return rc;
   cudaStream_t s = st.s;
-  uint64_t max_size = 0;
+  uint64_t mx = 0;
   for (size_t i = 0; i < n; ++i) {
     st.sc.h_ptrs[i] = h_ptrs[i];
     st.sc.h_sizes[i] = h_sizes[i];
     st.sc.h_seqs[i] = st.next_seq + i;
-    max_size = std::max(max_size, h_sizes[i]);
+    mx = std::max(mx, h_sizes[i]);
     if (h_keys) {
       uint64_t k0 = le64(h_keys + 16 * i), k1 = le64(h_keys + 16 * i + 8);
       CB_CHECK(!(k0 == kKeyMask0 && k1 == kKeyMask1), CASCADE_ERR_INVALID,
@@ -542,27 +572,214 @@ static int put_batch_locked(Store &st, size_t n, const uint64_t *h_ptrs,
   CB_CUDA(cudaMemcpyAsync(st.sc.ptrs, st.sc.h_ptrs, n * 8, cudaMemcpyHostToDevice, s));
   CB_CUDA(cudaMemcpyAsync(st.sc.sizes, st.sc.h_sizes, n * 8, cudaMemcpyHostToDevice, s));
   CB_CUDA(cudaMemcpyAsync(st.sc.seqs, st.sc.h_seqs, n * 8, cudaMemcpyHostToDevice, s));
-  if (h_keys) {
+  if (h_keys)
     CB_CUDA(cudaMemcpyAsync(st.sc.keys, st.sc.h_keys, n * 16, cudaMemcpyHostToDevice, s));
-  } else {
-    rc = launch_sha256(st.sc.ptrs, st.sc.sizes, (int)n, st.sc.digests, s);
+  *max_size = mx;
+  return CASCADE_OK;
+}
+
+// True when every block of a content-addressed batch can be given an HBM
+// slot before its digest is known (the HBM tier takes all of them even if
+// none is a duplicate).
+static bool can_speculate(const Store &st, size_t n) {
+  if (!st.hbm) return false;
+  uint64_t need = 0;
+  for (size_t i = 0; i < n; ++i) {
+    const uint64_t size = st.sc.h_sizes[i];
+    need += payload_bytes(size, q8_eligible(st, size, false));
+  }
+  return st.gpu_used + need <= st.pool_cap;
+}
+
+// Content-addressed put with the hash off the critical path: every block
+// gets an HBM slot and its payload (INT8 codes or a copy) on the main
+// stream while SHA-256 runs on the hash stream; when the digests are in,
+// the index decides winners and the slots of duplicates are freed.  The
+// result is the same as hashing first (the index sees the same keys in the
+// same sequence order); only the order of device work differs.
+// `digests_ready`: the caller already hashed on s2 and recorded ev2.
+static int put_speculative(Store &st, size_t n, const uint8_t *h_prefix,
+                           uint64_t max_size, bool digests_ready) {
+  cudaStream_t s = st.s;
+  bool any_q8 = false, any_raw = false;
+  for (size_t i = 0; i < n; ++i) {
+    const uint64_t size = st.sc.h_sizes[i];
+    const bool q8 = q8_eligible(st, size, false);
+    st.sc.h_req[i] = payload_bytes(size, q8);
+    st.sc.h_off[i] = kInvalidOffset;
+    st.sc.h_dst[i] = 0;
+    st.sc.h_flags[i] = kTierHbm | (q8 ? kFlagQ8 : 0) |
+                       ((h_prefix && h_prefix[i] && st.cfg.dedup_enabled)
+                            ? kFlagPrefix : 0);
+    any_q8 |= q8;
+    any_raw |= !q8;
+    int rc = ensure_stack(st, size_class(std::max<uint64_t>(st.sc.h_req[i], 1)));
     if (rc) return rc;
   }
-  rc = put_placed(st, n, h_keys == nullptr, h_prefix, max_size);
+  if (st.claimed + n > st.nslots / 2) {
+    int rc = grow_index(st);
+    if (rc) return rc;
+  }
+  CB_CUDA(cudaMemcpyAsync(st.sc.req, st.sc.h_req, n * 8, cudaMemcpyHostToDevice, s));
+  CB_CUDA(cudaMemcpyAsync(st.sc.hoff, st.sc.h_off, n * 8, cudaMemcpyHostToDevice, s));
+  CB_CUDA(cudaMemcpyAsync(st.sc.hdst, st.sc.h_dst, n * 8, cudaMemcpyHostToDevice, s));
+  CB_CUDA(cudaMemcpyAsync(st.sc.flags, st.sc.h_flags, n * 4, cudaMemcpyHostToDevice, s));
+  int rc;
+  if (!digests_ready) {  // hash on s2 as soon as the descriptors are there
+    CB_CUDA(cudaEventRecord(st.ev, s));
+    CB_CUDA(cudaStreamWaitEvent(st.s2, st.ev, 0));
+    rc = launch_sha256(st.sc.ptrs, st.sc.sizes, (int)n, st.sc.digests, st.s2);
+    if (rc) return rc;
+    CB_CUDA(cudaEventRecord(st.ev2, st.s2));
+  }
+  rc = launch_pool_alloc(st.d_pool, st.sc.req, (int)n, st.sc.off, s);
   if (rc) return rc;
-  if (h_digests && !h_keys) {
+  const int nb = (int)((n + 255) / 256);
+  prepare_kernel<<<nb, 256, 0, s>>>((int)n, st.sc.req, st.sc.off, st.sc.hoff,
+                                    st.sc.hdst, st.sc.flags, st.sc.sizes,
+                                    (uint64_t)(uintptr_t)st.pool, st.sc.dst,
+                                    st.sc.eff_raw, st.sc.eff_q8);
+  count_launches(1);
+  CB_CUDA(cudaGetLastError());
+  if (any_q8) {
+    rc = launch_minmax(st.sc.ptrs, st.sc.eff_q8, (int)n, max_size, st.sc.mnmx, s);
+    if (!rc) rc = launch_quantize(st.sc.ptrs, st.sc.eff_q8, (int)n, max_size,
+                                  st.sc.mnmx, st.sc.dst, st.sc.hdr, 0, s);
+  }
+  if (!rc && any_raw)
+    rc = launch_copy(st.sc.ptrs, st.sc.dst, st.sc.eff_raw, (int)n, max_size, s);
+  if (rc) return rc;
+  // The digests decide who stores.
+  CB_CUDA(cudaStreamWaitEvent(s, st.ev2, 0));
+  CB_CUDA(cudaMemsetAsync(st.sc.err, 0, sizeof(int), s));
+  const uint64_t *keys = reinterpret_cast<const uint64_t *>(st.sc.digests);
+  const uint64_t epoch = st.next_epoch;
+  st.next_epoch += n;
+  rc = launch_index_claim(st.slots, st.nslots - 1, keys, 4, st.sc.seqs, (int)n,
+                          st.sc.slot, st.sc.err, s);
+  if (!rc) rc = launch_index_resolve(st.slots, st.sc.slot, st.sc.seqs, (int)n,
+                                     st.sc.status, s);
+  if (!rc) rc = launch_index_commit(st.slots, st.sc.slot, st.sc.status,
+                                    st.sc.off, st.sc.sizes, st.sc.flags,
+                                    st.sc.hdr, epoch, (int)n, s);
+  if (!rc) rc = launch_index_finalize(st.slots, st.sc.slot, st.sc.off,
+                                      st.sc.status, (int)n, s);
+  if (!rc) rc = launch_pool_free_unstored(st.d_pool, st.sc.req, st.sc.off,
+                                          st.sc.status, (int)n, s);
+  if (rc) return rc;
+  CB_CUDA(cudaMemcpyAsync(st.sc.h_status, st.sc.status, n,
+                          cudaMemcpyDeviceToHost, s));
+  CB_CUDA(cudaMemcpyAsync(st.sc.h_off, st.sc.off, n * 8,
+                          cudaMemcpyDeviceToHost, s));
+  CB_CUDA(cudaMemcpyAsync(st.sc.h_err, st.sc.err, sizeof(int),
+                          cudaMemcpyDeviceToHost, s));
+  CB_CUDA(cudaStreamSynchronize(s));
+  return check_device_err(st);
+}
+
+// Runs a put batch whose description upload_batch() has placed on the
+// device, then accounts for it.
+//   mode 0: content-addressed with HBM room for every block: speculative
+//           (the hash overlaps the payload work);
+//   mode 1: tiered placement (HBM while it has room, then DRAM);
+//   mode 2: tiered placement without HBM.
+// Blocks whose HBM slot could not be allocated (the size classes are
+// fuller than the byte count says) are placed again by the next mode, as
+// the reference falls back to the SHM tier when the GPU put fails
+// (cascade_core.cpp:1097-1118).  On return sc.h_status holds the final
+// per-block status.
+static int put_uploaded(Store &st, size_t n, bool content_addressed,
+                        const uint8_t *h_prefix, uint64_t max_size,
+                        bool digests_ready, int mode = -1) {
+  int rc;
+  if (mode < 0) mode = (content_addressed && can_speculate(st, n)) ? 0 : 1;
+  if (mode == 0) {
+    if ((rc = put_speculative(st, n, h_prefix, max_size, digests_ready)))
+      return rc;
+  } else {
+    if (content_addressed) {
+      if (digests_ready) {
+        CB_CUDA(cudaStreamWaitEvent(st.s, st.ev2, 0));
+      } else {
+        rc = launch_sha256(st.sc.ptrs, st.sc.sizes, (int)n, st.sc.digests, st.s);
+        if (rc) return rc;
+      }
+    }
+    if ((rc = put_placed(st, n, content_addressed, h_prefix, max_size,
+                         mode == 1)))
+      return rc;
+  }
+  // A failed HBM allocation sends every failed block of the batch to the
+  // next mode, duplicates of a failed block included (they follow it).
+  std::vector<size_t> retry;
+  bool hbm_alloc_failed = false;
+  for (size_t i = 0; i < n; ++i)
+    hbm_alloc_failed |= st.sc.h_status[i] == CASCADE_PUT_FAILED &&
+                        (st.sc.h_flags[i] & kTierHbm) &&
+                        st.sc.h_off[i] == kInvalidOffset;
+  const bool can_retry =
+      hbm_alloc_failed && (mode == 0 || (mode == 1 && st.dram_tier));
+  for (size_t i = 0; can_retry && i < n; ++i)
+    if (st.sc.h_status[i] == CASCADE_PUT_FAILED) retry.push_back(i);
+  if (retry.empty()) {
+    tally_put(st, n);
+    return CASCADE_OK;
+  }
+  // Keys of the blocks to place again: digest bytes 0..15 or the given keys.
+  std::vector<uint8_t> keys;
+  if (content_addressed) {
     CB_CUDA(cudaMemcpyAsync(st.sc.h_digests, st.sc.digests, 32 * n,
-                            cudaMemcpyDeviceToHost, s));
-    CB_CUDA(cudaStreamSynchronize(s));
-    std::memcpy(h_digests, st.sc.h_digests, 32 * n);
+                            cudaMemcpyDeviceToHost, st.s));
+    CB_CUDA(cudaStreamSynchronize(st.s));
   }
-  uint64_t ok = 0;
-  for (size_t i = 0; i < n; ++i) {
-    if (st.sc.h_status[i] != CASCADE_PUT_FAILED) ++ok;
-    if (h_status) h_status[i] = st.sc.h_status[i];
+  std::vector<uint64_t> ptrs, sizes;
+  std::vector<uint8_t> pre;
+  for (size_t i : retry) {
+    uint8_t k[16];
+    if (content_addressed) {
+      std::memcpy(k, st.sc.h_digests + 32 * i, 16);
+    } else {
+      for (int b = 0; b < 8; ++b) {
+        k[b] = (uint8_t)(st.sc.h_keys[2 * i] >> (8 * b));
+        k[8 + b] = (uint8_t)(st.sc.h_keys[2 * i + 1] >> (8 * b));
+      }
+    }
+    keys.insert(keys.end(), k, k + 16);
+    ptrs.push_back(st.sc.h_ptrs[i]);
+    sizes.push_back(st.sc.h_sizes[i]);
+    pre.push_back(h_prefix ? h_prefix[i] : 0);
+    st.sc.h_status[i] = kRetry;
   }
-  if (n_stored) *n_stored = ok;
+  tally_put(st, n);
+  // The sub-batch overwrites the scratch arrays; keep this batch's view.
+  std::vector<uint8_t> status(st.sc.h_status, st.sc.h_status + n);
+  std::vector<uint64_t> all_ptrs(st.sc.h_ptrs, st.sc.h_ptrs + n);
+  std::vector<uint64_t> all_sizes(st.sc.h_sizes, st.sc.h_sizes + n);
+  const size_t m = retry.size();
+  uint64_t mx = 0;
+  if ((rc = upload_batch(st, m, ptrs.data(), sizes.data(), keys.data(), &mx)))
+    return rc;
+  if ((rc = put_uploaded(st, m, false, pre.data(), mx, false, mode + 1)))
+    return rc;
+  for (size_t k = 0; k < m; ++k) status[retry[k]] = st.sc.h_status[k];
+  std::memcpy(st.sc.h_status, status.data(), n);
+  std::memcpy(st.sc.h_ptrs, all_ptrs.data(), 8 * n);
+  std::memcpy(st.sc.h_sizes, all_sizes.data(), 8 * n);
   return CASCADE_OK;
+}
+
+// Uploads the batch description and runs the put.  When h_keys is null the
+// blocks are content-addressed: the SHA-256 digests are the keys.  h_ptrs
+// are device addresses.
+static int put_batch_locked(Store &st, size_t n, const uint64_t *h_ptrs,
+                            const uint64_t *h_sizes, const uint8_t *h_keys,
+                            const uint8_t *h_prefix, uint8_t *h_status,
+                            uint8_t *h_digests, uint64_t *n_stored) {
+  uint64_t max_size = 0;
+  int rc = upload_batch(st, n, h_ptrs, h_sizes, h_keys, &max_size);
+  if (!rc) rc = put_uploaded(st, n, h_keys == nullptr, h_prefix, max_size, false);
+  if (rc) return rc;
+  return finish_put(st, n, h_keys == nullptr, h_status, h_digests, n_stored);
 }
 
 // ----------------------------------------------------------------- get
@@ -880,7 +1097,11 @@ static int create_store(const cascade_config_t *cfg, Store **out) {
   st->dev = cfg->gpu_device_id;
   DeviceGuard g(st->dev);
   CB_CUDA(cudaStreamCreateWithFlags(&st->s, cudaStreamNonBlocking));
+  CB_CUDA(cudaStreamCreateWithFlags(&st->s2, cudaStreamNonBlocking));
+  CB_CUDA(cudaStreamCreateWithFlags(&st->s3, cudaStreamNonBlocking));
   CB_CUDA(cudaEventCreateWithFlags(&st->ev, cudaEventDisableTiming));
+  CB_CUDA(cudaEventCreateWithFlags(&st->ev2, cudaEventDisableTiming));
+  CB_CUDA(cudaEventCreateWithFlags(&st->ev3, cudaEventDisableTiming));
   st->hbm = cfg->use_gpu && cfg->gpu_capacity_bytes > 0;
   st->dram_tier = cfg->shm_capacity_bytes > 0;
   if (st->hbm) {
@@ -917,7 +1138,8 @@ static int create_store(const cascade_config_t *cfg, Store **out) {
 
 static void destroy_store(Store *st) {
   DeviceGuard g(st->dev);
-  if (st->s) cudaStreamSynchronize(st->s);
+  for (cudaStream_t q : {st->s, st->s2, st->s3})
+    if (q) cudaStreamSynchronize(q);
   st->dram.reset();
   for (int c = 0; c < kNumClasses; ++c)
     if (st->stack_ptr[c]) cudaFree(st->stack_ptr[c]);
@@ -929,8 +1151,11 @@ static void destroy_store(Store *st) {
   if (st->d_stage) cudaFree(st->d_stage);
   if (st->h_stage) cudaFreeHost(st->h_stage);
   if (st->d_q8stage) cudaFree(st->d_q8stage);
-  if (st->ev) cudaEventDestroy(st->ev);
-  if (st->s) cudaStreamDestroy(st->s);
+  if (st->sha_state) cudaFree(st->sha_state);
+  for (cudaEvent_t e : {st->ev, st->ev2, st->ev3})
+    if (e) cudaEventDestroy(e);
+  for (cudaStream_t q : {st->s, st->s2, st->s3})
+    if (q) cudaStreamDestroy(q);
   delete st;
 }
 
@@ -1016,20 +1241,91 @@ static int get_host_locked(Store &st, const Key &k, uint8_t *out,
   return CASCADE_OK;
 }
 
-// Host blocks for the batched put: copied into one device staging area
-// (directly when the host memory is pinned), then the device batch path.
+// Host blocks for the batched put.
+//
+// Uniform batches (equal sizes, equally spaced, in pinned memory) stream to
+// the GPU in stripes: stripe k holds bytes [k*B, (k+1)*B) of every block and
+// is one strided copy; as each stripe lands, the hash stream advances every
+// block's SHA-256 over that stripe's chunks (the running states are kept
+// between stripes).  Hashing thus hides under the host-to-device transfer,
+// and when the last stripe lands only its chunks, the INT8 compression and
+// the index work remain.
+//
+// Other batches are copied block by block (directly from pinned memory,
+// through the pinned stage otherwise) and then put like device blocks.
 static int put_batch_host_locked(Store &st, size_t n,
                                  const uint8_t *const *blocks,
                                  const uint64_t *sizes, const uint8_t *keys,
                                  const uint8_t *prefix, uint8_t *status,
                                  uint8_t *digests, uint64_t *n_stored) {
+  const uint64_t S = sizes[0];
+  const intptr_t pitch = n > 1 ? (intptr_t)(blocks[1] - blocks[0]) : (intptr_t)S;
+  bool uniform = keys == nullptr && S > 0 && pitch >= (intptr_t)S;
+  for (size_t i = 0; uniform && i < n; ++i)
+    uniform = sizes[i] == S && blocks[i] == blocks[0] + (intptr_t)i * pitch;
+  if (uniform) {
+    cudaPointerAttributes a0, a1;
+    bool p0 = cudaPointerGetAttributes(&a0, blocks[0]) == cudaSuccess &&
+              a0.type == cudaMemoryTypeHost;
+    cudaGetLastError();
+    bool p1 = cudaPointerGetAttributes(&a1, blocks[n - 1] + S - 1) == cudaSuccess &&
+              a1.type == cudaMemoryTypeHost;
+    cudaGetLastError();
+    uniform = p0 && p1;
+  }
+  int rc;
+  if (uniform) {
+    const uint64_t Pd = (S + 255) & ~uint64_t(255);
+    if ((rc = ensure_device_buf(st.d_stage, st.d_stage_cap, n * Pd, st.s)))
+      return rc;
+    if (n > st.sha_state_cap) {
+      CB_CUDA(cudaStreamSynchronize(st.s2));
+      if (st.sha_state) CB_CUDA(cudaFree(st.sha_state));
+      st.sha_state = nullptr;
+      st.sha_state_cap = 0;
+      CB_CUDA(cudaMalloc(&st.sha_state, n * 32));
+      st.sha_state_cap = n;
+    }
+    std::vector<uint64_t> ptrs(n);
+    for (size_t i = 0; i < n; ++i)
+      ptrs[i] = (uint64_t)(uintptr_t)(st.d_stage + i * Pd);
+    uint64_t max_size = 0;
+    if ((rc = upload_batch(st, n, ptrs.data(), sizes, nullptr, &max_size)))
+      return rc;
+    CB_CUDA(cudaEventRecord(st.ev, st.s));
+    CB_CUDA(cudaStreamWaitEvent(st.s2, st.ev, 0));
+    // ~16 stripes for large blocks, each a whole number of 64-byte chunks.
+    uint64_t K = std::min<uint64_t>(16, (S + 65535) / 65536);
+    if (K < 1) K = 1;
+    const uint64_t B = ((S + K - 1) / K + 63) & ~uint64_t(63);
+    K = (S + B - 1) / B;
+    for (uint64_t k = 0; k < K; ++k) {
+      const uint64_t off = k * B, w = std::min<uint64_t>(B, S - off);
+      CB_CUDA(cudaMemcpy2DAsync(st.d_stage + off, Pd, blocks[0] + off,
+                                (size_t)pitch, w, n, cudaMemcpyHostToDevice,
+                                st.s3));
+      CB_CUDA(cudaEventRecord(st.ev3, st.s3));
+      CB_CUDA(cudaStreamWaitEvent(st.s2, st.ev3, 0));
+      const uint64_t c0 = off / 64;
+      const uint64_t c1 = (k + 1 == K) ? ~0ull : (off + B) / 64;
+      rc = launch_sha256_range(st.sc.ptrs, st.sc.sizes, (int)n, st.sc.digests,
+                               st.sha_state, c0, c1, st.s2);
+      if (rc) return rc;
+    }
+    CB_CUDA(cudaEventRecord(st.ev2, st.s2));
+    CB_CUDA(cudaStreamWaitEvent(st.s, st.ev3, 0));  // every stripe is in
+    rc = put_uploaded(st, n, true, prefix, max_size, true);
+    if (rc) return rc;
+    return finish_put(st, n, true, status, digests, n_stored);
+  }
+
   uint64_t total = 0;
   std::vector<uint64_t> offs(n);
   for (size_t i = 0; i < n; ++i) {
     offs[i] = total;
     total += (sizes[i] + 255) & ~uint64_t(255);
   }
-  int rc = ensure_device_buf(st.d_stage, st.d_stage_cap, total, st.s);
+  rc = ensure_device_buf(st.d_stage, st.d_stage_cap, total, st.s);
   if (rc) return rc;
   size_t pinned_need = 0;
   std::vector<uint8_t> pinned(n);

@@ -188,10 +188,11 @@ int launch_index_scan(const Slot *slots, uint64_t nslots, uint32_t tier_flag,
 // the allocation, or kInvalidOffset (no request, or the pool is full).
 int launch_pool_alloc(PoolDev *pool, const uint64_t *req, int n,
                       uint64_t *offsets, cudaStream_t s);
-// Returns offsets[i] (allocated for req[i] bytes) to the free stacks where
-// release[i] is non-zero.
-int launch_pool_free(PoolDev *pool, const uint64_t *req,
-                     const uint64_t *offsets, const uint8_t *release, int n,
-                     cudaStream_t s);
+// Returns offsets[i] (allocated for req[i] bytes) to the free stacks for
+// every request whose status is not CASCADE_PUT_STORED (speculative
+// allocations of blocks that turned out to be duplicates).
+int launch_pool_free_unstored(PoolDev *pool, const uint64_t *req,
+                              const uint64_t *offsets, const uint8_t *status,
+                              int n, cudaStream_t s);
 
 }  // namespace cb

@@ -213,9 +213,9 @@ __global__ void pool_alloc_finish_kernel(PoolDev *pool) {
 
 __global__ void pool_free_kernel(PoolDev *pool, const uint64_t *__restrict__ req,
                                  const uint64_t *__restrict__ offsets,
-                                 const uint8_t *__restrict__ release, int n) {
+                                 const uint8_t *__restrict__ status, int n) {
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= n || !release[i]) return;
+  if (i >= n || status[i] == CASCADE_PUT_STORED) return;
   const uint64_t off = offsets[i];
   if (off == kInvalidOffset || req[i] == kNoRequest) return;
   const int c = size_class(req[i]);
@@ -325,11 +325,11 @@ int launch_pool_alloc(PoolDev *pool, const uint64_t *req, int n,
   return CASCADE_OK;
 }
 
-int launch_pool_free(PoolDev *pool, const uint64_t *req,
-                     const uint64_t *offsets, const uint8_t *release, int n,
-                     cudaStream_t s) {
+int launch_pool_free_unstored(PoolDev *pool, const uint64_t *req,
+                              const uint64_t *offsets, const uint8_t *status,
+                              int n, cudaStream_t s) {
   if (n <= 0) return CASCADE_OK;
-  pool_free_kernel<<<blocks_for(n), 256, 0, s>>>(pool, req, offsets, release,
+  pool_free_kernel<<<blocks_for(n), 256, 0, s>>>(pool, req, offsets, status,
                                                  n);
   count_launches(1);
   CB_CUDA(cudaGetLastError());

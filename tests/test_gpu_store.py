@@ -263,3 +263,56 @@ def test_cuda_tensor_put_get_by_name():
     out = torch.zeros(4096, device=DEV, dtype=torch.int16)
     assert st.get("tensor_block", out) == (True, 8192)
     assert torch.equal(out, t)
+
+
+@pytest.mark.parametrize("size", [1000, 65536 + 100, (2 << 20) + 100])
+def test_host_batch_striped_uniform_pinned(size):
+    """Equal-size blocks in one pinned array stream to the GPU in stripes
+    while SHA-256 advances stripe by stripe; the result must equal hashing
+    whole blocks (OpenSSL) and store the same bytes."""
+    n = 24
+    rng = np.random.default_rng(size)
+    host = torch.from_numpy(rng.integers(0, 256, (n, size), dtype=np.uint8)).pin_memory()
+    rows = [host.numpy()[i] for i in range(n)]
+    rows[5] = rows[2]                       # a duplicate inside the batch
+    host.numpy()[5] = host.numpy()[2]
+    st = make_store(use_gpu=True, gpu_cap=256 << 20)
+    stored, status, digests = st.put_batch_host(rows, return_status=True)
+    assert stored == n
+    assert status[5] == 2 and (np.delete(status, 5) == 0).all()
+    for i in range(n):
+        assert digests[i].tobytes() == hashlib.sha256(rows[i].tobytes()).digest()
+    buf = np.zeros(size, np.uint8)
+    for i in (0, 5, n - 1):
+        assert st.get(digests[i][:16].tobytes().hex(), buf) == (True, size)
+        assert np.array_equal(buf, rows[i])
+    assert st.get_stats().dedup_hits == 1
+
+
+@pytest.mark.parametrize("with_dram", [False, True])
+def test_hbm_allocation_failure_falls_back(with_dram):
+    """4097-byte blocks use 4608-byte pool classes: a pool sized by byte
+    count cannot hold all of them.  The blocks that get no HBM slot go to the
+    DRAM tier (as the reference falls back to SHM), or fail without one."""
+    n = 16
+    rng = np.random.default_rng(4)
+    blocks = torch.from_numpy(rng.integers(0, 256, (n, 4097), dtype=np.uint8)).to(DEV)
+    st = make_store(use_gpu=True, gpu_cap=n * 4097 + 100,
+                    shm_cap=(1 << 20) if with_dram else 0)
+    stored, status, digests = st.put_batch(blocks, return_status=True)
+    in_hbm = (n * 4097 + 100) // 4608
+    s = st.get_stats()
+    assert s.gpu_used == in_hbm * 4097
+    if with_dram:
+        assert stored == n and (status == 0).all()
+        assert s.shm_used == (n - in_hbm) * 4097 and s.shm_puts == n - in_hbm
+    else:
+        assert stored == in_hbm
+        assert (status == 0).sum() == in_hbm and (status == 3).sum() == n - in_hbm
+    buf = np.zeros(4097, np.uint8)
+    host = blocks.cpu().numpy()
+    for i in range(n):
+        found, size = st.get(digests[i][:16].tobytes().hex(), buf)
+        assert found == (status[i] == 0)
+        if found:
+            assert np.array_equal(buf, host[i])
