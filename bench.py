@@ -228,14 +228,28 @@ def main_ours(args):
     cfg.kv_compression = True
     cfg.gpu_q8 = True
     cfg.index_slots = 1 << 15
-    store = cc.CascadeStore(cfg)
     ptrs = np.arange(n, dtype=np.uint64) * np.uint64(bb) + np.uint64(blocks.data_ptr())
     sizes = np.full(n, bb, np.uint64)
     stream = torch.cuda.current_stream(dev).cuda_stream
+    if world > 1:
+        # the dedup index is sharded over the ranks (NCCL all-to-all)
+        from cascade_b200.sharded import ShardedCascadeStore
+        sharded = ShardedCascadeStore(cfg)
+        store = sharded.store
 
-    def step():
-        store.clear()
-        return store._put_batch_raw(n, ptrs, sizes, None, None, False, stream)
+        def put_rows(rows):
+            return sharded.put_batch(rows)
+
+        def step():
+            sharded.clear()
+            return put_rows(blocks)
+    else:
+        store = cc.CascadeStore(cfg)
+
+        def step():
+            store.clear()
+            return store._put_batch_raw(n, ptrs, sizes, None, None, False,
+                                        stream)
 
     for _ in range(args.warmup):
         assert step() == n
@@ -305,10 +319,17 @@ def main_ours(args):
     host_np = host.numpy()
     rows = [host_np[i] for i in range(n)]
     e2e_steps = max(1, min(args.e2e_steps, args.steps))
+    if world > 1:
+        staging = torch.empty((n, bb), dtype=torch.uint8, device=dev)
 
-    def e2e_step():
-        store.clear()
-        return store.put_batch_host(rows)
+        def e2e_step():
+            sharded.clear()
+            staging.copy_(host, non_blocking=True)
+            return sharded.put_batch(staging)
+    else:
+        def e2e_step():
+            store.clear()
+            return store.put_batch_host(rows)
 
     e2e_step()
     torch.cuda.synchronize()
@@ -324,7 +345,7 @@ def main_ours(args):
     e2e_value = world * e2e_steps * total / e2e_s / 1e9
 
     cpu = None
-    if rank == 0 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
         sample = host_np[:SAMPLE_BLOCKS].copy()
         try:
             res = cpu_reference(sample, os.cpu_count() or 1, CPU_MIN_SECONDS)
@@ -375,8 +396,12 @@ def main_ours(args):
         "cpu_baseline": cpu,
         "e2e": {"value": e2e_value, "unit": UNIT,
                 "h2d_bytes_per_step": total, "d2h_bytes_per_step": n * 33,
-                "steps": e2e_steps, "api": "CascadeStore.put_batch_host "
-                                           "(pinned host blocks)"},
+                "steps": e2e_steps,
+                "api": ("CascadeStore.put_batch_host (pinned host blocks, "
+                        "striped H2D with hashing under the copy)")
+                if world == 1 else
+                ("pinned host -> HBM copy + ShardedCascadeStore.put_batch "
+                 "per rank")},
         "gpu_launches": int(launches),
         "clocks": clk.summary(),
     }

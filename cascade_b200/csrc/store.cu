@@ -127,6 +127,11 @@ struct Store {
   uint64_t claimed = 0;  // keys that own a slot (upper bound)
   std::unique_ptr<DramArena> dram;
   Scratch sc;
+  Scratch oc;                  // owner-side records of a sharded batch
+  uint8_t *shard_aux = nullptr;  // staged records + per-owner counters
+  size_t oc_aux_cap = 0;
+  int shard_rank = 0;            // this store's rank in the open batch
+  size_t shard_open = 0;         // blocks of the open sharded batch
   uint8_t *d_stage = nullptr;  // device staging for host buffers
   size_t d_stage_cap = 0;
   uint8_t *h_stage = nullptr;  // pinned staging for host buffers
@@ -199,21 +204,23 @@ void carve_all(Scratch &S, uint8_t *base, bool host) {
   }
 }
 
-int ensure_scratch(Store &st, size_t n) {
-  if (n <= st.sc.cap) return CASCADE_OK;
-  size_t cap = std::max<size_t>(n, std::max<size_t>(1024, 2 * st.sc.cap));
+int ensure_scratch_of(Store &st, Scratch &sc, size_t n) {
+  if (n <= sc.cap) return CASCADE_OK;
+  size_t cap = std::max<size_t>(n, std::max<size_t>(1024, 2 * sc.cap));
   CB_CUDA(cudaStreamSynchronize(st.s));
-  if (st.sc.dblob) cudaFree(st.sc.dblob);
-  if (st.sc.hblob) cudaFreeHost(st.sc.hblob);
-  st.sc = Scratch();
+  if (sc.dblob) cudaFree(sc.dblob);
+  if (sc.hblob) cudaFreeHost(sc.hblob);
+  sc = Scratch();
   size_t bytes = scratch_bytes(cap);
-  CB_CUDA(cudaMalloc(&st.sc.dblob, bytes));
-  CB_CUDA(cudaHostAlloc(&st.sc.hblob, bytes, cudaHostAllocDefault));
-  st.sc.cap = cap;
-  carve_all(st.sc, st.sc.dblob, false);
-  carve_all(st.sc, st.sc.hblob, true);
+  CB_CUDA(cudaMalloc(&sc.dblob, bytes));
+  CB_CUDA(cudaHostAlloc(&sc.hblob, bytes, cudaHostAllocDefault));
+  sc.cap = cap;
+  carve_all(sc, sc.dblob, false);
+  carve_all(sc, sc.hblob, true);
   return CASCADE_OK;
 }
+
+int ensure_scratch(Store &st, size_t n) { return ensure_scratch_of(st, st.sc, n); }
 
 int ensure_device_buf(uint8_t *&buf, size_t &cap, size_t need,
                       cudaStream_t s) {
@@ -598,7 +605,10 @@ static bool can_speculate(const Store &st, size_t n) {
 // result is the same as hashing first (the index sees the same keys in the
 // same sequence order); only the order of device work differs.
 // `digests_ready`: the caller already hashed on s2 and recorded ev2.
-static int put_speculative(Store &st, size_t n, const uint8_t *h_prefix,
+// First half of the speculative put: plan every block into HBM, start the
+// hash on s2 (unless the caller did, `digests_ready`), allocate the slots
+// and write the payloads on the main stream.  ev2 marks the digests.
+static int speculate_local(Store &st, size_t n, const uint8_t *h_prefix,
                            uint64_t max_size, bool digests_ready) {
   cudaStream_t s = st.s;
   bool any_q8 = false, any_raw = false;
@@ -648,6 +658,13 @@ static int put_speculative(Store &st, size_t n, const uint8_t *h_prefix,
   }
   if (!rc && any_raw)
     rc = launch_copy(st.sc.ptrs, st.sc.dst, st.sc.eff_raw, (int)n, max_size, s);
+  return rc;
+}
+
+static int put_speculative(Store &st, size_t n, const uint8_t *h_prefix,
+                           uint64_t max_size, bool digests_ready) {
+  cudaStream_t s = st.s;
+  int rc = speculate_local(st, n, h_prefix, max_size, digests_ready);
   if (rc) return rc;
   // The digests decide who stores.
   CB_CUDA(cudaStreamWaitEvent(s, st.ev2, 0));
@@ -1006,6 +1023,11 @@ static int get_batch_locked(Store &st, size_t n, const uint8_t *h_keys,
   std::vector<uint8_t> deliver(n);
   std::vector<uint64_t> out(h_out, h_out + n);
   uint64_t found = 0;
+  for (size_t i = 0; i < n; ++i)
+    CB_CHECK(!(st.sc.h_info[i].found && (st.sc.h_info[i].flags & kFlagRemote)),
+             CASCADE_ERR_UNSUPPORTED,
+             "block is held by another rank of a sharded store: read it on "
+             "its holder");
   for (size_t i = 0; i < n; ++i) {
     const LookupInfo &f = st.sc.h_info[i];
     uint64_t size = f.found ? ((f.flags & kFlagQ8) ? 2 * (f.size / 2) : f.size) : 0;
@@ -1146,8 +1168,11 @@ static void destroy_store(Store *st) {
   if (st->pool) cudaFree(st->pool);
   if (st->d_pool) cudaFree(st->d_pool);
   if (st->slots) cudaFree(st->slots);
-  if (st->sc.dblob) cudaFree(st->sc.dblob);
-  if (st->sc.hblob) cudaFreeHost(st->sc.hblob);
+  for (Scratch *sc : {&st->sc, &st->oc}) {
+    if (sc->dblob) cudaFree(sc->dblob);
+    if (sc->hblob) cudaFreeHost(sc->hblob);
+  }
+  if (st->shard_aux) cudaFree(st->shard_aux);
   if (st->d_stage) cudaFree(st->d_stage);
   if (st->h_stage) cudaFreeHost(st->h_stage);
   if (st->d_q8stage) cudaFree(st->d_q8stage);
@@ -1215,6 +1240,9 @@ static int get_host_locked(Store &st, const Key &k, uint8_t *out,
     *size = 0;
     return CASCADE_OK;
   }
+  CB_CHECK(!(f.flags & kFlagRemote), CASCADE_ERR_UNSUPPORTED,
+           "block is held by another rank of a sharded store: read it on its "
+           "holder");
   const uint64_t bytes = (f.flags & kFlagQ8) ? 2 * (f.size / 2) : f.size;
   *found = 1;
   *size = bytes;
@@ -1353,6 +1381,230 @@ static int put_batch_host_locked(Store &st, size_t n,
   }
   return put_batch_locked(st, n, ptrs.data(), sizes, keys, prefix, status,
                           digests, n_stored);
+}
+
+// ------------------------------------------------------- sharded dedup
+namespace {
+
+__global__ void shard_records_kernel(int n, int world, uint32_t rank,
+                                     uint64_t seq_base,
+                                     const uint64_t *__restrict__ digests,
+                                     const uint64_t *__restrict__ off,
+                                     const uint64_t *__restrict__ sizes,
+                                     const uint32_t *__restrict__ flags,
+                                     const uint8_t *__restrict__ hdr,
+                                     ShardRecord *__restrict__ tmp,
+                                     int *__restrict__ owner,
+                                     uint32_t *__restrict__ counts) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  ShardRecord r;
+  r.k0 = digests[4 * (size_t)i];
+  r.k1 = digests[4 * (size_t)i + 1];
+  r.seq = seq_base + (uint64_t)i;
+  r.offset = off[i];
+  r.size = sizes[i];
+  r.flags = flags[i];
+  r.holder = rank;
+  r.src_idx = (uint32_t)i;
+  const uint8_t *h = hdr + 8 * (size_t)i;
+  r.hdr_scale = (uint32_t)h[0] | ((uint32_t)h[1] << 8) |
+                ((uint32_t)h[2] << 16) | ((uint32_t)h[3] << 24);
+  r.hdr_zp = h[4];
+  r.pad = 0;
+  tmp[i] = r;
+  const int o = owner_of(r.k0, world);
+  owner[i] = o;
+  atomicAdd(&counts[o], 1u);
+}
+
+// Groups the records by owner rank (order inside a group is free: the
+// owner decides by sequence number).
+__global__ void shard_scatter_kernel(int n, int world,
+                                     const ShardRecord *__restrict__ tmp,
+                                     const int *__restrict__ owner,
+                                     const uint32_t *__restrict__ counts,
+                                     uint32_t *__restrict__ cursor,
+                                     ShardRecord *__restrict__ out) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const int o = owner[i];
+  uint32_t base = 0;
+  for (int j = 0; j < o; ++j) base += counts[j];
+  out[base + atomicAdd(&cursor[o], 1u)] = tmp[i];
+}
+
+__global__ void shard_unpack_kernel(int m, uint32_t rank,
+                                    const ShardRecord *__restrict__ in,
+                                    uint64_t *__restrict__ keys,
+                                    uint64_t *__restrict__ seqs,
+                                    uint64_t *__restrict__ off,
+                                    uint64_t *__restrict__ sizes,
+                                    uint32_t *__restrict__ flags,
+                                    uint8_t *__restrict__ hdr) {
+  const int j = blockIdx.x * blockDim.x + threadIdx.x;
+  if (j >= m) return;
+  const ShardRecord r = in[j];
+  keys[2 * (size_t)j] = r.k0;
+  keys[2 * (size_t)j + 1] = r.k1;
+  seqs[j] = r.seq;
+  off[j] = r.offset;
+  sizes[j] = r.size;
+  flags[j] = (r.flags & 0xffffu) | ((r.holder & 0xffu) << 16) |
+             (r.holder != rank ? (uint32_t)kFlagRemote : 0u);
+  uint8_t *h = hdr + 8 * (size_t)j;
+  h[0] = r.hdr_scale & 0xff; h[1] = (r.hdr_scale >> 8) & 0xff;
+  h[2] = (r.hdr_scale >> 16) & 0xff; h[3] = r.hdr_scale >> 24;
+  h[4] = (uint8_t)r.hdr_zp; h[5] = h[6] = h[7] = 0;
+}
+
+__global__ void shard_reply_kernel(int m, const ShardRecord *__restrict__ in,
+                                   const uint8_t *__restrict__ status,
+                                   ShardReply *__restrict__ out) {
+  const int j = blockIdx.x * blockDim.x + threadIdx.x;
+  if (j >= m) return;
+  ShardReply r;
+  r.src_idx = in[j].src_idx;
+  r.status = status[j];
+  out[j] = r;
+}
+
+__global__ void shard_apply_kernel(int m, int n,
+                                   const ShardReply *__restrict__ back,
+                                   uint8_t *__restrict__ status,
+                                   int *__restrict__ err) {
+  const int j = blockIdx.x * blockDim.x + threadIdx.x;
+  if (j >= m) return;
+  const ShardReply r = back[j];
+  if (r.src_idx < (uint32_t)n && r.status <= CASCADE_PUT_FAILED)
+    status[r.src_idx] = (uint8_t)r.status;
+  else
+    atomicExch(err, CASCADE_ERR_INVALID);
+}
+
+inline int nblocks(size_t n) { return (int)((n + 255) / 256); }
+
+}  // namespace
+
+static int shard_begin(Store &st, size_t n, const uint64_t *h_ptrs,
+                       const uint64_t *h_sizes, const uint8_t *h_prefix,
+                       int world, int rank, uint64_t seq_base, uint8_t *d_send,
+                       uint64_t *h_counts) {
+  CB_CHECK(world >= 1 && world <= 256 && rank >= 0 && rank < world,
+           CASCADE_ERR_INVALID, "bad world/rank");
+  CB_CHECK(st.hbm, CASCADE_ERR_UNSUPPORTED,
+           "sharded puts need the HBM tier (use_gpu)");
+  uint64_t max_size = 0;
+  int rc = upload_batch(st, n, h_ptrs, h_sizes, nullptr, &max_size);
+  if (rc) return rc;
+  CB_CHECK(can_speculate(st, n), CASCADE_ERR_NOMEM,
+           "sharded put: the HBM pool cannot hold the whole batch");
+  // per-batch device space: n staged records, n owner ids, 2 x 256 counters
+  const size_t need = n * sizeof(ShardRecord) + n * sizeof(int) + 2048;
+  static_assert(sizeof(ShardRecord) % 16 == 0, "record alignment");
+  if ((rc = ensure_device_buf(st.shard_aux, st.oc_aux_cap, need, st.s))) return rc;
+  ShardRecord *tmp = reinterpret_cast<ShardRecord *>(st.shard_aux);
+  int *owner = reinterpret_cast<int *>(st.shard_aux + n * sizeof(ShardRecord));
+  uint32_t *counts = reinterpret_cast<uint32_t *>(
+      st.shard_aux + n * sizeof(ShardRecord) + ((n * sizeof(int) + 255) & ~size_t(255)));
+  uint32_t *cursor = counts + 256;
+  if ((rc = speculate_local(st, n, h_prefix, max_size, false))) return rc;
+  cudaStream_t s = st.s;
+  CB_CUDA(cudaStreamWaitEvent(s, st.ev2, 0));
+  CB_CUDA(cudaMemsetAsync(counts, 0, 2 * 256 * sizeof(uint32_t), s));
+  shard_records_kernel<<<nblocks(n), 256, 0, s>>>(
+      (int)n, world, (uint32_t)rank, seq_base,
+      reinterpret_cast<const uint64_t *>(st.sc.digests), st.sc.off,
+      st.sc.sizes, st.sc.flags, st.sc.hdr, tmp, owner, counts);
+  count_launches(1);
+  shard_scatter_kernel<<<nblocks(n), 256, 0, s>>>(
+      (int)n, world, tmp, owner, counts, cursor,
+      reinterpret_cast<ShardRecord *>(d_send));
+  count_launches(1);
+  CB_CUDA(cudaGetLastError());
+  uint32_t hc[256];
+  CB_CUDA(cudaMemcpyAsync(hc, counts, world * sizeof(uint32_t),
+                          cudaMemcpyDeviceToHost, s));
+  CB_CUDA(cudaMemcpyAsync(st.sc.h_off, st.sc.off, n * 8,
+                          cudaMemcpyDeviceToHost, s));
+  CB_CUDA(cudaStreamSynchronize(s));
+  for (int r = 0; r < world; ++r) h_counts[r] = hc[r];
+  st.shard_rank = rank;
+  st.shard_open = n;
+  return CASCADE_OK;
+}
+
+static int shard_resolve(Store &st, const uint8_t *d_recv, size_t m,
+                         uint8_t *d_reply) {
+  if (m == 0) return CASCADE_OK;
+  Scratch &oc = st.oc;
+  int rc = ensure_scratch_of(st, oc, m);
+  if (rc) return rc;
+  if (st.claimed + m > st.nslots / 2 && (rc = grow_index(st))) return rc;
+  cudaStream_t s = st.s;
+  const ShardRecord *in = reinterpret_cast<const ShardRecord *>(d_recv);
+  shard_unpack_kernel<<<nblocks(m), 256, 0, s>>>(
+      (int)m, (uint32_t)st.shard_rank, in, oc.keys, oc.seqs, oc.off,
+      oc.sizes, oc.flags, oc.hdr);
+  count_launches(1);
+  CB_CUDA(cudaGetLastError());
+  CB_CUDA(cudaMemsetAsync(oc.err, 0, sizeof(int), s));
+  const uint64_t epoch = st.next_epoch;
+  st.next_epoch += m;
+  rc = launch_index_claim(st.slots, st.nslots - 1, oc.keys, 2, oc.seqs,
+                          (int)m, oc.slot, oc.err, s);
+  if (!rc) rc = launch_index_resolve(st.slots, oc.slot, oc.seqs, (int)m,
+                                     oc.status, s);
+  if (!rc) rc = launch_index_commit(st.slots, oc.slot, oc.status, oc.off,
+                                    oc.sizes, oc.flags, oc.hdr, epoch,
+                                    (int)m, s);
+  if (!rc) rc = launch_index_finalize(st.slots, oc.slot, oc.off, oc.status,
+                                      (int)m, s);
+  if (rc) return rc;
+  shard_reply_kernel<<<nblocks(m), 256, 0, s>>>(
+      (int)m, in, oc.status, reinterpret_cast<ShardReply *>(d_reply));
+  count_launches(1);
+  CB_CUDA(cudaGetLastError());
+  CB_CUDA(cudaMemcpyAsync(oc.h_status, oc.status, m, cudaMemcpyDeviceToHost, s));
+  CB_CUDA(cudaMemcpyAsync(oc.h_err, oc.err, sizeof(int), cudaMemcpyDeviceToHost, s));
+  CB_CUDA(cudaStreamSynchronize(s));
+  if (*oc.h_err) {
+    set_error("device index is full: raise index_slots");
+    return CASCADE_ERR_FULL;
+  }
+  for (size_t j = 0; j < m; ++j) st.claimed += oc.h_status[j] == CASCADE_PUT_STORED;
+  return CASCADE_OK;
+}
+
+static int shard_end(Store &st, const uint8_t *d_back, size_t n,
+                     uint8_t *h_status, uint8_t *h_digests,
+                     uint64_t *n_stored) {
+  CB_CHECK(st.shard_open == n, CASCADE_ERR_INVALID,
+           "shard_put_end: no open batch of this size");
+  cudaStream_t s = st.s;
+  CB_CUDA(cudaMemsetAsync(st.sc.status, CASCADE_PUT_FAILED, n, s));
+  CB_CUDA(cudaMemsetAsync(st.sc.err, 0, sizeof(int), s));
+  shard_apply_kernel<<<nblocks(n), 256, 0, s>>>(
+      (int)n, (int)n, reinterpret_cast<const ShardReply *>(d_back),
+      st.sc.status, st.sc.err);
+  count_launches(1);
+  CB_CUDA(cudaGetLastError());
+  int rc = launch_pool_free_unstored(st.d_pool, st.sc.req, st.sc.off,
+                                     st.sc.status, (int)n, s);
+  if (rc) return rc;
+  CB_CUDA(cudaMemcpyAsync(st.sc.h_status, st.sc.status, n,
+                          cudaMemcpyDeviceToHost, s));
+  CB_CUDA(cudaMemcpyAsync(st.sc.h_err, st.sc.err, sizeof(int),
+                          cudaMemcpyDeviceToHost, s));
+  CB_CUDA(cudaStreamSynchronize(s));
+  st.shard_open = 0;
+  CB_CHECK(*st.sc.h_err == 0, CASCADE_ERR_INVALID,
+           "shard_put_end: a reply names no block of this batch");
+  // Index load is counted by the owners; the rest is this rank's.
+  const uint64_t claimed = st.claimed;
+  tally_put(st, n);
+  st.claimed = claimed;
+  return finish_put(st, n, true, h_status, h_digests, n_stored);
 }
 
 }  // namespace cb
@@ -1565,4 +1817,60 @@ extern "C" int cascade_store_get_batch(cascade_store_t *s, size_t n,
   }
   return cb::get_batch_locked(st, n, h_keys, h_out_ptrs, h_out_caps, h_sizes,
                               h_found, n_found);
+}
+
+extern "C" int cascade_shard_put_begin(cascade_store_t *s, size_t n,
+                                       const uint64_t *h_ptrs,
+                                       const uint64_t *h_sizes,
+                                       const uint8_t *h_prefix, int world,
+                                       int rank, uint64_t seq_base,
+                                       uint8_t *d_send,
+                                       uint64_t *h_send_counts,
+                                       void *stream) {
+  STORE_ENTRY(s);
+  CB_CHECK(h_send_counts && (n == 0 || (h_ptrs && h_sizes && d_send)),
+           CASCADE_ERR_INVALID, "null argument");
+  CB_CHECK(n <= (size_t)INT32_MAX, CASCADE_ERR_INVALID, "batch too large");
+  CB_CHECK(((uintptr_t)d_send & 15u) == 0, CASCADE_ERR_INVALID,
+           "d_send must be 16-byte aligned");
+  if (n == 0) {
+    for (int r = 0; r < world; ++r) h_send_counts[r] = 0;
+    st.shard_rank = rank;
+    st.shard_open = 0;
+    return CASCADE_OK;
+  }
+  if (stream) {
+    CB_CUDA(cudaEventRecord(st.ev, static_cast<cudaStream_t>(stream)));
+    CB_CUDA(cudaStreamWaitEvent(st.s, st.ev, 0));
+  }
+  return cb::shard_begin(st, n, h_ptrs, h_sizes, h_prefix, world, rank,
+                         seq_base, d_send, h_send_counts);
+}
+
+extern "C" int cascade_shard_resolve(cascade_store_t *s, const uint8_t *d_recv,
+                                     size_t m, uint8_t *d_reply, void *stream) {
+  STORE_ENTRY(s);
+  CB_CHECK(m == 0 || (d_recv && d_reply), CASCADE_ERR_INVALID,
+           "null argument");
+  CB_CHECK(m <= (size_t)INT32_MAX, CASCADE_ERR_INVALID, "batch too large");
+  if (stream) {
+    CB_CUDA(cudaEventRecord(st.ev, static_cast<cudaStream_t>(stream)));
+    CB_CUDA(cudaStreamWaitEvent(st.s, st.ev, 0));
+  }
+  return cb::shard_resolve(st, d_recv, m, d_reply);
+}
+
+extern "C" int cascade_shard_put_end(cascade_store_t *s, const uint8_t *d_back,
+                                     size_t n, uint8_t *h_status,
+                                     uint8_t *h_digests, uint64_t *n_stored,
+                                     void *stream) {
+  STORE_ENTRY(s);
+  if (n_stored) *n_stored = 0;
+  if (n == 0) return CASCADE_OK;
+  CB_CHECK(d_back, CASCADE_ERR_INVALID, "null argument");
+  if (stream) {
+    CB_CUDA(cudaEventRecord(st.ev, static_cast<cudaStream_t>(stream)));
+    CB_CUDA(cudaStreamWaitEvent(st.s, st.ev, 0));
+  }
+  return cb::shard_end(st, d_back, n, h_status, h_digests, n_stored);
 }

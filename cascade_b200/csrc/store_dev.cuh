@@ -35,7 +35,37 @@ enum SlotFlags : uint32_t {
   kFlagQ8 = 1u << 1,      // payload is INT8 codes; header in hdr_*
   kTierHbm = 1u << 2,     // payload in the HBM pool
   kTierDram = 1u << 3,    // payload in the pinned DRAM arena
+  kFlagRemote = 1u << 4,  // payload held by another rank (bits 16..23)
 };
+
+// Sharded dedup exchange (one box, one rank per GPU).  A rank sends one
+// record per block of its batch to the rank that owns the block's key;
+// the owner answers with a reply per record.
+struct ShardRecord {
+  uint64_t k0, k1;     // key: digest bytes 0..15, little-endian
+  uint64_t seq;        // global sequence number: the smallest stores
+  uint64_t offset;     // payload offset in the holder's pool (or invalid)
+  uint64_t size;       // logical block size
+  uint32_t flags;      // SlotFlags of the holder's copy
+  uint32_t holder;     // rank whose pool holds the payload
+  uint32_t src_idx;    // position of the block in the holder's batch
+  uint32_t hdr_scale;  // INT8 header
+  uint32_t hdr_zp;
+  uint32_t pad;
+};
+static_assert(sizeof(ShardRecord) == 64, "shard record layout");
+
+struct ShardReply {
+  uint32_t src_idx;
+  uint32_t status;     // CASCADE_PUT_*
+};
+static_assert(sizeof(ShardReply) == 8, "shard reply layout");
+
+// Owner rank of a key among `world` ranks: the top bits of digest byte 0
+// (the low byte of k0), scaled to the rank count.
+__host__ __device__ inline int owner_of(uint64_t k0, int world) {
+  return (int)(((k0 & 0xffu) * (uint64_t)world) >> 8);
+}
 
 struct __align__(16) Slot {
   uint64_t k0, k1;     // stored key (key ^ mask); (0,0) = empty slot

@@ -1,0 +1,180 @@
+"""Content-addressed PUT with the dedup index sharded across the GPUs of one
+box (one process per GPU, torch.distributed for the exchange).
+
+The reference's multi-node store keeps a replicated dedup set per rank and
+reconciles it with MPI_Allgatherv (DistributedStore::put and
+sync_metadata, distributed_backend.cpp:583-590, 1269-1324).  Here every key
+has exactly one owner rank (the top bits of SHA-256 digest byte 0) and a
+batch is exact at once:
+
+1. every rank hashes its blocks and stores them speculatively in its own
+   HBM pool (``cascade_shard_put_begin``), writing one 64-byte record per
+   block, grouped by owner rank;
+2. the records go to their owners in one all-to-all (NCCL on GPUs);
+3. each owner resolves the records it received against its slice of the
+   index (``cascade_shard_resolve``): a key already stored is a dedup hit,
+   and among new keys the smallest global sequence number stores, which is
+   what serial puts in (rank, block) order would do;
+4. the 8-byte replies return in a second all-to-all and each rank frees the
+   slots of its duplicates (``cascade_shard_put_end``).
+
+Block payloads never leave the rank that produced them.  Every rank must
+call ``put_batch`` the same number of times, in the same order.
+"""
+from __future__ import annotations
+
+import ctypes
+import threading
+from typing import Optional, Sequence
+
+import numpy as np
+
+from . import _lib
+from ._lib import check
+from .cascade_cpp import CascadeConfig, CascadeStore, _cuda_u8
+
+RECORD_BYTES = 64
+REPLY_BYTES = 8
+
+_vp = ctypes.c_void_p
+_sz = ctypes.c_size_t
+_u64 = ctypes.c_uint64
+_int = ctypes.c_int
+_lib.register("cascade_shard_put_begin", _int,
+              [_vp, _sz, _vp, _vp, _vp, _int, _int, _u64, _vp, _vp, _vp])
+_lib.register("cascade_shard_resolve", _int, [_vp, _vp, _sz, _vp, _vp])
+_lib.register("cascade_shard_put_end", _int,
+              [_vp, _vp, _sz, _vp, _vp, ctypes.POINTER(_u64), _vp])
+
+
+class CudaShardOps:
+    """The three per-rank steps on this rank's GPU, through the C ABI."""
+
+    def __init__(self, store: CascadeStore):
+        import torch
+        self.store = store
+        self.device = torch.device("cuda", store._device)
+        self._n = 0
+
+    def _stream(self):
+        import torch
+        return torch.cuda.current_stream(self.device).cuda_stream
+
+    def begin(self, blocks, is_prefix, world, rank, seq_base):
+        import torch
+        if isinstance(blocks, torch.Tensor) and blocks.dim() == 2:
+            rows = blocks.contiguous()   # one block per row
+            n = rows.shape[0]
+            stride = rows.stride(0) * rows.element_size()
+            ptrs = (np.arange(n, dtype=np.uint64) * np.uint64(stride)
+                    + np.uint64(rows.data_ptr()))
+            sizes = np.full(n, rows.shape[1] * rows.element_size(), np.uint64)
+            self._keep = rows
+        else:
+            blocks = [_cuda_u8(b) for b in blocks]
+            n = len(blocks)
+            self._keep = blocks
+            ptrs = np.array([b.data_ptr() for b in blocks], dtype=np.uint64)
+            sizes = np.array([b.numel() for b in blocks], dtype=np.uint64)
+        pf = (np.array([1 if p else 0 for p in is_prefix], dtype=np.uint8)
+              if is_prefix is not None else None)
+        send = torch.empty((n, RECORD_BYTES), dtype=torch.uint8,
+                           device=self.device)
+        counts = np.zeros(world, dtype=np.uint64)
+        check(_lib.load().cascade_shard_put_begin(
+            self.store._h, n, ptrs.ctypes.data if n else None,
+            sizes.ctypes.data if n else None,
+            pf.ctypes.data if pf is not None else None, world, rank, seq_base,
+            send.data_ptr() if n else None, counts.ctypes.data,
+            self._stream()))
+        self._n = n
+        return send, [int(c) for c in counts]
+
+    def resolve(self, recv):
+        import torch
+        m = recv.shape[0]
+        reply = torch.empty((m, REPLY_BYTES), dtype=torch.uint8,
+                            device=self.device)
+        check(_lib.load().cascade_shard_resolve(
+            self.store._h, recv.data_ptr() if m else None, m,
+            reply.data_ptr() if m else None, self._stream()))
+        return reply
+
+    def end(self, back):
+        n = self._n
+        status = np.zeros(n, np.uint8)
+        digests = np.zeros((n, 32), np.uint8)
+        stored = _u64(0)
+        check(_lib.load().cascade_shard_put_end(
+            self.store._h, back.data_ptr() if n else None, n,
+            status.ctypes.data if n else None,
+            digests.ctypes.data if n else None, ctypes.byref(stored),
+            self._stream()))
+        self._keep = None
+        return int(stored.value), status, digests
+
+
+class ShardedCascadeStore:
+    """One rank's view of a store whose dedup index is sharded by key over
+    the ranks of ``group``.  ``ops`` defaults to the GPU implementation."""
+
+    def __init__(self, config: Optional[CascadeConfig] = None, group=None,
+                 ops=None):
+        import torch.distributed as dist
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        if ops is None:
+            self.store = CascadeStore(config)
+            ops = CudaShardOps(self.store)
+        self.ops = ops
+        self._next_seq = 1
+        self._lock = threading.Lock()
+
+    def put_batch(self, blocks: Sequence, is_prefix=None,
+                  return_status: bool = False):
+        """Collective: every rank calls it with its own blocks (a list of
+        CUDA tensors, or one 2-D CUDA tensor with a block per row).  Returns
+        the number of this rank's blocks stored or deduplicated (and, with
+        ``return_status``, per-block status codes and 32-byte digests)."""
+        import torch
+        import torch.distributed as dist
+        with self._lock:
+            dev = self.ops.device
+            n = len(blocks)
+            mine = torch.tensor([n], dtype=torch.int64, device=dev)
+            every = [torch.zeros_like(mine) for _ in range(self.world)]
+            dist.all_gather(every, mine, group=self.group)
+            counts = [int(t.item()) for t in every]
+            seq_base = self._next_seq + sum(counts[:self.rank])
+            self._next_seq += sum(counts)
+
+            send, send_splits = self.ops.begin(blocks, is_prefix, self.world,
+                                               self.rank, seq_base)
+            sc = torch.tensor(send_splits, dtype=torch.int64, device=dev)
+            rc = torch.empty(self.world, dtype=torch.int64, device=dev)
+            dist.all_to_all_single(rc, sc, group=self.group)
+            recv_splits = [int(x) for x in rc.tolist()]
+            recv = torch.empty((sum(recv_splits), RECORD_BYTES),
+                               dtype=torch.uint8, device=dev)
+            dist.all_to_all_single(recv, send, recv_splits, send_splits,
+                                   group=self.group)
+            reply = self.ops.resolve(recv)
+            back = torch.empty((n, REPLY_BYTES), dtype=torch.uint8,
+                               device=dev)
+            dist.all_to_all_single(back, reply, send_splits, recv_splits,
+                                   group=self.group)
+            stored, status, digests = self.ops.end(back)
+        if return_status:
+            return stored, status, digests
+        return stored
+
+    def get_stats(self):
+        return self.ops.store.get_stats()
+
+    def clear(self):
+        """Collective: every rank empties its store."""
+        import torch.distributed as dist
+        dist.barrier(group=self.group)
+        self.ops.store.clear()
+        self._next_seq = 1

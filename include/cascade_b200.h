@@ -244,6 +244,37 @@ int cascade_store_get_batch(cascade_store_t *s, size_t n,
                             uint8_t *h_found, void *stream,
                             uint64_t *n_found);
 
+/* ------------------------------------------------------------------ */
+/* Sharded dedup across the GPUs of one box (one rank per GPU).         */
+/* The reference keeps one replicated dedup set per node, synchronised  */
+/* by MPI_Allgatherv (DistributedStore::put / sync_metadata,            */
+/* distributed_backend.cpp:583-590, 1269-1324).  Here each key has one   */
+/* owner rank (the top bits of digest byte 0) and a batch is three      */
+/* calls around two all-to-all exchanges the caller runs (NCCL):         */
+/*   begin:   hash, store every block speculatively in this rank's HBM   */
+/*            pool, and write one 64-byte record per block to d_send,    */
+/*            grouped by owner rank (h_send_counts[r] records for r);    */
+/*   resolve: as owner, decide each received record (the smallest global */
+/*            sequence number of a new key stores; later ones and keys   */
+/*            already stored are dedup hits) and write 8-byte replies;   */
+/*   end:     take the replies for this rank's blocks (in any order),    */
+/*            free the slots of duplicates and report per-block status.  */
+/* A rank must not run other operations on the store between begin and */
+/* end.  Blocks are content-addressed; HBM must hold the whole batch.    */
+#define CASCADE_SHARD_RECORD_BYTES 64
+#define CASCADE_SHARD_REPLY_BYTES 8
+
+int cascade_shard_put_begin(cascade_store_t *s, size_t n,
+                            const uint64_t *h_ptrs, const uint64_t *h_sizes,
+                            const uint8_t *h_prefix, int world, int rank,
+                            uint64_t seq_base, uint8_t *d_send,
+                            uint64_t *h_send_counts, void *stream);
+int cascade_shard_resolve(cascade_store_t *s, const uint8_t *d_recv,
+                          size_t m, uint8_t *d_reply, void *stream);
+int cascade_shard_put_end(cascade_store_t *s, const uint8_t *d_back,
+                          size_t n, uint8_t *h_status, uint8_t *h_digests,
+                          uint64_t *n_stored, void *stream);
+
 #ifdef __cplusplus
 }
 #endif
