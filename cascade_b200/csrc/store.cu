@@ -138,6 +138,10 @@ struct Store {
   size_t h_stage_cap = 0;
   uint8_t *d_q8stage = nullptr;  // INT8 payloads on their way to DRAM
   size_t d_q8stage_cap = 0;
+  uint8_t *d_evstage = nullptr;  // INT8 forms of blocks being demoted
+  size_t d_evstage_cap = 0;
+  uint8_t *scan_d = nullptr;     // live-slot scan for victim choice
+  size_t scan_cap = 0;           // bytes
   std::mutex mu;
   uint64_t next_seq = 1, next_epoch = 1, next_name = 1;
   std::unordered_map<std::string, Key> names;
@@ -377,6 +381,145 @@ static void tally_put(Store &st, size_t n) {
 }
 
 
+// ------------------------------------------------------------- demotion
+// Moves least-recently-used HBM blocks to the DRAM tier until `deficit`
+// bytes of HBM are free (GPUBackend::evict_for_space + evict_lru_semantic,
+// gpu_backend.cu:432-487, and CascadeStore::evict_gpu_to_shm,
+// cascade_core.cpp:998-1018).  Victims are chosen by LRU epoch over the
+// whole pool (the reference takes the LRU tail of its largest shard), with
+// prefix blocks last when semantic_eviction is on.  A demoted block keeps
+// its index slot, which now points into the DRAM arena; blocks go to DRAM in
+// the DRAM tier's format (INT8 when kv_compression applies, compressed on
+// the device here; the reference demotes raw bytes).  Stops early when the
+// DRAM tier is full.  Uses the owner-side scratch, so it can run in the
+// middle of a put whose batch occupies the main scratch.
+static int evict_hbm(Store &st, uint64_t deficit) {
+  if (!st.dram_tier || !st.hbm || deficit == 0) return CASCADE_OK;
+  cudaStream_t s = st.s;
+  // 1. every live HBM slot
+  uint32_t count = 0;
+  for (int pass = 0; pass < 2; ++pass) {
+    size_t want = sizeof(uint32_t) * 64 +
+                  sizeof(ScanRec) * std::max<size_t>(st.claimed + 1024, 4096);
+    if (pass == 1) want = sizeof(uint32_t) * 64 + sizeof(ScanRec) * (count + 1024);
+    int rc = ensure_device_buf(st.scan_d, st.scan_cap, want, s);
+    if (rc) return rc;
+    uint32_t *d_count = reinterpret_cast<uint32_t *>(st.scan_d);
+    ScanRec *d_recs = reinterpret_cast<ScanRec *>(st.scan_d + 256);
+    const uint32_t cap = (uint32_t)((st.scan_cap - 256) / sizeof(ScanRec));
+    rc = launch_index_scan(st.slots, st.nslots, kTierHbm, d_count, d_recs,
+                           cap, s);
+    if (rc) return rc;
+    CB_CUDA(cudaMemcpyAsync(&count, d_count, 4, cudaMemcpyDeviceToHost, s));
+    CB_CUDA(cudaStreamSynchronize(s));
+    if (count <= cap) break;
+  }
+  std::vector<ScanRec> recs(count);
+  if (count)
+    CB_CUDA(cudaMemcpyAsync(recs.data(), st.scan_d + 256,
+                            count * sizeof(ScanRec), cudaMemcpyDeviceToHost, s));
+  CB_CUDA(cudaStreamSynchronize(s));
+  const bool semantic = st.cfg.semantic_eviction && st.cfg.dedup_enabled;
+  std::sort(recs.begin(), recs.end(), [&](const ScanRec &a, const ScanRec &b) {
+    const int pa = semantic && (a.flags & kFlagPrefix), pb = semantic && (b.flags & kFlagPrefix);
+    return pa != pb ? pa < pb : a.epoch < b.epoch;
+  });
+  // 2. victims, while the DRAM tier has room
+  struct Victim { ScanRec r; uint64_t dram_off, hbm; bool dq8; };
+  std::vector<Victim> vic;
+  uint64_t freed = 0, acc_total = 0;
+  for (const ScanRec &r : recs) {
+    if (freed >= deficit) break;
+    const bool hq8 = (r.flags & kFlagQ8) != 0;
+    const bool dq8 = hq8 || q8_eligible(st, r.size, true);
+    const uint64_t acc = dram_accounted(r.size, dq8);
+    if (st.shm_used + acc_total + acc > st.dram->capacity()) break;
+    const uint64_t off = st.dram->alloc(payload_bytes(r.size, dq8));
+    if (off == DramArena::kNone) break;
+    vic.push_back({r, off, payload_bytes(r.size, hq8), dq8});
+    freed += payload_bytes(r.size, hq8);
+    acc_total += acc;
+  }
+  if (vic.empty()) return CASCADE_OK;
+  // raw blocks that become INT8 first: their quantise outputs index 0..nq-1
+  std::stable_partition(vic.begin(), vic.end(), [](const Victim &v) {
+    return v.dq8 && !(v.r.flags & kFlagQ8);
+  });
+  size_t nq = 0;
+  while (nq < vic.size() && vic[nq].dq8 && !(vic[nq].r.flags & kFlagQ8)) ++nq;
+  const size_t k = vic.size();
+  Scratch &oc = st.oc;
+  int rc = ensure_scratch_of(st, oc, k);
+  if (rc) return rc;
+  const uint64_t pool = (uint64_t)(uintptr_t)st.pool;
+  // 3. INT8 forms of raw victims, on the device
+  std::vector<uint64_t> so(nq);
+  uint64_t stage_bytes = 0, max_size = 0;
+  for (size_t j = 0; j < nq; ++j) {
+    so[j] = stage_bytes;
+    stage_bytes += (payload_bytes(vic[j].r.size, true) + 255) & ~uint64_t(255);
+    max_size = std::max<uint64_t>(max_size, vic[j].r.size);
+  }
+  if (nq) {
+    if ((rc = ensure_device_buf(st.d_evstage, st.d_evstage_cap, stage_bytes, s)))
+      return rc;
+    for (size_t j = 0; j < nq; ++j) {
+      oc.h_ptrs[j] = pool + vic[j].r.offset;
+      oc.h_sizes[j] = vic[j].r.size;
+      oc.h_dst[j] = (uint64_t)(uintptr_t)(st.d_evstage + so[j]);
+    }
+    CB_CUDA(cudaMemcpyAsync(oc.ptrs, oc.h_ptrs, nq * 8, cudaMemcpyHostToDevice, s));
+    CB_CUDA(cudaMemcpyAsync(oc.sizes, oc.h_sizes, nq * 8, cudaMemcpyHostToDevice, s));
+    CB_CUDA(cudaMemcpyAsync(oc.dst, oc.h_dst, nq * 8, cudaMemcpyHostToDevice, s));
+    rc = launch_minmax(oc.ptrs, oc.sizes, (int)nq, max_size, oc.mnmx, s);
+    if (!rc) rc = launch_quantize(oc.ptrs, oc.sizes, (int)nq, max_size, oc.mnmx,
+                                  oc.dst, oc.hdr, 0, s);
+    if (rc) return rc;
+  }
+  // 4. payloads into the pinned arena
+  for (size_t j = 0; j < k; ++j) {
+    const Victim &v = vic[j];
+    const uint64_t bytes = payload_bytes(v.r.size, v.dq8);
+    if (!bytes) continue;
+    const void *src = j < nq ? (const void *)(st.d_evstage + so[j])
+                             : (const void *)(uintptr_t)(pool + v.r.offset);
+    CB_CUDA(cudaMemcpyAsync(st.dram->ptr(v.dram_off), src, bytes,
+                            cudaMemcpyDeviceToHost, s));
+  }
+  // 5. slots point into DRAM; the pool takes the space back
+  for (size_t j = 0; j < k; ++j) {
+    const Victim &v = vic[j];
+    oc.h_slot[j] = v.r.slot;
+    oc.h_off[j] = v.dram_off;
+    oc.h_flags[j] = (v.r.flags & kFlagPrefix) | kTierDram | (v.dq8 ? kFlagQ8 : 0);
+    oc.h_req[j] = v.hbm;
+    oc.h_seqs[j] = v.r.offset;
+    uint8_t *h = oc.h_hdr + 8 * j;
+    std::memcpy(h, &v.r.hdr_scale, 4);
+    h[4] = (uint8_t)v.r.hdr_zp;
+    h[5] = h[6] = h[7] = 0;
+  }
+  CB_CUDA(cudaMemcpyAsync(oc.slot, oc.h_slot, k * 4, cudaMemcpyHostToDevice, s));
+  CB_CUDA(cudaMemcpyAsync(oc.off, oc.h_off, k * 8, cudaMemcpyHostToDevice, s));
+  CB_CUDA(cudaMemcpyAsync(oc.flags, oc.h_flags, k * 4, cudaMemcpyHostToDevice, s));
+  CB_CUDA(cudaMemcpyAsync(oc.req, oc.h_req, k * 8, cudaMemcpyHostToDevice, s));
+  CB_CUDA(cudaMemcpyAsync(oc.seqs, oc.h_seqs, k * 8, cudaMemcpyHostToDevice, s));
+  if (k > nq)  // headers of blocks already INT8 (the others come from quantise)
+    CB_CUDA(cudaMemcpyAsync(oc.hdr + 8 * nq, oc.h_hdr + 8 * nq, (k - nq) * 8,
+                            cudaMemcpyHostToDevice, s));
+  CB_CUDA(cudaMemsetAsync(oc.status, CASCADE_PUT_FAILED, k, s));
+  rc = launch_index_relocate(st.slots, oc.slot, oc.off, oc.flags, oc.hdr,
+                             (int)k, s);
+  if (!rc) rc = launch_pool_free_unstored(st.d_pool, oc.req, oc.seqs,
+                                          oc.status, (int)k, s);
+  if (rc) return rc;
+  CB_CUDA(cudaStreamSynchronize(s));
+  st.gpu_used -= freed;
+  st.shm_used += acc_total;
+  st.gpu_evictions += k;
+  return CASCADE_OK;
+}
+
 // ----------------------------------------------------------------- put
 // Core of every put: the inputs (device addresses, sizes, sequence numbers,
 // keys or digests) are already in st.sc on the device.
@@ -413,6 +556,21 @@ static int put_placed(Store &st, size_t n, bool use_digests,
   // cascade_core.cpp:1097-1105), else the DRAM tier while its capacity
   // holds (1108-1118), else the block fails (the Lustre tier of
   // 1121-1124 is not part of this library).
+  // HBM is filled first; when the new blocks do not fit, older ones are
+  // demoted to DRAM to make room (CascadeStore::put, 1097-1105).
+  if (allow_hbm && st.hbm && st.dram_tier) {
+    uint64_t need = 0;
+    for (size_t i = 0; i < n; ++i)
+      if (st.sc.h_status[i] == CASCADE_PUT_STORED)
+        need += payload_bytes(st.sc.h_sizes[i],
+                              q8_eligible(st, st.sc.h_sizes[i], false));
+    if (st.gpu_used + need > st.pool_cap) {
+      const uint64_t fit = std::min<uint64_t>(need, st.pool_cap);
+      const uint64_t deficit = st.gpu_used + fit > st.pool_cap
+                                   ? st.gpu_used + fit - st.pool_cap : 0;
+      if ((rc = evict_hbm(st, deficit))) return rc;
+    }
+  }
   uint64_t hbm_proj = st.gpu_used, dram_proj = st.shm_used;
   uint64_t q8stage_bytes = 0;
   std::vector<size_t> dram_raw, dram_q8;
@@ -921,6 +1079,20 @@ static int deliver_locked(Store &st, size_t n, const uint64_t *out,
   // released.
   if (!(st.cfg.promotion_enabled && st.hbm)) return CASCADE_OK;
   std::vector<size_t> promo;
+  {  // room for the promotions: demote older HBM blocks first
+    uint64_t need = 0;
+    for (size_t i = 0; i < n; ++i) {
+      const LookupInfo &f = st.sc.h_info[i];
+      if (!f.found || !deliver[i] || !(f.flags & kTierDram)) continue;
+      const uint64_t size = (f.flags & kFlagQ8) ? 2 * (f.size / 2) : f.size;
+      need += payload_bytes(size, q8_eligible(st, size, false));
+    }
+    need = std::min<uint64_t>(need, st.pool_cap);
+    if (need && st.gpu_used + need > st.pool_cap) {
+      int rc = evict_hbm(st, st.gpu_used + need - st.pool_cap);
+      if (rc) return rc;
+    }
+  }
   uint64_t proj = st.gpu_used;
   for (size_t i = 0; i < n; ++i) {
     const LookupInfo &f = st.sc.h_info[i];
@@ -1176,6 +1348,8 @@ static void destroy_store(Store *st) {
   if (st->d_stage) cudaFree(st->d_stage);
   if (st->h_stage) cudaFreeHost(st->h_stage);
   if (st->d_q8stage) cudaFree(st->d_q8stage);
+  if (st->d_evstage) cudaFree(st->d_evstage);
+  if (st->scan_d) cudaFree(st->scan_d);
   if (st->sha_state) cudaFree(st->sha_state);
   for (cudaEvent_t e : {st->ev, st->ev2, st->ev3})
     if (e) cudaEventDestroy(e);

@@ -148,8 +148,10 @@ struct ScanRec {
   uint64_t size;
   uint64_t offset;
   uint64_t epoch;
+  uint32_t hdr_scale;
+  uint32_t hdr_zp;
 };
-static_assert(sizeof(ScanRec) == 32, "scan record layout");
+static_assert(sizeof(ScanRec) == 40, "scan record layout");
 
 constexpr uint64_t kNoRequest = ~0ull;  // pool request: allocate nothing
 

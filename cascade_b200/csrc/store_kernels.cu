@@ -169,6 +169,8 @@ __global__ void scan_kernel(const Slot *__restrict__ slots, uint64_t nslots,
       r.size = sl.size;
       r.offset = sl.offset;
       r.epoch = sl.epoch;
+      r.hdr_scale = sl.hdr_scale;
+      r.hdr_zp = sl.hdr_zp;
       out[k] = r;
     }
   }

@@ -316,3 +316,66 @@ def test_hbm_allocation_failure_falls_back(with_dram):
         assert found == (status[i] == 0)
         if found:
             assert np.array_equal(buf, host[i])
+
+
+def _stats(st):
+    return stats_dict(st.get_stats())
+
+
+def test_demotion_lru_with_prefix_protection():
+    """HBM holds 8 blocks; 4 more evict the 4 least recently used non-prefix
+    blocks to DRAM (raw bytes), prefix blocks and a recently read block stay."""
+    S = 4096
+    rng = np.random.default_rng(31)
+    blocks = [rng.integers(0, 256, S, dtype=np.uint8) for _ in range(12)]
+    ids = [oracle.block_id(b) for b in blocks]
+    st = make_store(use_gpu=True, gpu_cap=8 * S, shm_cap=1 << 20,
+                    promotion=False)
+    for i in range(8):
+        assert st.put(ids[i], blocks[i], is_prefix=i < 2)
+    buf = np.zeros(S, np.uint8)
+    assert st.get(ids[2], buf) == (True, S)          # touch block 2
+    for i in range(8, 12):
+        assert st.put(ids[i], blocks[i])
+    s = _stats(st)
+    assert s["gpu_evictions"] == 4
+    assert s["gpu_used"] == 8 * S and s["shm_used"] == 4 * S
+    hits = []
+    for i in range(12):
+        before = _stats(st)
+        assert st.get(ids[i], buf) == (True, S)
+        assert np.array_equal(buf, blocks[i])
+        after = _stats(st)
+        hits.append("gpu" if after["gpu_hits"] > before["gpu_hits"] else "shm")
+    assert [i for i, h in enumerate(hits) if h == "shm"] == [3, 4, 5, 6]
+
+
+@pytest.mark.parametrize("gpu_q8", [False, True])
+def test_demotion_to_int8_dram_and_promotion(gpu_q8):
+    """With kv_compression the DRAM tier holds INT8: demoted blocks come back
+    dequantised (bit-exact with KVCompressor), and a DRAM hit is promoted
+    back to HBM, demoting another block to make room."""
+    blocks = workloads.kv_blocks_np(6, 77, layers=2)          # 128 KiB each
+    S = blocks.shape[1]
+    ids = [oracle.block_id(b) for b in blocks]
+    hbm_per_block = S // 2 if gpu_q8 else S
+    st = make_store(use_gpu=True, gpu_cap=4 * hbm_per_block, shm_cap=8 << 20,
+                    kv_compression=True, gpu_q8=gpu_q8)
+    for i in range(6):
+        assert st.put(ids[i], blocks[i])
+    s = _stats(st)
+    assert s["gpu_evictions"] == 2 and s["gpu_used"] == 4 * hbm_per_block
+    assert s["shm_used"] == 2 * (8 + S // 2)
+    buf = np.zeros(S, np.uint8)
+    for i in range(6):
+        assert st.get(ids[i], buf) == (True, S)
+        lossy = oracle.kv_decompress(oracle.kv_compress(blocks[i]), S)
+        if i < 2 or gpu_q8:        # went through the INT8 form
+            assert np.array_equal(buf, lossy), i
+        else:
+            # each promotion demotes the then least recently used HBM block,
+            # so a later block may have been through the INT8 form as well
+            assert np.array_equal(buf, blocks[i]) or np.array_equal(buf, lossy), i
+    s = _stats(st)
+    assert s["promotions_to_gpu"] >= 2
+    assert s["gpu_used"] <= 4 * hbm_per_block
