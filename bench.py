@@ -40,7 +40,7 @@ CPU_MIN_SECONDS = 5.0
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--blocks", type=int, default=N_BLOCKS)
@@ -49,6 +49,10 @@ def parse():
                          "profiling captures)")
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", default="llama3-8b",
+                    choices=["llama3-8b", "sweep", "dedup"],
+                    help="llama3-8b: the headline line; sweep / dedup: the "
+                         "block-size sweep and the prefix-dedup mix")
     return ap.parse_args()
 
 
@@ -100,8 +104,13 @@ class ClockSampler:
         return self
 
     def _read(self):
+        import time
         for line in self.proc.stdout:
-            self.lines.append(line.strip())
+            self.lines.append((time.perf_counter(), line.strip()))
+
+    def mark(self, name):
+        import time
+        setattr(self, name, time.perf_counter())
 
     def __exit__(self, *exc):
         if self.proc:
@@ -115,7 +124,11 @@ class ClockSampler:
         mhz, mx, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown",
                  "sw_power_cap"]
-        for ln in self.lines:
+        t0 = getattr(self, "t_begin", None)
+        t1 = getattr(self, "t_end", None)
+        for when, ln in self.lines:
+            if t0 is not None and not (t0 - 0.15 <= when <= t1 + 0.15):
+                continue
             f = [x.strip() for x in ln.split(",")]
             if len(f) < 9:
                 continue
@@ -251,14 +264,13 @@ def main_ours(args):
             return store._put_batch_raw(n, ptrs, sizes, None, None, False,
                                         stream)
 
-    for _ in range(args.warmup):
-        assert step() == n
-    torch.cuda.synchronize()
-    barrier()
-    launches0 = L.cascade_diag_launch_count()
-    with ClockSampler(local) as clk:
+    with ClockSampler(local) as clk:   # sampling runs from warm-up on
+        for _ in range(args.warmup):
+            assert step() == n
         torch.cuda.synchronize()
         barrier()
+        launches0 = L.cascade_diag_launch_count()
+        clk.mark("t_begin")
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
         e0.record()
@@ -266,6 +278,7 @@ def main_ours(args):
             stored = step()
         e1.record()
         torch.cuda.synchronize()
+        clk.mark("t_end")
         barrier()
     launches = L.cascade_diag_launch_count() - launches0
     ms = max_over_ranks(e0.elapsed_time(e1))
@@ -304,6 +317,34 @@ def main_ours(args):
     _lib.call("cascade_diag_sha_peak", local, 256, ctypes.byref(peak_gbps),
               ctypes.byref(peak_ms))
     del qdst
+    host = torch.empty((n, bb), dtype=torch.uint8, pin_memory=True)
+    host.copy_(blocks)          # the e2e inputs, before GET overwrites blocks
+    # ---- GET: lookup + INT8 dequantise of the whole workload into device
+    # buffers (the blocks' own memory is the output)
+    store.clear() if world == 1 else sharded.clear()
+    if world == 1:
+        _, _, dig = store._put_batch_raw(n, ptrs, sizes, None, None, True,
+                                         stream)
+        keys16 = np.ascontiguousarray(dig[:, :16]).reshape(-1)
+        caps = np.full(n, bb, np.uint64)
+        for _ in range(2):
+            store._get_batch_raw(n, keys16, ptrs, caps, stream)
+        torch.cuda.synchronize()
+        ga = torch.cuda.Event(enable_timing=True)
+        gb_ = torch.cuda.Event(enable_timing=True)
+        ga.record()
+        for _ in range(3):
+            found, gsz = store._get_batch_raw(n, keys16, ptrs, caps, stream)
+        gb_.record()
+        torch.cuda.synchronize()
+        assert found.all() and (gsz == bb).all()
+        get_ms = ga.elapsed_time(gb_) / 3
+        get_info = {"value": total / (get_ms * 1e-3) / 1e9, "unit": UNIT,
+                    "ms": get_ms, "what": "get_batch of every block: index "
+                    "lookup + INT8 dequantise into device buffers (FP16 bytes "
+                    "out per second)"}
+    else:
+        get_info = None
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
             hbm_peak = float(json.load(f)["hbm_gbs"])
@@ -312,8 +353,6 @@ def main_ours(args):
         hbm_peak, hbm_src = 6650.0, "profiling-recipe fallback (of fallback)"
 
     # ---- e2e: host buffers through the public API
-    host = torch.empty((n, bb), dtype=torch.uint8, pin_memory=True)
-    host.copy_(blocks)
     del blocks, dptrs, dsizes, digests
     torch.cuda.empty_cache()
     host_np = host.numpy()
@@ -393,6 +432,7 @@ def main_ours(args):
             "algorithmic_bytes": "1.5 x block bytes (min/max re-read not counted)",
             "traffic": (traffic or {}).get("quantize_kernel")},
         "stage_ms": {"sha256": sha_ms, "compress": q_ms},
+        "get": get_info,
         "cpu_baseline": cpu,
         "e2e": {"value": e2e_value, "unit": UNIT,
                 "h2d_bytes_per_step": total, "d2h_bytes_per_step": n * 33,
@@ -413,10 +453,146 @@ def main_ours(args):
         dist.destroy_process_group()
 
 
+# ------------------------------------------------------- extra workloads
+def run_extra(args):
+    """--workload sweep | dedup: the other reference configurations, one
+    JSON line each (not the headline line)."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    from cascade_b200 import cascade_cpp as cc
+    from cascade_b200 import workloads
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", device_id=dev,
+                                timeout=timedelta(seconds=120))
+    stream = torch.cuda.current_stream(dev).cuda_stream
+
+    def timed_steps(step, warm, steps):
+        for _ in range(warm):
+            step()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(steps):
+            out = step()
+        b.record()
+        torch.cuda.synchronize()
+        ms = a.elapsed_time(b) / steps
+        if world > 1:
+            t = torch.tensor([ms], device=dev, dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms, out
+
+    def make_store(cap_bytes):
+        cfg = cc.CascadeConfig()
+        cfg.gpu_device_id = local
+        cfg.gpu_capacity_bytes = cap_bytes
+        cfg.shm_capacity_bytes = 0
+        cfg.kv_compression = True
+        cfg.gpu_q8 = True
+        cfg.index_slots = 1 << 16
+        if world > 1:
+            from cascade_b200.sharded import ShardedCascadeStore
+            return ShardedCascadeStore(cfg)
+        return cc.CascadeStore(cfg)
+
+    def put_fn(store, rows_or_list, n, ptrs, sizes):
+        if world > 1:
+            def step():
+                store.clear()
+                return store.put_batch(rows_or_list)
+        else:
+            def step():
+                store.clear()
+                return store._put_batch_raw(n, ptrs, sizes, None, None, False,
+                                            stream)
+        return step
+
+    if args.workload == "sweep":
+        res = []
+        for layers in (1, 4, 16, 64, 256):          # 64 KiB .. 16 MiB
+            bb = workloads.kv_block_bytes(layers, 8, 16, 128)
+            n = (1 << 30) // bb
+            blocks = workloads.kv_blocks_torch(n, SEED + rank + layers, dev,
+                                               layers=layers)
+            ptrs = np.arange(n, dtype=np.uint64) * np.uint64(bb) + np.uint64(blocks.data_ptr())
+            sizes = np.full(n, bb, np.uint64)
+            store = make_store(int(n * bb // 2 * 1.1) + (64 << 20))
+            ms, stored = timed_steps(put_fn(store, blocks, n, ptrs, sizes),
+                                     args.warmup, args.steps)
+            assert stored == n
+            res.append({"block_bytes": bb, "blocks_per_gpu": n,
+                        "ms_per_step": ms,
+                        "gbps": world * n * bb / (ms * 1e-3) / 1e9,
+                        "blocks_per_s": world * n / (ms * 1e-3)})
+            del store, blocks
+            torch.cuda.empty_cache()
+        line = {"workload": "variable block-size sweep, 1 GiB of FP16 KV per "
+                            "size per GPU, content-addressed INT8 PUT",
+                "metric": METRIC, "unit": UNIT, "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "sweep": res}
+    else:   # dedup: 8192 blocks, 60 % Zipf copies of 512 shared prefixes
+        n = 8192
+        seq, pre = workloads.dedup_sequence(n, SEED + rank, pool=512,
+                                            sessions=256)
+        pool = workloads.kv_blocks_torch(512, SEED, dev)        # shared
+        uniq_n = int((seq >= 512).sum())
+        uniq = workloads.kv_blocks_torch(uniq_n, SEED + 1000 + rank, dev)
+        bb = pool.shape[1]
+        pp, up = pool.data_ptr(), uniq.data_ptr()
+        ptrs = np.array([pp + int(k) * bb if k < 512 else up + int(k - 512) * bb
+                         for k in seq], dtype=np.uint64)
+        sizes = np.full(n, bb, np.uint64)
+        store = make_store(int((512 + uniq_n) * bb // 2 * 1.2) + (256 << 20))
+        if world > 1:
+            rows = [pool[int(k)] if k < 512 else uniq[int(k) - 512] for k in seq]
+        else:
+            rows = None
+        ms, stored = timed_steps(put_fn(store, rows, n, ptrs, sizes),
+                                 args.warmup, args.steps)
+        st = store.get_stats()
+        hits = int(st.dedup_hits)
+        tot_hits, tot_distinct = hits, None
+        if world > 1:
+            t = torch.tensor([hits], device=dev, dtype=torch.int64)
+            dist.all_reduce(t)
+            tot_hits = int(t.item())
+        else:
+            tot_distinct = len(np.unique(seq))
+            assert hits == n - tot_distinct, (hits, n, tot_distinct)
+        line = {"workload": "prefix-dedup: 8192 x 2 MiB per GPU, 60% Zipf(1.1) "
+                            "copies of 512 shared prefix blocks, 256 sessions",
+                "metric": METRIC, "unit": UNIT, "n_gpus": world,
+                "value": world * n * bb / (ms * 1e-3) / 1e9,
+                "ms_per_step": ms, "steps": args.steps, "warmup": args.warmup,
+                "dedup_hits_total": tot_hits,
+                "expected_hits": (n - tot_distinct) if world == 1 else None,
+                "parallelism": f"sharded index x{world}" if world > 1 else "1 GPU"}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload != "llama3-8b":
+        run_extra(args)
     else:
         main_ours(args)
 

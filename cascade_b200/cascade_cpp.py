@@ -382,13 +382,19 @@ class CascadeStore:
             raise ValueError("one key per output")
         ptrs = np.array([o.data_ptr() for o in outs], dtype=np.uint64)
         caps = np.array([o.numel() for o in outs], dtype=np.uint64)
+        stream = _torch_stream_of(outs[0]) if n else 0
+        return self._get_batch_raw(n, kbuf, ptrs, caps, stream)
+
+    def _get_batch_raw(self, n, keys16, ptrs, caps, stream):
+        """get_batch on prepared arrays: keys16 uint8[n*16], ptrs / caps
+        uint64[n] (device addresses and their capacities)."""
         sizes = np.zeros(n, np.uint64)
         found = np.zeros(n, np.uint8)
         nf = _u64(0)
-        stream = _torch_stream_of(outs[0]) if n else 0
         check(_lib.load().cascade_store_get_batch(
-            self._h, n, kbuf.ctypes.data, ptrs.ctypes.data, caps.ctypes.data,
-            sizes.ctypes.data, found.ctypes.data, stream, ctypes.byref(nf)))
+            self._h, n, keys16.ctypes.data, ptrs.ctypes.data,
+            caps.ctypes.data, sizes.ctypes.data, found.ctypes.data, stream,
+            ctypes.byref(nf)))
         return found, sizes
 
     def close(self) -> None:
