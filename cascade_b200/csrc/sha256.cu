@@ -123,7 +123,7 @@ __device__ __forceinline__ void message_words(const Lane &l, uint64_t c,
 // beyond c_end gets its running state saved to `state` (and the next call
 // with c_begin = this c_end resumes from it).  c_begin = 0 starts from the
 // initial hash value.  One call with [0, ~0) hashes whole blocks.
-template <int kGroups, int kStages, int kRound>
+template <int kGroups, int kStages, int kRound, int kUnroll = 64>
 __global__ void __launch_bounds__(64 * kGroups)
     sha256_pipelined(const uint64_t *__restrict__ ptrs,
                      const uint64_t *__restrict__ sizes, int n,
@@ -203,16 +203,23 @@ __global__ void __launch_bounds__(64 * kGroups)
     bar_sync(full_bar + s);
     uint32_t a = st[0], b = st[1], cc = st[2], d = st[3];
     uint32_t e = st[4], f = st[5], g = st[6], h = st[7];
+    // Every round runs the same instructions (K[t] is folded into kw by the
+    // producer), and the eight working variables come back to their
+    // registers every 8 rounds, so kUnroll rounds (a multiple of 8) form a
+    // loop body small enough for the instruction cache.
+#pragma unroll 1
+    for (int t0 = 0; t0 < 64; t0 += kUnroll) {
 #pragma unroll
-    for (int t = 0; t < 64; t += 4) {
-      const uint4 kw = ring[s][t >> 2][lane];
-      const uint32_t kv[4] = {kw.x, kw.y, kw.z, kw.w};
+      for (int t = t0; t < t0 + kUnroll; t += 4) {
+        const uint4 kw = ring[s][t >> 2][lane];
+        const uint32_t kv[4] = {kw.x, kw.y, kw.z, kw.w};
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        if (kRound == 0)
-          sha::round_kw(a, b, cc, d, e, f, g, h, kv[u], one, neg_one);
-        else
-          sha::round_kw3(a, b, cc, d, e, f, g, h, kv[u], one, neg_one);
+        for (int u = 0; u < 4; ++u) {
+          if (kRound == 0)
+            sha::round_kw(a, b, cc, d, e, f, g, h, kv[u], one, neg_one);
+          else
+            sha::round_kw3(a, b, cc, d, e, f, g, h, kv[u], one, neg_one);
+        }
       }
     }
     bar_arrive(empty_bar + s);
@@ -235,13 +242,13 @@ __global__ void __launch_bounds__(64 * kGroups)
 
 }  // namespace
 
-template <int G, int S, int R>
+template <int G, int S, int R, int U = 64>
 int launch_sha256_pipelined(const uint64_t *d_ptrs, const uint64_t *d_sizes,
                             int n, uint8_t *d_digests, uint32_t *d_state,
                             uint64_t c_begin, uint64_t c_end, cudaStream_t s) {
   if (n <= 0) return CASCADE_OK;
   const int blocks = (n + 32 * G - 1) / (32 * G);
-  sha256_pipelined<G, S, R><<<blocks, 64 * G, 0, s>>>(
+  sha256_pipelined<G, S, R, U><<<blocks, 64 * G, 0, s>>>(
       d_ptrs, d_sizes, n, reinterpret_cast<uint32_t *>(d_digests), 1u,
       0xffffffffu, d_state, c_begin, c_end);
   count_launches(1);
@@ -257,10 +264,10 @@ int launch_sha256_range(const uint64_t *d_ptrs, const uint64_t *d_sizes,
   // operations deep) wins; once every scheduler has work, the ALU pipe is
   // the limit and the round with the fewest ALU instructions wins.
   if (n <= 32 * kSmCount)
-    return launch_sha256_pipelined<1, 4, 1>(d_ptrs, d_sizes, n, d_digests,
-                                            d_state, c_begin, c_end, s);
-  return launch_sha256_pipelined<2, 3, 0>(d_ptrs, d_sizes, n, d_digests,
-                                          d_state, c_begin, c_end, s);
+    return launch_sha256_pipelined<1, 4, 1, 16>(d_ptrs, d_sizes, n, d_digests,
+                                                d_state, c_begin, c_end, s);
+  return launch_sha256_pipelined<2, 3, 0, 16>(d_ptrs, d_sizes, n, d_digests,
+                                              d_state, c_begin, c_end, s);
 }
 
 int launch_sha256(const uint64_t *d_ptrs, const uint64_t *d_sizes, int n,
