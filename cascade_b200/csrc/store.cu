@@ -1756,7 +1756,8 @@ static int shard_end(Store &st, const uint8_t *d_back, size_t n,
   CB_CHECK(st.shard_open == n, CASCADE_ERR_INVALID,
            "shard_put_end: no open batch of this size");
   cudaStream_t s = st.s;
-  CB_CUDA(cudaMemsetAsync(st.sc.status, CASCADE_PUT_FAILED, n, s));
+  // 0xff marks "no reply yet"; every block must get exactly one reply.
+  CB_CUDA(cudaMemsetAsync(st.sc.status, 0xff, n, s));
   CB_CUDA(cudaMemsetAsync(st.sc.err, 0, sizeof(int), s));
   shard_apply_kernel<<<nblocks(n), 256, 0, s>>>(
       (int)n, (int)n, reinterpret_cast<const ShardReply *>(d_back),
@@ -1774,6 +1775,11 @@ static int shard_end(Store &st, const uint8_t *d_back, size_t n,
   st.shard_open = 0;
   CB_CHECK(*st.sc.h_err == 0, CASCADE_ERR_INVALID,
            "shard_put_end: a reply names no block of this batch");
+  size_t missing = 0;
+  for (size_t i = 0; i < n; ++i) missing += st.sc.h_status[i] == 0xff;
+  CB_CHECK(missing == 0, CASCADE_ERR_INVALID,
+           "shard_put_end: " + std::to_string(missing) +
+               " blocks of this batch got no reply");
   // Index load is counted by the owners; the rest is this rank's.
   const uint64_t claimed = st.claimed;
   tally_put(st, n);
@@ -1787,6 +1793,18 @@ static int shard_end(Store &st, const uint8_t *d_back, size_t n,
 struct cascade_store {
   cb::Store *impl;
 };
+
+namespace {
+// The store's streams are non-blocking, so they do not wait for the legacy
+// default stream by themselves: the caller's stream (NULL = the legacy
+// default stream, which is also torch's default) is always joined with an
+// event before the inputs are read.
+int join_caller(cb::Store &st, void *stream) {
+  CB_CUDA(cudaEventRecord(st.ev, static_cast<cudaStream_t>(stream)));
+  CB_CUDA(cudaStreamWaitEvent(st.s, st.ev, 0));
+  return CASCADE_OK;
+}
+}  // namespace
 
 #define STORE_ENTRY(s)                                                       \
   cb::clear_error();                                                         \
@@ -1952,10 +1970,7 @@ extern "C" int cascade_store_put_batch(cascade_store_t *s, size_t n,
   if (n == 0) return CASCADE_OK;
   CB_CHECK(h_ptrs && h_sizes, CASCADE_ERR_INVALID, "null argument");
   CB_CHECK(n <= (size_t)INT32_MAX, CASCADE_ERR_INVALID, "batch too large");
-  if (stream) {  // the caller's producer work comes first
-    CB_CUDA(cudaEventRecord(st.ev, static_cast<cudaStream_t>(stream)));
-    CB_CUDA(cudaStreamWaitEvent(st.s, st.ev, 0));
-  }
+  if (int rc = join_caller(st, stream)) return rc;
   return cb::put_batch_locked(st, n, h_ptrs, h_sizes, h_keys, h_prefix,
                               h_status, h_digests, n_stored);
 }
@@ -1985,10 +2000,7 @@ extern "C" int cascade_store_get_batch(cascade_store_t *s, size_t n,
   CB_CHECK(h_keys && h_out_ptrs && h_out_caps, CASCADE_ERR_INVALID,
            "null argument");
   CB_CHECK(n <= (size_t)INT32_MAX, CASCADE_ERR_INVALID, "batch too large");
-  if (stream) {
-    CB_CUDA(cudaEventRecord(st.ev, static_cast<cudaStream_t>(stream)));
-    CB_CUDA(cudaStreamWaitEvent(st.s, st.ev, 0));
-  }
+  if (int rc = join_caller(st, stream)) return rc;
   return cb::get_batch_locked(st, n, h_keys, h_out_ptrs, h_out_caps, h_sizes,
                               h_found, n_found);
 }
@@ -2013,10 +2025,7 @@ extern "C" int cascade_shard_put_begin(cascade_store_t *s, size_t n,
     st.shard_open = 0;
     return CASCADE_OK;
   }
-  if (stream) {
-    CB_CUDA(cudaEventRecord(st.ev, static_cast<cudaStream_t>(stream)));
-    CB_CUDA(cudaStreamWaitEvent(st.s, st.ev, 0));
-  }
+  if (int rc = join_caller(st, stream)) return rc;
   return cb::shard_begin(st, n, h_ptrs, h_sizes, h_prefix, world, rank,
                          seq_base, d_send, h_send_counts);
 }
@@ -2027,10 +2036,7 @@ extern "C" int cascade_shard_resolve(cascade_store_t *s, const uint8_t *d_recv,
   CB_CHECK(m == 0 || (d_recv && d_reply), CASCADE_ERR_INVALID,
            "null argument");
   CB_CHECK(m <= (size_t)INT32_MAX, CASCADE_ERR_INVALID, "batch too large");
-  if (stream) {
-    CB_CUDA(cudaEventRecord(st.ev, static_cast<cudaStream_t>(stream)));
-    CB_CUDA(cudaStreamWaitEvent(st.s, st.ev, 0));
-  }
+  if (int rc = join_caller(st, stream)) return rc;
   return cb::shard_resolve(st, d_recv, m, d_reply);
 }
 
@@ -2042,9 +2048,6 @@ extern "C" int cascade_shard_put_end(cascade_store_t *s, const uint8_t *d_back,
   if (n_stored) *n_stored = 0;
   if (n == 0) return CASCADE_OK;
   CB_CHECK(d_back, CASCADE_ERR_INVALID, "null argument");
-  if (stream) {
-    CB_CUDA(cudaEventRecord(st.ev, static_cast<cudaStream_t>(stream)));
-    CB_CUDA(cudaStreamWaitEvent(st.s, st.ev, 0));
-  }
+  if (int rc = join_caller(st, stream)) return rc;
   return cb::shard_end(st, d_back, n, h_status, h_digests, n_stored);
 }

@@ -148,6 +148,28 @@ def test_device_batch_put_get_content_addressed():
     assert np.array_equal(buf, host[3])
 
 
+@pytest.mark.parametrize("side_stream", [False, True])
+def test_batch_put_waits_for_callers_stream(side_stream):
+    """The blocks' final bytes are written on the caller's stream behind a
+    long sleep kernel; the put must hash and store those bytes, whether the
+    caller's stream is torch's default stream (handle 0, the legacy default
+    stream) or a stream of its own."""
+    n = 8
+    want = workloads.kv_blocks_torch(n, 11, DEV, layers=2)
+    blocks = torch.zeros_like(want)
+    torch.cuda.synchronize()
+    side = torch.cuda.Stream(DEV) if side_stream else None
+    st = make_store(use_gpu=True, gpu_cap=64 << 20)
+    with torch.cuda.stream(side) if side is not None else torch.cuda.device(DEV):
+        torch.cuda._sleep(200_000_000)          # ~0.1 s at 1.9 GHz
+        blocks.copy_(want)
+        stored, status, digests = st.put_batch(blocks, return_status=True)
+    assert stored == n and (status == 0).all()
+    host = want.cpu().numpy()
+    for i in range(n):
+        assert digests[i].tobytes() == hashlib.sha256(host[i].tobytes()).digest()
+
+
 def test_device_batch_q8_roundtrip_matches_oracle():
     blocks = workloads.kv_blocks_torch(8, 9, DEV)                # 2 MiB each
     st = make_store(use_gpu=True, gpu_cap=256 << 20, kv_compression=True,
