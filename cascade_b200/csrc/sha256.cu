@@ -22,6 +22,22 @@ __device__ __forceinline__ uint4 ldg_stream(const uint4 *p) {
   return v;
 }
 
+// 16-byte global -> shared copy that completes asynchronously; each thread
+// waits for its own copies with cp.async.wait_group.
+__device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
+  const uint32_t dst = (uint32_t)__cvta_generic_to_shared(smem);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst),
+               "l"(gmem)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+template <int kPending>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(kPending) : "memory");
+}
+
 __device__ __forceinline__ uint32_t ldg_u32(const uint32_t *p) {
   uint32_t v;
   asm volatile("ld.global.nc.u32 %0, [%1];" : "=r"(v) : "l"(p));
@@ -115,15 +131,51 @@ __device__ __forceinline__ void message_words(const Lane &l, uint64_t c,
   }
 }
 
+// Producer side of one chunk: waits for ring slot it % kStages to be free,
+// expands the message schedule and publishes K[t] + W[t] for t = 0..63.
+template <int kStages>
+__device__ __forceinline__ void publish_chunk(uint4 (*ring)[16][32], int lane,
+                                              uint32_t it, uint32_t w[16],
+                                              int full_bar, int empty_bar) {
+  const int s = (int)(it % kStages);
+  if (it >= kStages) bar_sync(empty_bar + s);
+#pragma unroll
+  for (int t = 0; t < 64; t += 4) {
+    uint32_t kw[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int tt = t + u;
+      uint32_t wt;
+      if (tt < 16) {
+        wt = w[tt];
+      } else {
+        wt = w[tt & 15] + sha::sig0(w[(tt - 15) & 15]) + w[(tt - 7) & 15] +
+             sha::sig1(w[(tt - 2) & 15]);
+        w[tt & 15] = wt;
+      }
+      kw[u] = wt + sha::K(tt);
+    }
+    ring[s][t >> 2][lane] = make_uint4(kw[0], kw[1], kw[2], kw[3]);
+  }
+  bar_arrive(full_bar + s);
+}
+
 // kGroups (consumer, producer) warp pairs per CTA: warp 2g consumes and
-// warp 2g+1 produces for group g.  Named barrier ids per group:
+// warp 2g+1 produces for group g.  kAhead > 0: the producer streams the
+// chunks that every live lane of its warp has in full, at 16-byte-aligned
+// addresses, through a ring of kAhead chunk slots in shared memory
+// (cp.async, kAhead chunks in flight per lane), which hides DRAM latency
+// when each scheduler holds a single warp pair; the other chunks (unaligned
+// blocks, tails, padding), and every chunk when kAhead = 0, take the generic
+// path that loads the next chunk into registers while this one is expanded
+// (enough once several warps share a scheduler).  Named barrier ids per group:
 // full = 1 + 2*kStages*g + s, empty = full + kStages (at most 15 ids).
 // Chunks [c_begin, c_end) of every block are processed; a block whose last
 // chunk falls in that range gets its digest written, a block that goes on
 // beyond c_end gets its running state saved to `state` (and the next call
 // with c_begin = this c_end resumes from it).  c_begin = 0 starts from the
 // initial hash value.  One call with [0, ~0) hashes whole blocks.
-template <int kGroups, int kStages, int kRound, int kUnroll = 64>
+template <int kGroups, int kStages, int kRound, int kUnroll, int kAhead>
 __global__ void __launch_bounds__(64 * kGroups)
     sha256_pipelined(const uint64_t *__restrict__ ptrs,
                      const uint64_t *__restrict__ sizes, int n,
@@ -133,9 +185,12 @@ __global__ void __launch_bounds__(64 * kGroups)
   static_assert(2 * kGroups * kStages <= 15, "named barrier ids");
   // ring[g][s][t/4][lane] holds K[t..t+3] + W[t..t+3] of one chunk.
   __shared__ uint4 ring_all[kGroups][kStages][16][32];
+  // raw[g][slot][k][lane]: bytes 16k..16k+15 of a lane's chunk in flight
+  __shared__ uint4 raw_all[kGroups][kAhead > 0 ? kAhead : 1][4][32];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int grp = warp >> 1;
+  const int grp = kGroups == 1 ? 0 : warp >> 1;
   uint4 (*ring)[16][32] = ring_all[grp];
+  uint4 (*raw)[4][32] = raw_all[grp];
   const int full_bar = 1 + 2 * kStages * grp;
   const int empty_bar = full_bar + kStages;
   const int i = (blockIdx.x * kGroups + grp) * 32 + lane;
@@ -146,47 +201,76 @@ __global__ void __launch_bounds__(64 * kGroups)
   const uint32_t iters = c_stop > c_begin ? (uint32_t)(c_stop - c_begin) : 0u;
 
   if (warp & 1) {  // -------------------------------------------- producer
-    uint4 pre[4] = {};
     const uint4 *q = reinterpret_cast<const uint4 *>(l.p);
-    if (l.aligned && c_begin < l.nfull && iters > 0) {
+    uint32_t it = 0;
+    // Loads never reach past this call's range: the bytes of later chunks
+    // may not have arrived yet.
+    if constexpr (kAhead > 0) {
+      // Fast range (warp-uniform): chunks that every live lane has in full
+      // at a 16-byte-aligned address.  Lanes without a block load nothing
+      // and publish words that the consumer discards.
+      const bool live = i < n;
+      const uint64_t mine = !live ? ~0ull : (l.aligned ? l.nfull : 0ull);
+      const uint32_t fast_end = __reduce_min_sync(
+          0xffffffffu, (uint32_t)(mine < 0xffffffffull ? mine : 0xffffffffull));
+      const uint64_t fast_stop = fast_end < c_stop ? fast_end : c_stop;
+      const uint32_t it_fast =
+          fast_stop > c_begin ? (uint32_t)(fast_stop - c_begin) : 0u;
+#pragma unroll 1
+      for (uint32_t j = 0; j < (uint32_t)kAhead; ++j) {
+        if (live && j < it_fast) {
 #pragma unroll
-      for (int k = 0; k < 4; ++k) pre[k] = ldg_stream(q + 4 * c_begin + k);
+          for (int k = 0; k < 4; ++k)
+            cp_async16(&raw[j][k][lane], q + 4 * (c_begin + j) + k);
+        }
+        cp_async_commit();
+      }
+#pragma unroll 1
+      for (; it < it_fast; ++it) {
+        const int slot = (int)(it % (uint32_t)kAhead);
+        cp_async_wait<kAhead - 1>();  // this lane's copy of chunk it landed
+        uint32_t w[16];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const uint4 v = raw[slot][k][lane];
+          w[4 * k] = sha::bswap(v.x);
+          w[4 * k + 1] = sha::bswap(v.y);
+          w[4 * k + 2] = sha::bswap(v.z);
+          w[4 * k + 3] = sha::bswap(v.w);
+        }
+        // The slot is refilled after its words are in registers.
+        if (live && it + kAhead < it_fast) {
+          const uint64_t cn = c_begin + it + kAhead;
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            cp_async16(&raw[slot][k][lane], q + 4 * cn + k);
+        }
+        cp_async_commit();
+        publish_chunk<kStages>(ring, lane, it, w, full_bar, empty_bar);
+      }
+      cp_async_wait<0>();
     }
-    for (uint32_t it = 0; it < iters; ++it) {
+    // Generic range: unaligned blocks, the tail and the padding chunks,
+    // with the next chunk's loads in registers.
+    uint4 pre[4] = {};
+    if (l.aligned && c_begin + it < l.nfull && it < iters) {
+#pragma unroll
+      for (int k = 0; k < 4; ++k) pre[k] = ldg_stream(q + 4 * (c_begin + it) + k);
+    }
+#pragma unroll 1
+    for (; it < iters; ++it) {
       const uint64_t c = c_begin + it;
-      const int s = (int)(it % kStages);
       uint32_t w[16];
       message_words(l, c, pre, w);
-      // the next chunk's loads in flight (never past this call's range: the
-      // bytes of later chunks may not have arrived yet)
       if (l.aligned && c + 1 < l.nfull && it + 1 < iters) {
 #pragma unroll
         for (int k = 0; k < 4; ++k) pre[k] = ldg_stream(q + 4 * (c + 1) + k);
       }
-      if (it >= kStages) bar_sync(empty_bar + s);
-#pragma unroll
-      for (int t = 0; t < 64; t += 4) {
-        uint32_t kw[4];
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const int tt = t + u;
-          uint32_t wt;
-          if (tt < 16) {
-            wt = w[tt];
-          } else {
-            wt = w[tt & 15] + sha::sig0(w[(tt - 15) & 15]) + w[(tt - 7) & 15] +
-                 sha::sig1(w[(tt - 2) & 15]);
-            w[tt & 15] = wt;
-          }
-          kw[u] = wt + sha::K(tt);
-        }
-        ring[s][t >> 2][lane] = make_uint4(kw[0], kw[1], kw[2], kw[3]);
-      }
-      bar_arrive(full_bar + s);
+      publish_chunk<kStages>(ring, lane, it, w, full_bar, empty_bar);
     }
     // Take the consumer's last releases so no arrival is left pending.
-    for (uint32_t it = iters > kStages ? iters - kStages : 0; it < iters; ++it)
-      bar_sync(empty_bar + (int)(it % kStages));
+    for (uint32_t j = iters > kStages ? iters - kStages : 0; j < iters; ++j)
+      bar_sync(empty_bar + (int)(j % kStages));
     return;
   }
   // -------------------------------------------------------------- consumer
@@ -242,13 +326,13 @@ __global__ void __launch_bounds__(64 * kGroups)
 
 }  // namespace
 
-template <int G, int S, int R, int U = 64>
+template <int G, int S, int R, int U, int A>
 int launch_sha256_pipelined(const uint64_t *d_ptrs, const uint64_t *d_sizes,
                             int n, uint8_t *d_digests, uint32_t *d_state,
                             uint64_t c_begin, uint64_t c_end, cudaStream_t s) {
   if (n <= 0) return CASCADE_OK;
   const int blocks = (n + 32 * G - 1) / (32 * G);
-  sha256_pipelined<G, S, R, U><<<blocks, 64 * G, 0, s>>>(
+  sha256_pipelined<G, S, R, U, A><<<blocks, 64 * G, 0, s>>>(
       d_ptrs, d_sizes, n, reinterpret_cast<uint32_t *>(d_digests), 1u,
       0xffffffffu, d_state, c_begin, c_end);
   count_launches(1);
@@ -260,14 +344,15 @@ int launch_sha256_range(const uint64_t *d_ptrs, const uint64_t *d_sizes,
                         int n, uint8_t *d_digests, uint32_t *d_state,
                         uint64_t c_begin, uint64_t c_end, cudaStream_t s) {
   // While there are fewer producer/consumer pairs than SMs each chain runs
-  // alone on its SM and the latency-tuned round (both recurrences three
-  // operations deep) wins; once every scheduler has work, the ALU pipe is
-  // the limit and the round with the fewest ALU instructions wins.
+  // alone on its SM: the latency-tuned round (both recurrences three
+  // operations deep), all 64 rounds unrolled, and 8 chunks of loads in
+  // flight per lane.  Once every scheduler has work, the ALU pipe is the
+  // limit and the round with the fewest ALU instructions wins.
   if (n <= 32 * kSmCount)
-    return launch_sha256_pipelined<1, 4, 1, 16>(d_ptrs, d_sizes, n, d_digests,
-                                                d_state, c_begin, c_end, s);
-  return launch_sha256_pipelined<2, 3, 0, 16>(d_ptrs, d_sizes, n, d_digests,
-                                              d_state, c_begin, c_end, s);
+    return launch_sha256_pipelined<1, 4, 1, 64, 8>(
+        d_ptrs, d_sizes, n, d_digests, d_state, c_begin, c_end, s);
+  return launch_sha256_pipelined<2, 3, 0, 16, 0>(d_ptrs, d_sizes, n, d_digests,
+                                                 d_state, c_begin, c_end, s);
 }
 
 int launch_sha256(const uint64_t *d_ptrs, const uint64_t *d_sizes, int n,
