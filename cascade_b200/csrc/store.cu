@@ -132,6 +132,11 @@ struct Store {
   size_t oc_aux_cap = 0;
   int shard_rank = 0;            // this store's rank in the open batch
   size_t shard_open = 0;         // blocks of the open sharded batch
+  size_t shard_get_open = 0;     // keys of the open sharded get
+  // Pools of the other ranks mapped into this process (CUDA IPC); entry
+  // peer_rank is this store's own pool.
+  std::vector<uint8_t *> peer_base;
+  int peer_rank = -1;
   uint8_t *d_stage = nullptr;  // device staging for host buffers
   size_t d_stage_cap = 0;
   uint8_t *h_stage = nullptr;  // pinned staging for host buffers
@@ -985,9 +990,12 @@ static int upload_keys(Store &st, size_t n, const uint8_t *h_keys) {
 
 // Moves the found blocks (h_info) into device buffers out[i], decoding INT8
 // payloads.  deliver[i] = 0 skips a block.  Updates hit/miss counters and
-// promotes DRAM hits to HBM when the configuration asks for it.
+// promotes DRAM hits to HBM when the configuration asks for it.  HBM
+// payloads are read at pool + offset, or at bases[i] + offset when `bases`
+// is given (another rank's pool mapped into this process).
 static int deliver_locked(Store &st, size_t n, const uint64_t *out,
-                          const uint8_t *deliver) {
+                          const uint8_t *deliver,
+                          const uint64_t *bases = nullptr) {
   cudaStream_t s = st.s;
   // Copy jobs and dequantise jobs, packed into the scratch arrays:
   //   copies:  ptrs (src) / dst / eff_raw (bytes)
@@ -1015,7 +1023,7 @@ static int deliver_locked(Store &st, size_t n, const uint64_t *out,
     const bool q8 = (f.flags & kFlagQ8) != 0;
     uint64_t src;
     if (f.flags & kTierHbm) {
-      src = (uint64_t)(uintptr_t)st.pool + f.offset;
+      src = (bases ? bases[i] : (uint64_t)(uintptr_t)st.pool) + f.offset;
     } else {  // DRAM: bring the payload up first
       uint64_t pay = payload_bytes(f.size, q8);
       if (!q8) {
@@ -1330,11 +1338,20 @@ static int create_store(const cascade_config_t *cfg, Store **out) {
   return CASCADE_OK;
 }
 
+static void close_peer_pools(Store &st) {
+  for (size_t r = 0; r < st.peer_base.size(); ++r)
+    if ((int)r != st.peer_rank && st.peer_base[r])
+      cudaIpcCloseMemHandle(st.peer_base[r]);
+  st.peer_base.clear();
+  st.peer_rank = -1;
+}
+
 static void destroy_store(Store *st) {
   DeviceGuard g(st->dev);
   for (cudaStream_t q : {st->s, st->s2, st->s3})
     if (q) cudaStreamSynchronize(q);
   st->dram.reset();
+  close_peer_pools(*st);
   for (int c = 0; c < kNumClasses; ++c)
     if (st->stack_ptr[c]) cudaFree(st->stack_ptr[c]);
   if (st->pool) cudaFree(st->pool);
@@ -1787,6 +1804,185 @@ static int shard_end(Store &st, const uint8_t *d_back, size_t n,
   return finish_put(st, n, true, h_status, h_digests, n_stored);
 }
 
+// ------------------------------------------------------------ sharded get
+namespace {
+
+__global__ void shard_query_keys_kernel(int m,
+                                        const ShardQuery *__restrict__ in,
+                                        uint64_t *__restrict__ keys) {
+  const int j = blockIdx.x * blockDim.x + threadIdx.x;
+  if (j >= m) return;
+  keys[2 * (size_t)j] = in[j].k0;
+  keys[2 * (size_t)j + 1] = in[j].k1;
+}
+
+// Holder of a live entry: the rank recorded at put time when the payload
+// sits in another rank's pool, this rank otherwise.
+__global__ void shard_locate_kernel(int m, uint32_t rank,
+                                    const ShardQuery *__restrict__ in,
+                                    const LookupInfo *__restrict__ info,
+                                    ShardLocation *__restrict__ out) {
+  const int j = blockIdx.x * blockDim.x + threadIdx.x;
+  if (j >= m) return;
+  const LookupInfo f = info[j];
+  ShardLocation r;
+  r.src_idx = in[j].src_idx;
+  r.found = f.found;
+  r.flags = f.flags;
+  r.holder = (f.flags & kFlagRemote) ? ((f.flags >> 16) & 0xffu) : rank;
+  r.offset = f.offset;
+  r.size = f.size;
+  r.hdr_scale = f.hdr_scale;
+  r.hdr_zp = f.hdr_zp;
+  r.pad = 0;
+  out[j] = r;
+}
+
+}  // namespace
+
+static int shard_attach(Store &st, int world, int rank,
+                        const uint8_t *h_handles) {
+  CB_CHECK(world >= 1 && world <= 256 && rank >= 0 && rank < world,
+           CASCADE_ERR_INVALID, "bad world/rank");
+  CB_CHECK(st.hbm && st.pool, CASCADE_ERR_UNSUPPORTED,
+           "sharded gets need the HBM tier (use_gpu)");
+  close_peer_pools(st);
+  std::vector<uint8_t *> bases(world, nullptr);
+  for (int r = 0; r < world; ++r) {
+    if (r == rank) {
+      bases[r] = st.pool;
+      continue;
+    }
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, h_handles + (size_t)CASCADE_IPC_HANDLE_BYTES * r,
+                sizeof(h));
+    void *p = nullptr;
+    cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) {
+      for (int q = 0; q < r; ++q)
+        if (q != rank && bases[q]) cudaIpcCloseMemHandle(bases[q]);
+      return cuda_fail(e, "cudaIpcOpenMemHandle (peer pool)");
+    }
+    bases[r] = static_cast<uint8_t *>(p);
+  }
+  st.peer_base = std::move(bases);
+  st.peer_rank = rank;
+  return CASCADE_OK;
+}
+
+static int shard_get_begin(Store &st, size_t n, const uint8_t *h_keys,
+                           uint8_t *d_send, uint64_t *h_counts) {
+  const int world = (int)st.peer_base.size();
+  CB_CHECK(world > 0, CASCADE_ERR_INVALID,
+           "sharded get: attach the ranks' pools first");
+  std::vector<uint64_t> counts(world, 0), cursor(world, 0);
+  std::vector<int> owner(n);
+  for (size_t i = 0; i < n; ++i) {
+    owner[i] = owner_of(le64(h_keys + 16 * i), world);
+    ++counts[owner[i]];
+  }
+  for (int r = 1; r < world; ++r) cursor[r] = cursor[r - 1] + counts[r - 1];
+  int rc = ensure_host_stage(st, n * sizeof(ShardQuery));
+  if (rc) return rc;
+  ShardQuery *q = reinterpret_cast<ShardQuery *>(st.h_stage);
+  for (size_t i = 0; i < n; ++i) {
+    ShardQuery &r = q[cursor[owner[i]]++];
+    r.k0 = le64(h_keys + 16 * i);
+    r.k1 = le64(h_keys + 16 * i + 8);
+    r.src_idx = (uint32_t)i;
+    r.pad0 = 0;
+    r.pad1 = 0;
+  }
+  CB_CUDA(cudaMemcpyAsync(d_send, st.h_stage, n * sizeof(ShardQuery),
+                          cudaMemcpyHostToDevice, st.s));
+  CB_CUDA(cudaStreamSynchronize(st.s));
+  for (int r = 0; r < world; ++r) h_counts[r] = counts[r];
+  st.shard_get_open = n;
+  return CASCADE_OK;
+}
+
+static int shard_lookup(Store &st, const uint8_t *d_recv, size_t m,
+                        uint8_t *d_reply) {
+  CB_CHECK(st.peer_rank >= 0, CASCADE_ERR_INVALID,
+           "sharded get: attach the ranks' pools first");
+  if (m == 0) return CASCADE_OK;
+  Scratch &oc = st.oc;
+  int rc = ensure_scratch_of(st, oc, m);
+  if (rc) return rc;
+  cudaStream_t s = st.s;
+  const ShardQuery *in = reinterpret_cast<const ShardQuery *>(d_recv);
+  shard_query_keys_kernel<<<nblocks(m), 256, 0, s>>>((int)m, in, oc.keys);
+  count_launches(1);
+  CB_CUDA(cudaGetLastError());
+  const uint64_t epoch = st.next_epoch;
+  st.next_epoch += m;
+  rc = launch_index_lookup(st.slots, st.nslots - 1, oc.keys, 2, (int)m, 1,
+                           epoch, oc.info, s);
+  if (rc) return rc;
+  shard_locate_kernel<<<nblocks(m), 256, 0, s>>>(
+      (int)m, (uint32_t)st.peer_rank, in, oc.info,
+      reinterpret_cast<ShardLocation *>(d_reply));
+  count_launches(1);
+  CB_CUDA(cudaGetLastError());
+  CB_CUDA(cudaStreamSynchronize(s));
+  return CASCADE_OK;
+}
+
+static int shard_get_end(Store &st, const uint8_t *d_back, size_t n,
+                         const uint64_t *h_out, const uint64_t *h_caps,
+                         uint64_t *h_sizes, uint8_t *h_found,
+                         uint64_t *n_found) {
+  CB_CHECK(st.shard_get_open == n, CASCADE_ERR_INVALID,
+           "shard_get_end: no open get of this size");
+  st.shard_get_open = 0;
+  int rc = ensure_scratch(st, n);
+  if (!rc) rc = ensure_host_stage(st, n * sizeof(ShardLocation));
+  if (rc) return rc;
+  CB_CUDA(cudaMemcpyAsync(st.h_stage, d_back, n * sizeof(ShardLocation),
+                          cudaMemcpyDeviceToHost, st.s));
+  CB_CUDA(cudaStreamSynchronize(st.s));
+  const ShardLocation *loc = reinterpret_cast<const ShardLocation *>(st.h_stage);
+  const int world = (int)st.peer_base.size();
+  std::vector<uint8_t> seen(n, 0), deliver(n, 0);
+  std::vector<uint64_t> bases(n, 0);
+  uint64_t found = 0;
+  for (size_t j = 0; j < n; ++j) {
+    const ShardLocation &r = loc[j];
+    CB_CHECK(r.src_idx < n && !seen[r.src_idx], CASCADE_ERR_INVALID,
+             "shard_get_end: the locations do not name each key once");
+    seen[r.src_idx] = 1;
+    LookupInfo &f = st.sc.h_info[r.src_idx];
+    f.found = r.found;
+    f.flags = r.flags;
+    f.offset = r.offset;
+    f.size = r.size;
+    f.hdr_scale = r.hdr_scale;
+    f.hdr_zp = r.hdr_zp;
+    f.slot = kNoSlot;
+    f.pad = 0;
+    if (!r.found) continue;
+    const bool local = (int)r.holder == st.peer_rank;
+    CB_CHECK((int)r.holder < world, CASCADE_ERR_INVALID,
+             "shard_get_end: holder rank out of range");
+    CB_CHECK(local || (r.flags & kTierHbm), CASCADE_ERR_UNSUPPORTED,
+             "sharded get: the block is in another rank's DRAM tier");
+    bases[r.src_idx] = (uint64_t)(uintptr_t)st.peer_base[r.holder];
+  }
+  for (size_t i = 0; i < n; ++i) {
+    const LookupInfo &f = st.sc.h_info[i];
+    const uint64_t size =
+        f.found ? ((f.flags & kFlagQ8) ? 2 * (f.size / 2) : f.size) : 0;
+    if (h_sizes) h_sizes[i] = size;
+    if (h_found) h_found[i] = f.found ? 1 : 0;
+    found += f.found ? 1 : 0;
+    deliver[i] = (!f.found || size <= h_caps[i]) ? 1 : 0;
+  }
+  if (n_found) *n_found = found;
+  // A DRAM hit can only be local here; it is read (and promoted) from this
+  // store's own arena.
+  return deliver_locked(st, n, h_out, deliver.data(), bases.data());
+}
+
 }  // namespace cb
 
 // ------------------------------------------------------------------ C-ABI
@@ -2050,4 +2246,71 @@ extern "C" int cascade_shard_put_end(cascade_store_t *s, const uint8_t *d_back,
   CB_CHECK(d_back, CASCADE_ERR_INVALID, "null argument");
   if (int rc = join_caller(st, stream)) return rc;
   return cb::shard_end(st, d_back, n, h_status, h_digests, n_stored);
+}
+
+extern "C" int cascade_shard_pool_handle(cascade_store_t *s,
+                                         uint8_t *h_handle) {
+  STORE_ENTRY(s);
+  CB_CHECK(h_handle, CASCADE_ERR_INVALID, "null argument");
+  CB_CHECK(st.hbm && st.pool, CASCADE_ERR_UNSUPPORTED,
+           "sharded gets need the HBM tier (use_gpu)");
+  static_assert(sizeof(cudaIpcMemHandle_t) == CASCADE_IPC_HANDLE_BYTES,
+                "IPC handle size");
+  cudaIpcMemHandle_t h;
+  CB_CUDA(cudaIpcGetMemHandle(&h, st.pool));
+  std::memcpy(h_handle, &h, sizeof(h));
+  return CASCADE_OK;
+}
+
+extern "C" int cascade_shard_attach_pools(cascade_store_t *s, int world,
+                                          int rank, const uint8_t *h_handles) {
+  STORE_ENTRY(s);
+  CB_CHECK(h_handles, CASCADE_ERR_INVALID, "null argument");
+  return cb::shard_attach(st, world, rank, h_handles);
+}
+
+extern "C" int cascade_shard_detach_pools(cascade_store_t *s) {
+  STORE_ENTRY(s);
+  CB_CUDA(cudaStreamSynchronize(st.s));
+  cb::close_peer_pools(st);
+  return CASCADE_OK;
+}
+
+extern "C" int cascade_shard_get_begin(cascade_store_t *s, size_t n,
+                                       const uint8_t *h_keys, uint8_t *d_send,
+                                       uint64_t *h_send_counts, void *stream) {
+  STORE_ENTRY(s);
+  CB_CHECK(h_send_counts && (n == 0 || (h_keys && d_send)),
+           CASCADE_ERR_INVALID, "null argument");
+  CB_CHECK(n <= (size_t)INT32_MAX, CASCADE_ERR_INVALID, "batch too large");
+  if (int rc = join_caller(st, stream)) return rc;
+  return cb::shard_get_begin(st, n, h_keys, d_send, h_send_counts);
+}
+
+extern "C" int cascade_shard_lookup(cascade_store_t *s, const uint8_t *d_recv,
+                                    size_t m, uint8_t *d_reply, void *stream) {
+  STORE_ENTRY(s);
+  CB_CHECK(m == 0 || (d_recv && d_reply), CASCADE_ERR_INVALID,
+           "null argument");
+  CB_CHECK(m <= (size_t)INT32_MAX, CASCADE_ERR_INVALID, "batch too large");
+  if (int rc = join_caller(st, stream)) return rc;
+  return cb::shard_lookup(st, d_recv, m, d_reply);
+}
+
+extern "C" int cascade_shard_get_end(cascade_store_t *s, const uint8_t *d_back,
+                                     size_t n, const uint64_t *h_out_ptrs,
+                                     const uint64_t *h_out_caps,
+                                     uint64_t *h_sizes, uint8_t *h_found,
+                                     uint64_t *n_found, void *stream) {
+  STORE_ENTRY(s);
+  if (n_found) *n_found = 0;
+  CB_CHECK(n == 0 || (d_back && h_out_ptrs && h_out_caps),
+           CASCADE_ERR_INVALID, "null argument");
+  if (int rc = join_caller(st, stream)) return rc;
+  if (n == 0) {
+    st.shard_get_open = 0;
+    return CASCADE_OK;
+  }
+  return cb::shard_get_end(st, d_back, n, h_out_ptrs, h_out_caps, h_sizes,
+                           h_found, n_found);
 }

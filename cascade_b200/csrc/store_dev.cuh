@@ -55,6 +55,29 @@ struct ShardRecord {
 };
 static_assert(sizeof(ShardRecord) == 64, "shard record layout");
 
+// Sharded get: a key routed to its owner rank.
+struct ShardQuery {
+  uint64_t k0, k1;     // key: digest bytes 0..15, little-endian
+  uint32_t src_idx;    // position of the key in the requester's batch
+  uint32_t pad0;
+  uint64_t pad1;
+};
+static_assert(sizeof(ShardQuery) == 32, "shard query layout");
+
+// The owner's answer to a query: where the block lives.
+struct ShardLocation {
+  uint32_t src_idx;
+  uint32_t found;      // 1 when the key is live
+  uint32_t flags;      // SlotFlags of the stored copy
+  uint32_t holder;     // rank whose pool holds the payload
+  uint64_t offset;     // payload offset in the holder's pool
+  uint64_t size;       // logical block size
+  uint32_t hdr_scale;  // INT8 header
+  uint32_t hdr_zp;
+  uint64_t pad;
+};
+static_assert(sizeof(ShardLocation) == 48, "shard location layout");
+
 struct ShardReply {
   uint32_t src_idx;
   uint32_t status;     // CASCADE_PUT_*

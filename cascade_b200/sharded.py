@@ -18,8 +18,16 @@ batch is exact at once:
 4. the 8-byte replies return in a second all-to-all and each rank frees the
    slots of its duplicates (``cascade_shard_put_end``).
 
-Block payloads never leave the rank that produced them.  Every rank must
-call ``put_batch`` the same number of times, in the same order.
+Block payloads never leave the rank that produced them until they are read.
+``get_batch`` reads any block from any rank (the reference's remote read,
+DistributedStore::get, distributed_backend.cpp:673-767): keys go to their
+owners in one all-to-all, each owner answers with the block's location
+(holder rank, pool offset, size, INT8 header), and each rank copies or
+dequantises the payloads straight out of the holders' HBM pools, which every
+rank maps at construction (CUDA IPC; the reads cross NVLink).
+
+Every rank must call ``put_batch``, ``get_batch``, ``clear`` and ``close``
+the same number of times, in the same order.
 """
 from __future__ import annotations
 
@@ -35,6 +43,9 @@ from .cascade_cpp import CascadeConfig, CascadeStore, _cuda_u8
 
 RECORD_BYTES = 64
 REPLY_BYTES = 8
+QUERY_BYTES = 32
+LOCATION_BYTES = 48
+IPC_HANDLE_BYTES = 64
 
 _vp = ctypes.c_void_p
 _sz = ctypes.c_size_t
@@ -45,6 +56,13 @@ _lib.register("cascade_shard_put_begin", _int,
 _lib.register("cascade_shard_resolve", _int, [_vp, _vp, _sz, _vp, _vp])
 _lib.register("cascade_shard_put_end", _int,
               [_vp, _vp, _sz, _vp, _vp, ctypes.POINTER(_u64), _vp])
+_lib.register("cascade_shard_pool_handle", _int, [_vp, _vp])
+_lib.register("cascade_shard_attach_pools", _int, [_vp, _int, _int, _vp])
+_lib.register("cascade_shard_detach_pools", _int, [_vp])
+_lib.register("cascade_shard_get_begin", _int, [_vp, _sz, _vp, _vp, _vp, _vp])
+_lib.register("cascade_shard_lookup", _int, [_vp, _vp, _sz, _vp, _vp])
+_lib.register("cascade_shard_get_end", _int,
+              [_vp, _vp, _sz, _vp, _vp, _vp, _vp, ctypes.POINTER(_u64), _vp])
 
 
 class CudaShardOps:
@@ -113,6 +131,70 @@ class CudaShardOps:
         self._keep = None
         return int(stored.value), status, digests
 
+    # ---------------------------------------------------------------- get
+    def key(self, block_id) -> bytes:
+        return self.store._key(block_id)
+
+    def pool_handle(self) -> bytes:
+        buf = (ctypes.c_uint8 * IPC_HANDLE_BYTES)()
+        check(_lib.load().cascade_shard_pool_handle(self.store._h, buf))
+        return bytes(buf)
+
+    def attach(self, world, rank, handles: bytes):
+        check(_lib.load().cascade_shard_attach_pools(
+            self.store._h, world, rank, handles))
+
+    def detach(self):
+        check(_lib.load().cascade_shard_detach_pools(self.store._h))
+
+    def get_begin(self, keys: bytes, world):
+        import torch
+        n = len(keys) // 16
+        send = torch.empty((n, QUERY_BYTES), dtype=torch.uint8,
+                           device=self.device)
+        counts = np.zeros(world, dtype=np.uint64)
+        kbuf = np.frombuffer(keys, np.uint8) if n else None
+        check(_lib.load().cascade_shard_get_begin(
+            self.store._h, n, kbuf.ctypes.data if n else None,
+            send.data_ptr() if n else None, counts.ctypes.data,
+            self._stream()))
+        return send, [int(c) for c in counts]
+
+    def lookup(self, recv):
+        import torch
+        m = recv.shape[0]
+        reply = torch.empty((m, LOCATION_BYTES), dtype=torch.uint8,
+                            device=self.device)
+        check(_lib.load().cascade_shard_lookup(
+            self.store._h, recv.data_ptr() if m else None, m,
+            reply.data_ptr() if m else None, self._stream()))
+        return reply
+
+    def get_end(self, back, outs):
+        import torch
+        if isinstance(outs, torch.Tensor) and outs.dim() == 2:
+            if not outs.is_contiguous() or outs.device != self.device:
+                raise ValueError("outs: a contiguous 2-D tensor on this GPU")
+            n = outs.shape[0]
+            row = outs.stride(0) * outs.element_size()
+            ptrs = (np.arange(n, dtype=np.uint64) * np.uint64(row)
+                    + np.uint64(outs.data_ptr()))
+            caps = np.full(n, outs.shape[1] * outs.element_size(), np.uint64)
+        else:
+            outs = [_cuda_u8(o) for o in outs]
+            n = len(outs)
+            ptrs = np.array([o.data_ptr() for o in outs], dtype=np.uint64)
+            caps = np.array([o.numel() for o in outs], dtype=np.uint64)
+        sizes = np.zeros(n, np.uint64)
+        found = np.zeros(n, np.uint8)
+        nf = _u64(0)
+        check(_lib.load().cascade_shard_get_end(
+            self.store._h, back.data_ptr() if n else None, n,
+            ptrs.ctypes.data if n else None, caps.ctypes.data if n else None,
+            sizes.ctypes.data if n else None, found.ctypes.data if n else None,
+            ctypes.byref(nf), self._stream()))
+        return found, sizes
+
 
 class ShardedCascadeStore:
     """One rank's view of a store whose dedup index is sharded by key over
@@ -130,6 +212,22 @@ class ShardedCascadeStore:
         self.ops = ops
         self._next_seq = 1
         self._lock = threading.Lock()
+        self._attached = False
+        self._attach()
+
+    def _attach(self):
+        """Collective: every rank maps the other ranks' pools."""
+        import torch
+        import torch.distributed as dist
+        if not hasattr(self.ops, "attach"):
+            return
+        mine = torch.frombuffer(bytearray(self.ops.pool_handle()),
+                                dtype=torch.uint8).to(self.ops.device)
+        every = [torch.empty_like(mine) for _ in range(self.world)]
+        dist.all_gather(every, mine, group=self.group)
+        handles = b"".join(bytes(t.cpu().numpy().tobytes()) for t in every)
+        self.ops.attach(self.world, self.rank, handles)
+        self._attached = True
 
     def put_batch(self, blocks: Sequence, is_prefix=None,
                   return_status: bool = False):
@@ -168,6 +266,55 @@ class ShardedCascadeStore:
         if return_status:
             return stored, status, digests
         return stored
+
+    def get_batch(self, ids, outs):
+        """Collective: every rank reads its own list of blocks (any rank may
+        hold them) into its output buffers on this rank's GPU: a list of
+        CUDA tensors, or one 2-D CUDA tensor with a block per row.  Returns
+        (found[n] uint8, sizes[n] uint64) as CascadeStore.get_batch: a block
+        larger than its output is reported with its size and not written.
+        ``ids``: content ids (32 hex characters) or 16-byte keys, or all the
+        keys at once as a uint8 array of shape (n, 16)."""
+        import torch
+        import torch.distributed as dist
+        if isinstance(ids, np.ndarray) and ids.dtype == np.uint8 \
+                and ids.ndim == 2 and ids.shape[1] == 16:
+            keys = np.ascontiguousarray(ids).tobytes()
+        else:
+            keys = b"".join(self.ops.key(k) for k in ids)
+        n_out = outs.shape[0] if isinstance(outs, torch.Tensor) else len(outs)
+        if len(keys) // 16 != n_out:
+            raise ValueError("one output per id")
+        with self._lock:
+            dev = self.ops.device
+            send, send_splits = self.ops.get_begin(keys, self.world)
+            sc = torch.tensor(send_splits, dtype=torch.int64, device=dev)
+            rc = torch.empty(self.world, dtype=torch.int64, device=dev)
+            dist.all_to_all_single(rc, sc, group=self.group)
+            recv_splits = [int(x) for x in rc.tolist()]
+            recv = torch.empty((sum(recv_splits), QUERY_BYTES),
+                               dtype=torch.uint8, device=dev)
+            dist.all_to_all_single(recv, send, recv_splits, send_splits,
+                                   group=self.group)
+            reply = self.ops.lookup(recv)
+            back = torch.empty((n_out, LOCATION_BYTES), dtype=torch.uint8,
+                               device=dev)
+            dist.all_to_all_single(back, reply, send_splits, recv_splits,
+                                   group=self.group)
+            # Synchronous: the reads of the peers' pools are complete when
+            # this returns, and clear() / close() start with a barrier, so
+            # no pool is reset or unmapped while another rank reads it.
+            found, sizes = self.ops.get_end(back, outs)
+        return found, sizes
+
+    def close(self):
+        """Collective: unmaps the other ranks' pools on every rank, then
+        synchronises, so that no rank frees a pool another rank can read."""
+        import torch.distributed as dist
+        if self._attached:
+            self.ops.detach()
+            self._attached = False
+        dist.barrier(group=self.group)
 
     def get_stats(self):
         return self.ops.store.get_stats()

@@ -275,6 +275,50 @@ int cascade_shard_put_end(cascade_store_t *s, const uint8_t *d_back,
                           size_t n, uint8_t *h_status, uint8_t *h_digests,
                           uint64_t *n_stored, void *stream);
 
+/* Sharded get: any rank reads any block of the sharded store.  The
+ * reference reads a block another node holds through DistributedStore::get
+ * (distributed_backend.cpp:673-767: local tiers, then the global location
+ * table and a read of the holder's DRAM shadow).
+ * Here the payload never leaves the holder's HBM pool until it is read:
+ * every rank maps the other ranks' pools once (CUDA IPC, peer access over
+ * NVLink), and a get is three calls around two all-to-all exchanges:
+ *   get_begin: route each 16-byte key to its owner: one 32-byte query per
+ *              key in d_send, grouped by owner rank;
+ *   lookup:    as owner, look the received keys up in this rank's slice of
+ *              the index (touching their LRU epochs) and write one 48-byte
+ *              location per query (found, holder rank, offset, size, INT8
+ *              header);
+ *   get_end:   take the locations of this rank's keys (in any order) and
+ *              copy or dequantise each block from its holder's pool (this
+ *              GPU's own or a peer's) into h_out_ptrs[i]; sizes, found
+ *              flags and gpu_hits / misses as in cascade_store_get_batch.
+ * cascade_shard_attach_pools must have run on every rank first.  Blocks of
+ * a sharded store live in HBM (a sharded put needs the whole batch to fit
+ * there); a block found in another rank's DRAM tier is an error. */
+#define CASCADE_SHARD_QUERY_BYTES 32
+#define CASCADE_SHARD_LOCATION_BYTES 48
+#define CASCADE_IPC_HANDLE_BYTES 64
+
+/* This store's HBM pool as a CUDA IPC handle (64 bytes). */
+int cascade_shard_pool_handle(cascade_store_t *s, uint8_t *h_handle);
+/* Maps the pools of the other ranks: h_handles holds world handles, one per
+ * rank in rank order (this rank's own is not opened).  Mappings are closed
+ * by cascade_shard_detach_pools or when the store is destroyed.  A rank
+ * must not free its store while another rank can still read its pool: have
+ * every rank detach, then synchronise the ranks, then destroy. */
+int cascade_shard_attach_pools(cascade_store_t *s, int world, int rank,
+                               const uint8_t *h_handles);
+int cascade_shard_detach_pools(cascade_store_t *s);
+int cascade_shard_get_begin(cascade_store_t *s, size_t n,
+                            const uint8_t *h_keys, uint8_t *d_send,
+                            uint64_t *h_send_counts, void *stream);
+int cascade_shard_lookup(cascade_store_t *s, const uint8_t *d_recv, size_t m,
+                         uint8_t *d_reply, void *stream);
+int cascade_shard_get_end(cascade_store_t *s, const uint8_t *d_back,
+                          size_t n, const uint64_t *h_out_ptrs,
+                          const uint64_t *h_out_caps, uint64_t *h_sizes,
+                          uint8_t *h_found, uint64_t *n_found, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

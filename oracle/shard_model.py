@@ -1,12 +1,14 @@
 """ORACLE — test infrastructure only.
 
-CPU stand-in for the three per-rank steps of the sharded PUT
-(cascade_b200.sharded.CudaShardOps), with the same 64-byte record and
-8-byte reply layouts, so the exchange protocol of ShardedCascadeStore can
-be run on CPU ranks (gloo).  The dedup decision restates the reference's
-rule (CascadeStore::put, cascade_core.cpp:1077-1080, applied to puts in
-global (rank, block) order): a key already stored is a hit; among new keys
-the first put stores and later ones are hits.
+CPU stand-in for the per-rank steps of the sharded PUT and GET
+(cascade_b200.sharded.CudaShardOps), with the same 64-byte record, 8-byte
+reply, 32-byte query and 48-byte location layouts, so the exchange protocol
+of ShardedCascadeStore can be run on CPU ranks (gloo).  The dedup decision
+restates the reference's rule (CascadeStore::put, cascade_core.cpp:1077-1080,
+applied to puts in global (rank, block) order): a key already stored is a
+hit; among new keys the first put stores and later ones are hits.  For the
+GET, a directory shared by the ranks stands in for the holders' HBM pools
+(each holder writes the blocks it stored there, one file per key).
 """
 from __future__ import annotations
 
@@ -20,7 +22,14 @@ REC = np.dtype([("k0", "<u8"), ("k1", "<u8"), ("seq", "<u8"),
                 ("holder", "<u4"), ("src_idx", "<u4"), ("hdr_scale", "<u4"),
                 ("hdr_zp", "<u4"), ("pad", "<u4")])
 REPLY = np.dtype([("src_idx", "<u4"), ("status", "<u4")])
+QUERY = np.dtype([("k0", "<u8"), ("k1", "<u8"), ("src_idx", "<u4"),
+                  ("pad0", "<u4"), ("pad1", "<u8")])
+LOCATION = np.dtype([("src_idx", "<u4"), ("found", "<u4"), ("flags", "<u4"),
+                     ("holder", "<u4"), ("offset", "<u8"), ("size", "<u8"),
+                     ("hdr_scale", "<u4"), ("hdr_zp", "<u4"), ("pad", "<u8")])
 assert REC.itemsize == 64 and REPLY.itemsize == 8
+assert QUERY.itemsize == 32 and LOCATION.itemsize == 48
+TIER_HBM, FLAG_REMOTE = 1 << 2, 1 << 4
 
 
 def owner_of(digest: bytes, world: int) -> int:
@@ -28,11 +37,16 @@ def owner_of(digest: bytes, world: int) -> int:
 
 
 class CpuShardOps:
-    def __init__(self):
+    def __init__(self, shared_dir=None):
         import torch
         self.device = torch.device("cpu")
-        self.index = {}        # this rank's key slice: key -> seq of storer
+        self.index = {}        # this rank's key slice: key -> (seq, holder, size)
         self._digests = None
+        self._blocks = None
+        self._rank = None
+        self._world = None
+        self._get_keys = None
+        self.shared_dir = shared_dir
         self.store = None
 
     def begin(self, blocks, is_prefix, world, rank, seq_base):
@@ -55,6 +69,7 @@ class CpuShardOps:
         counts = np.bincount(owners, minlength=world).tolist()
         send = torch.from_numpy(recs[order].view(np.uint8).reshape(n, 64).copy())
         self._digests = digests
+        self._blocks = [np.ascontiguousarray(b) for b in blocks]
         return send, counts
 
     def resolve(self, recv):
@@ -70,7 +85,8 @@ class CpuShardOps:
             elif key in seen:
                 status[j] = DUP_BATCH
             else:
-                seen[key] = int(recs[j]["seq"])
+                seen[key] = (int(recs[j]["seq"]), int(recs[j]["holder"]),
+                             int(recs[j]["size"]))
                 status[j] = STORED
         self.index.update(seen)
         rep = np.zeros(m, REPLY)
@@ -86,7 +102,85 @@ class CpuShardOps:
         digests = np.frombuffer(b"".join(self._digests), np.uint8).reshape(n, 32) \
             if n else np.zeros((0, 32), np.uint8)
         stored = int((status != FAILED).sum())
+        if self.shared_dir is not None:   # this rank now holds these
+            import os
+            for i in np.nonzero(status == STORED)[0]:
+                name = self._digests[i][:16].hex() + ".bin"
+                with open(os.path.join(self.shared_dir, name), "wb") as f:
+                    f.write(self._blocks[i].tobytes())
+        self._blocks = None
         return stored, status, digests
+
+    # ---------------------------------------------------------------- get
+    def key(self, block_id) -> bytes:
+        if isinstance(block_id, (bytes, bytearray)) and len(block_id) == 16:
+            return bytes(block_id)
+        return bytes.fromhex(block_id)
+
+    def pool_handle(self) -> bytes:
+        import torch.distributed as dist
+        return bytes([dist.get_rank()]) * 64
+
+    def attach(self, world, rank, handles: bytes):
+        assert handles == b"".join(bytes([r]) * 64 for r in range(world))
+        self._world, self._rank = world, rank
+
+    def detach(self):
+        self._world = self._rank = None
+
+    def get_begin(self, keys: bytes, world):
+        import torch
+        n = len(keys) // 16
+        q = np.zeros(n, QUERY)
+        owners = np.zeros(n, np.int64)
+        for i in range(n):
+            k = keys[16 * i:16 * i + 16]
+            q[i]["k0"] = int.from_bytes(k[:8], "little")
+            q[i]["k1"] = int.from_bytes(k[8:], "little")
+            q[i]["src_idx"] = i
+            owners[i] = owner_of(k, world)
+        order = np.argsort(owners, kind="stable")
+        counts = np.bincount(owners, minlength=world).tolist()
+        self._get_keys = [keys[16 * i:16 * i + 16] for i in range(n)]
+        return torch.from_numpy(q[order].view(np.uint8).reshape(n, 32).copy()), counts
+
+    def lookup(self, recv):
+        import torch
+        q = recv.numpy().reshape(-1).view(QUERY) if recv.numel() else np.zeros(0, QUERY)
+        loc = np.zeros(len(q), LOCATION)
+        for j, r in enumerate(q):
+            loc[j]["src_idx"] = r["src_idx"]
+            hit = self.index.get((int(r["k0"]), int(r["k1"])))
+            if hit is None:
+                continue
+            _, holder, size = hit
+            loc[j]["found"] = 1
+            loc[j]["holder"] = holder
+            loc[j]["size"] = size
+            loc[j]["flags"] = TIER_HBM | (FLAG_REMOTE if holder != self._rank else 0)
+        return torch.from_numpy(loc.view(np.uint8).reshape(len(q), 48).copy())
+
+    def get_end(self, back, outs):
+        import os
+        loc = back.numpy().reshape(-1).view(LOCATION) if back.numel() else np.zeros(0, LOCATION)
+        n = len(outs)
+        found = np.zeros(n, np.uint8)
+        sizes = np.zeros(n, np.uint64)
+        assert sorted(loc["src_idx"].tolist()) == list(range(n))
+        for r in loc:
+            i = int(r["src_idx"])
+            if not r["found"]:
+                continue
+            found[i] = 1
+            sizes[i] = r["size"]
+            if r["size"] > len(outs[i]):
+                continue
+            name = self._get_keys[i].hex() + ".bin"
+            with open(os.path.join(self.shared_dir, name), "rb") as f:
+                data = np.frombuffer(f.read(), np.uint8)
+            assert len(data) == r["size"]
+            outs[i][:len(data)] = data
+        return found, sizes
 
 
 def serial_statuses(blocks_by_rank):

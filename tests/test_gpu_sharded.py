@@ -1,6 +1,10 @@
 """Sharded dedup on real GPUs (one process per GPU, NCCL): statuses equal
 serial puts in (rank, block) order, hits total N - #distinct, and each rank
-keeps exactly the bytes of the blocks it stored.  Needs two GPUs."""
+keeps exactly the bytes of the blocks it stored.  Then every rank reads
+every block, most of them held in the other GPU's pool (peer reads over
+NVLink), and gets the stored bytes back: exactly, or, with INT8 HBM
+blocks, the oracle's compress -> decompress of them.  Needs two GPUs."""
+import hashlib
 import json
 import os
 import socket
@@ -28,7 +32,15 @@ def _blocks(rank, batch):
     return [pool[p] if p < 48 else own[p - 48] for p in picks]
 
 
-def _rank_main(rank, world, port, out_dir):
+def _get_ids(world):
+    ids = []
+    for r in range(world):
+        for b in _blocks(r, 0):
+            ids.append(hashlib.sha256(b.tobytes()).hexdigest()[:32])
+    return ids + ["cd" * 16]
+
+
+def _rank_main(rank, world, port, out_dir, q8):
     import datetime
 
     import torch.distributed as dist
@@ -46,6 +58,8 @@ def _rank_main(rank, world, port, out_dir):
         cfg.gpu_device_id = rank
         cfg.gpu_capacity_bytes = 256 << 20
         cfg.shm_capacity_bytes = 0
+        cfg.kv_compression = q8
+        cfg.gpu_q8 = q8
         store = ShardedCascadeStore(cfg)
         res = []
         for batch in range(2):
@@ -56,6 +70,26 @@ def _rank_main(rank, world, port, out_dir):
                         "digests": [d.tobytes().hex() for d in digests]})
         s = store.get_stats()
         res.append({"gpu_used": s.gpu_used, "dedup_hits": s.dedup_hits})
+        ids = _get_ids(world)
+        # first read: a list of outputs (one of them too small) and hex ids;
+        # second read: one 2-D output tensor and the keys as an (n, 16) array
+        outs = [torch.zeros(65536, dtype=torch.uint8, device=dev)
+                for _ in ids]
+        outs[rank] = torch.zeros(100, dtype=torch.uint8, device=dev)
+        found, sizes = store.get_batch(ids, outs)
+        res.append({"found": found.tolist(), "sizes": sizes.tolist(),
+                    "sha": [hashlib.sha256(o.cpu().numpy().tobytes())
+                            .hexdigest() for o in outs]})
+        keys = np.frombuffer(b"".join(bytes.fromhex(k) for k in ids),
+                             np.uint8).reshape(-1, 16)
+        rows = torch.zeros((len(ids), 65536), dtype=torch.uint8, device=dev)
+        found, sizes = store.get_batch(keys, rows)
+        res.append({"found": found.tolist(), "sizes": sizes.tolist(),
+                    "sha": [hashlib.sha256(r.cpu().numpy().tobytes())
+                            .hexdigest() for r in rows]})
+        s = store.get_stats()
+        res.append({"gpu_hits": s.gpu_hits, "misses": s.misses})
+        store.close()
         with open(os.path.join(out_dir, f"r{rank}.json"), "w") as f:
             json.dump(res, f)
         dist.barrier()
@@ -64,11 +98,12 @@ def _rank_main(rank, world, port, out_dir):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < WORLD, reason="needs 2 GPUs")
-def test_sharded_put_two_gpus(tmp_path):
-    import hashlib
-
+@pytest.mark.parametrize("q8", [False, True], ids=["raw", "int8"])
+def test_sharded_put_get_two_gpus(tmp_path, q8):
     import torch.multiprocessing as mp
-    mp.spawn(_rank_main, args=(WORLD, _free_port(), str(tmp_path)),
+
+    import oracle
+    mp.spawn(_rank_main, args=(WORLD, _free_port(), str(tmp_path), q8),
              nprocs=WORLD, join=True)
     res = [json.load(open(tmp_path / f"r{r}.json")) for r in range(WORLD)]
     known = set()
@@ -87,5 +122,26 @@ def test_sharded_put_two_gpus(tmp_path):
                 total_hits += hit
                 stored_bytes[r] += 0 if hit else b.size
             assert got["stored"] == len(blocks)
-    assert sum(r[-1]["dedup_hits"] for r in res) == total_hits
-    assert [r[-1]["gpu_used"] for r in res] == stored_bytes
+    assert sum(r[2]["dedup_hits"] for r in res) == total_hits
+    want_used = [b // 2 for b in stored_bytes] if q8 else stored_bytes
+    assert [r[2]["gpu_used"] for r in res] == want_used
+    # reads: every block of batch 0 from both ranks, plus a missing id
+    ids = _get_ids(WORLD)
+    blocks = {hashlib.sha256(b.tobytes()).hexdigest()[:32]: b
+              for r in range(WORLD) for b in _blocks(r, 0)}
+    for rank in range(WORLD):
+        for rep, got in enumerate(res[rank][3:5]):
+            assert got["found"] == [1] * (len(ids) - 1) + [0]
+            assert got["sizes"] == [65536] * (len(ids) - 1) + [0]
+            for i, k in enumerate(ids[:-1]):
+                if i == rank and rep == 0:   # 100-byte buffer: untouched
+                    assert got["sha"][i] == hashlib.sha256(bytes(100)).hexdigest()
+                    continue
+                b = blocks[k]
+                want = oracle.kv_decompress(oracle.kv_compress(b), b.size) \
+                    if q8 else b
+                assert got["sha"][i] == hashlib.sha256(
+                    np.ascontiguousarray(want).tobytes()).hexdigest(), (rank, i)
+        hits = res[rank][5]      # the block that did not fit is no hit
+        assert hits["gpu_hits"] == 2 * (len(ids) - 1) - 1
+        assert hits["misses"] == 2

@@ -2,6 +2,7 @@
 two CPU ranks over gloo, with the per-rank steps done by the oracle's CPU
 stand-in: every rank's statuses must equal serial puts in (rank, block)
 order, and the hit total must be N - #distinct."""
+import hashlib
 import json
 import os
 import socket
@@ -29,6 +30,14 @@ def _blocks(rank, batch):
     return [pool[p] if p < 24 else own[p - 24] for p in picks]
 
 
+def _get_ids(world):
+    ids = []
+    for r in range(world):
+        for b in _blocks(r, 0):
+            ids.append(hashlib.sha256(b.tobytes()).hexdigest()[:32])
+    return ids + ["ab" * 16]
+
+
 def _rank_main(rank, world, port, out_dir):
     import torch.distributed as dist
     from cascade_b200.sharded import ShardedCascadeStore
@@ -37,12 +46,22 @@ def _rank_main(rank, world, port, out_dir):
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
-        store = ShardedCascadeStore(ops=CpuShardOps())
+        store = ShardedCascadeStore(ops=CpuShardOps(shared_dir=out_dir))
         res = []
         for batch in range(2):
             stored, status, digests = store.put_batch(_blocks(rank, batch),
                                                       return_status=True)
             res.append({"stored": stored, "status": status.tolist()})
+        # every rank reads every block of batch 0 (held on any rank), an id
+        # that was never stored, and one block into a too-small buffer
+        ids = _get_ids(world)
+        outs = [np.zeros(300, np.uint8) for _ in ids]
+        outs[rank] = np.zeros(10, np.uint8)
+        found, sizes = store.get_batch(ids, outs)
+        res.append({"found": found.tolist(), "sizes": sizes.tolist(),
+                    "sha": [hashlib.sha256(o.tobytes()).hexdigest()
+                            for o in outs]})
+        store.close()
         with open(os.path.join(out_dir, f"r{rank}.json"), "w") as f:
             json.dump(res, f)
     finally:
@@ -60,7 +79,6 @@ def test_sharded_exchange_matches_serial_puts(tmp_path, world):
         blocks = [_blocks(r, batch) for r in range(world)]
         # serial outcome across batches: earlier batches count as known
         want = []
-        import hashlib
         known = set(all_keys)
         for r in range(world):
             st = []
@@ -89,3 +107,22 @@ def test_serial_model_helper():
     a = [np.zeros(4, np.uint8), np.ones(4, np.uint8)]
     b = [np.ones(4, np.uint8), np.full(4, 2, np.uint8)]
     assert serial_statuses([a, b]) == [[STORED, STORED], [DUP_KNOWN, STORED]]
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_sharded_get_reads_blocks_held_on_any_rank(tmp_path, world):
+    mp.spawn(_rank_main, args=(world, _free_port(), str(tmp_path)),
+             nprocs=world, join=True)
+    ids = _get_ids(world)
+    blocks = {hashlib.sha256(b.tobytes()).hexdigest()[:32]: b
+              for r in range(world) for b in _blocks(r, 0)}
+    for rank in range(world):
+        got = json.load(open(tmp_path / f"r{rank}.json"))[-1]
+        assert got["found"] == [1] * (len(ids) - 1) + [0]
+        for i, k in enumerate(ids[:-1]):
+            assert got["sizes"][i] == 300
+            if i == rank:      # 10-byte buffer: reported, left untouched
+                assert got["sha"][i] == hashlib.sha256(bytes(10)).hexdigest()
+            else:
+                assert got["sha"][i] == hashlib.sha256(blocks[k].tobytes()).hexdigest()
+        assert got["sizes"][-1] == 0
