@@ -50,9 +50,14 @@ def parse():
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--workload", default="llama3-8b",
-                    choices=["llama3-8b", "sweep", "dedup"],
+                    choices=["llama3-8b", "sweep", "dedup", "llama3-70b-zipf"],
                     help="llama3-8b: the headline line; sweep / dedup: the "
-                         "block-size sweep and the prefix-dedup mix")
+                         "block-size sweep and the prefix-dedup mix; "
+                         "llama3-70b-zipf: 8192 x 5 MiB blocks per GPU, 30%% "
+                         "Zipf copies of a pool shared by all GPUs")
+    ap.add_argument("--cap-gib", type=float, default=120.0,
+                    help="llama3-70b-zipf: HBM pool per GPU (GiB); below the "
+                         "stored bytes, 1-GPU runs demote to the DRAM tier")
     return ap.parse_args()
 
 
@@ -483,8 +488,8 @@ def main_ours(args):
 
 # ------------------------------------------------------- extra workloads
 def run_extra(args):
-    """--workload sweep | dedup: the other reference configurations, one
-    JSON line each (not the headline line)."""
+    """--workload sweep | dedup | llama3-70b-zipf: the other reference
+    configurations, one JSON line each (not the headline line)."""
     import numpy as np
     import torch
     import torch.distributed as dist
@@ -572,6 +577,68 @@ def run_extra(args):
                             "size per GPU, content-addressed INT8 PUT",
                 "metric": METRIC, "unit": UNIT, "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup, "sweep": res}
+    elif args.workload == "llama3-70b-zipf":
+        # 65536 x 5 MiB over 8 GPUs (8192 per GPU), 30 % of them Zipf(1.1)
+        # copies of a 1024-block pool that every GPU draws from, so copies
+        # repeat inside a GPU's batch and across GPUs
+        n, pool_n = 8192, 1024
+        seq, pre = workloads.dedup_sequence(n, SEED + rank, pool=pool_n,
+                                            sessions=256, shared_frac=0.3)
+        geo = workloads.LLAMA3_70B
+        pool = workloads.kv_blocks_torch(pool_n, SEED, dev, **geo)
+        uniq_n = int((seq >= pool_n).sum())
+        uniq = workloads.kv_blocks_torch(uniq_n, SEED + 1000 + rank, dev,
+                                         **geo)
+        bb = pool.shape[1]
+        pp, up = pool.data_ptr(), uniq.data_ptr()
+        ptrs = np.where(seq < pool_n, pp + seq * bb,
+                        up + (seq - pool_n) * bb).astype(np.uint64)
+        sizes = np.full(n, bb, np.uint64)
+        cap = int(args.cap_gib * (1 << 30))
+        if world > 1:
+            store = make_store(cap)
+        else:
+            cfg = cc.CascadeConfig()
+            cfg.gpu_device_id = local
+            cfg.gpu_capacity_bytes = cap
+            cfg.shm_capacity_bytes = 64 << 30     # the demotion target
+            cfg.kv_compression = True
+            cfg.gpu_q8 = True
+            cfg.index_slots = 1 << 16
+            store = cc.CascadeStore(cfg)
+        rows = (ptrs, sizes) if world > 1 else None
+        ms, stored = timed_steps(put_fn(store, rows, n, ptrs, sizes),
+                                 args.warmup, args.steps)
+        assert stored == n, stored
+        st = store.get_stats()
+        store.close()
+        # expected hits: all blocks minus the distinct ones (the pool blocks
+        # used by any GPU, plus every GPU's unique blocks)
+        used = np.zeros(pool_n, np.int32)
+        used[np.unique(seq[seq < pool_n])] = 1
+        t = torch.tensor(np.concatenate([used, [uniq_n, int(st.dedup_hits),
+                                                int(st.gpu_evictions)]]),
+                         dtype=torch.int64, device=dev)
+        if world > 1:
+            every = [torch.empty_like(t) for _ in range(world)]
+            dist.all_gather(every, t)
+        else:
+            every = [t]
+        ev = torch.stack(every).cpu().numpy()
+        distinct = int((ev[:, :pool_n].max(axis=0) > 0).sum()) + int(ev[:, pool_n].sum())
+        hits = int(ev[:, pool_n + 1].sum())
+        assert hits == world * n - distinct, (hits, world * n, distinct)
+        line = {"workload": "llama3-70b KV: 8192 x 5 MiB per GPU, 30% "
+                            "Zipf(1.1) copies of a 1024-block pool shared by "
+                            "all GPUs, content-addressed INT8 PUT",
+                "metric": METRIC, "unit": UNIT, "n_gpus": world,
+                "value": world * n * bb / (ms * 1e-3) / 1e9,
+                "ms_per_step": ms, "steps": args.steps, "warmup": args.warmup,
+                "blocks_total": world * n, "block_bytes": bb,
+                "hbm_pool_gib_per_gpu": args.cap_gib,
+                "dedup_hits_total": hits, "expected_hits": world * n - distinct,
+                "gpu_evictions_total": int(ev[:, pool_n + 2].sum()),
+                "parallelism": f"sharded index x{world}" if world > 1 else "1 GPU"}
     else:   # dedup: 8192 blocks, 60 % Zipf copies of 512 shared prefixes
         n = 8192
         seq, pre = workloads.dedup_sequence(n, SEED + rank, pool=512,
@@ -585,10 +652,7 @@ def run_extra(args):
                          for k in seq], dtype=np.uint64)
         sizes = np.full(n, bb, np.uint64)
         store = make_store(int((512 + uniq_n) * bb // 2 * 1.2) + (256 << 20))
-        if world > 1:
-            rows = [pool[int(k)] if k < 512 else uniq[int(k) - 512] for k in seq]
-        else:
-            rows = None
+        rows = (ptrs, sizes) if world > 1 else None
         ms, stored = timed_steps(put_fn(store, rows, n, ptrs, sizes),
                                  args.warmup, args.steps)
         st = store.get_stats()

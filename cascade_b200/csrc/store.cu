@@ -556,13 +556,11 @@ static int put_placed(Store &st, size_t n, bool use_digests,
   CB_CUDA(cudaStreamSynchronize(s));
   if ((rc = check_device_err(st))) return rc;
 
-  // Placement, in sequence order as the reference's serial puts would:
-  // HBM while used + size fits the GPU capacity (CascadeStore::put,
-  // cascade_core.cpp:1097-1105), else the DRAM tier while its capacity
-  // holds (1108-1118), else the block fails (the Lustre tier of
-  // 1121-1124 is not part of this library).
-  // HBM is filled first; when the new blocks do not fit, older ones are
-  // demoted to DRAM to make room (CascadeStore::put, 1097-1105).
+  // Placement (CascadeStore::put, cascade_core.cpp:1097-1124): HBM first;
+  // when the new blocks do not fit, older ones are demoted to DRAM to make
+  // room (1097-1105).  Blocks that still get no HBM go to the DRAM tier
+  // while its capacity holds (1108-1118), else they fail (the Lustre tier
+  // of 1121-1124 is not part of this library).
   if (allow_hbm && st.hbm && st.dram_tier) {
     uint64_t need = 0;
     for (size_t i = 0; i < n; ++i)
@@ -574,6 +572,39 @@ static int put_placed(Store &st, size_t n, bool use_digests,
       const uint64_t deficit = st.gpu_used + fit > st.pool_cap
                                    ? st.gpu_used + fit - st.pool_cap : 0;
       if ((rc = evict_hbm(st, deficit))) return rc;
+    }
+  }
+  // Which new blocks get HBM.  Without a DRAM tier, the reference's serial
+  // puts store blocks while they fit and fail the rest (nothing can be
+  // demoted): first come, first placed.  With one, each serial put lands in
+  // HBM and demotes the least recently used blocks, prefix blocks last
+  // (evict_gpu_to_shm, cascade_core.cpp:998-1036): after the batch, HBM
+  // holds its prefix blocks and then its latest blocks.  That end state is
+  // placed directly, without writing blocks to HBM only to demote them
+  // within the same batch.
+  std::vector<char> hbm_pick(n, 0);
+  if (allow_hbm && st.hbm) {
+    std::vector<size_t> order;
+    for (size_t i = 0; i < n; ++i)
+      if (st.sc.h_status[i] == CASCADE_PUT_STORED) order.push_back(i);
+    if (st.dram_tier) {
+      const bool semantic = st.cfg.semantic_eviction && st.cfg.dedup_enabled;
+      auto rank_of = [&](size_t i) {
+        return (semantic && h_prefix && h_prefix[i]) ? 0 : 1;
+      };
+      std::stable_sort(order.begin(), order.end(), [&](size_t a, size_t b) {
+        if (rank_of(a) != rank_of(b)) return rank_of(a) < rank_of(b);
+        return a > b;
+      });
+    }
+    uint64_t proj = st.gpu_used;
+    for (size_t i : order) {
+      const uint64_t size = st.sc.h_sizes[i];
+      const uint64_t pay = payload_bytes(size, q8_eligible(st, size, false));
+      if (proj + pay <= st.pool_cap) {
+        hbm_pick[i] = 1;
+        proj += pay;
+      }
     }
   }
   uint64_t hbm_proj = st.gpu_used, dram_proj = st.shm_used;
@@ -591,8 +622,7 @@ static int put_placed(Store &st, size_t n, bool use_digests,
     st.sc.h_flags[i] = prefix;
     if (st.sc.h_status[i] != CASCADE_PUT_STORED) continue;
     const bool hq8 = st.hbm && q8_eligible(st, size, false);
-    if (allow_hbm && st.hbm &&
-        hbm_proj + payload_bytes(size, hq8) <= st.pool_cap) {
+    if (hbm_pick[i]) {
       const bool q8 = hq8;
       st.sc.h_req[i] = payload_bytes(size, q8);
       st.sc.h_flags[i] |= kTierHbm | (q8 ? kFlagQ8 : 0);

@@ -80,7 +80,12 @@ class CudaShardOps:
 
     def begin(self, blocks, is_prefix, world, rank, seq_base):
         import torch
-        if isinstance(blocks, torch.Tensor) and blocks.dim() == 2:
+        if isinstance(blocks, tuple):    # (device addresses, sizes)
+            ptrs = np.ascontiguousarray(blocks[0], dtype=np.uint64)
+            sizes = np.ascontiguousarray(blocks[1], dtype=np.uint64)
+            n = len(ptrs)
+            self._keep = None            # the caller keeps the blocks alive
+        elif isinstance(blocks, torch.Tensor) and blocks.dim() == 2:
             rows = blocks.contiguous()   # one block per row
             n = rows.shape[0]
             stride = rows.stride(0) * rows.element_size()
@@ -232,14 +237,16 @@ class ShardedCascadeStore:
     def put_batch(self, blocks: Sequence, is_prefix=None,
                   return_status: bool = False):
         """Collective: every rank calls it with its own blocks (a list of
-        CUDA tensors, or one 2-D CUDA tensor with a block per row).  Returns
+        CUDA tensors, one 2-D CUDA tensor with a block per row, or a tuple
+        (device addresses, sizes) of uint64 arrays for blocks on this rank's
+        GPU that the caller keeps alive until the call returns).  Returns
         the number of this rank's blocks stored or deduplicated (and, with
         ``return_status``, per-block status codes and 32-byte digests)."""
         import torch
         import torch.distributed as dist
         with self._lock:
             dev = self.ops.device
-            n = len(blocks)
+            n = len(blocks[0]) if isinstance(blocks, tuple) else len(blocks)
             mine = torch.tensor([n], dtype=torch.int64, device=dev)
             every = [torch.zeros_like(mine) for _ in range(self.world)]
             dist.all_gather(every, mine, group=self.group)

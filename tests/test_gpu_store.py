@@ -372,6 +372,46 @@ def test_demotion_lru_with_prefix_protection():
     assert [i for i, h in enumerate(hits) if h == "shm"] == [3, 4, 5, 6]
 
 
+def test_overflowing_batch_leaves_serial_end_state():
+    """A batch of 12 blocks into an HBM tier that holds 8: the blocks left in
+    HBM are the ones serial puts (each demoting the least recently used,
+    prefix blocks last) would leave there, i.e. the batch's prefix blocks and
+    its latest blocks.  The batch places them directly, so it counts no
+    demotions where the serial puts count 4."""
+    S = 4096
+    rng = np.random.default_rng(41)
+    blocks = [rng.integers(0, 256, S, dtype=np.uint8) for _ in range(12)]
+    ids = [oracle.block_id(b) for b in blocks]
+    pre = [i in (0, 5) for i in range(12)]
+
+    def tiers(st):
+        buf = np.zeros(S, np.uint8)
+        out = []
+        for i in range(12):
+            before = _stats(st)
+            assert st.get(ids[i], buf) == (True, S)
+            assert np.array_equal(buf, blocks[i])
+            out.append("gpu" if _stats(st)["gpu_hits"] > before["gpu_hits"]
+                       else "shm")
+        return out
+
+    serial = make_store(use_gpu=True, gpu_cap=8 * S, shm_cap=1 << 20,
+                        promotion=False)
+    for i in range(12):
+        assert serial.put(ids[i], blocks[i], is_prefix=pre[i])
+    assert _stats(serial)["gpu_evictions"] == 4
+    batch = make_store(use_gpu=True, gpu_cap=8 * S, shm_cap=1 << 20,
+                       promotion=False)
+    rows = torch.from_numpy(np.stack(blocks)).to(DEV)
+    stored, status, _ = batch.put_batch(rows, is_prefix=pre, return_status=True)
+    assert stored == 12 and (status == 0).all()
+    s = _stats(batch)
+    assert s["gpu_used"] == 8 * S and s["shm_used"] == 4 * S
+    want = ["shm" if i in (1, 2, 3, 4) else "gpu" for i in range(12)]
+    assert tiers(serial) == want
+    assert tiers(batch) == want
+
+
 @pytest.mark.parametrize("gpu_q8", [False, True])
 def test_demotion_to_int8_dram_and_promotion(gpu_q8):
     """With kv_compression the DRAM tier holds INT8: demoted blocks come back
