@@ -7,6 +7,9 @@
 // is bound by how fast one warp can run the rounds of one chunk; the kernel
 // below takes everything else (loads, byte swaps, the message schedule) off
 // that warp.
+#include <map>
+#include <mutex>
+
 #include "common.cuh"
 #include "sha256.cuh"
 
@@ -326,13 +329,66 @@ __global__ void __launch_bounds__(64 * kGroups)
 
 }  // namespace
 
+// Unused dynamic shared memory that keeps at most `want` CTAs of a kernel
+// with `static_smem` bytes of its own on one SM.
+struct SmemLimits {
+  int per_sm = 0, optin = 0, reserved = 0, sms = 0;
+};
+
+static int smem_limits(SmemLimits *out) {
+  static std::mutex mu;
+  static std::map<int, SmemLimits> cache;
+  int dev = 0;
+  CB_CUDA(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = cache.find(dev);
+  if (it == cache.end()) {
+    SmemLimits l;
+    CB_CUDA(cudaDeviceGetAttribute(
+        &l.per_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev));
+    CB_CUDA(cudaDeviceGetAttribute(
+        &l.optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
+    CB_CUDA(cudaDeviceGetAttribute(
+        &l.reserved, cudaDevAttrReservedSharedMemoryPerBlock, dev));
+    CB_CUDA(cudaDeviceGetAttribute(&l.sms, cudaDevAttrMultiProcessorCount,
+                                   dev));
+    it = cache.emplace(dev, l).first;
+  }
+  *out = it->second;
+  return CASCADE_OK;
+}
+
 template <int G, int S, int R, int U, int A>
 int launch_sha256_pipelined(const uint64_t *d_ptrs, const uint64_t *d_sizes,
                             int n, uint8_t *d_digests, uint32_t *d_state,
                             uint64_t c_begin, uint64_t c_end, cudaStream_t s) {
   if (n <= 0) return CASCADE_OK;
   const int blocks = (n + 32 * G - 1) / (32 * G);
-  sha256_pipelined<G, S, R, U, A><<<blocks, 64 * G, 0, s>>>(
+  auto kernel = sha256_pipelined<G, S, R, U, A>;
+  // Each chain's speed is its consumer warp's issue rate, so the CTAs must
+  // spread evenly: two consumers on one scheduler halve their chains' speed
+  // and the launch ends with the slowest chain.  A CTA is small enough that
+  // four fit on an SM, and when other kernels are resident as the launch
+  // dispatches (the speculative payload kernels of a put), some SMs took 3-4
+  // CTAs: 8192 chains of 2 MiB ran 54 ms instead of 28.  Unused dynamic
+  // shared memory caps each SM at ceil(blocks / SMs) CTAs.
+  SmemLimits lim;
+  int rc = smem_limits(&lim);
+  if (rc) return rc;
+  cudaFuncAttributes attr;
+  CB_CUDA(cudaFuncGetAttributes(&attr, kernel));
+  const size_t own = attr.sharedSizeBytes + (size_t)lim.reserved;
+  const int want = (blocks + lim.sms - 1) / lim.sms;
+  size_t pad = 0;
+  const size_t slice = (size_t)lim.per_sm / (want + 1) + 1;  // want+1 cannot fit
+  if (slice > own && (size_t)want * slice <= (size_t)lim.per_sm &&
+      attr.sharedSizeBytes + (slice - own) <= (size_t)lim.optin)
+    pad = slice - own;
+  if (pad > (size_t)attr.maxDynamicSharedSizeBytes)
+    CB_CUDA(cudaFuncSetAttribute(kernel,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 lim.optin - (int)attr.sharedSizeBytes));
+  kernel<<<blocks, 64 * G, pad, s>>>(
       d_ptrs, d_sizes, n, reinterpret_cast<uint32_t *>(d_digests), 1u,
       0xffffffffu, d_state, c_begin, c_end);
   count_launches(1);
@@ -343,12 +399,13 @@ int launch_sha256_pipelined(const uint64_t *d_ptrs, const uint64_t *d_sizes,
 int launch_sha256_range(const uint64_t *d_ptrs, const uint64_t *d_sizes,
                         int n, uint8_t *d_digests, uint32_t *d_state,
                         uint64_t c_begin, uint64_t c_end, cudaStream_t s) {
-  // While there are fewer producer/consumer pairs than SMs each chain runs
-  // alone on its SM: the latency-tuned round (both recurrences three
-  // operations deep), all 64 rounds unrolled, and 8 chunks of loads in
-  // flight per lane.  Once every scheduler has work, the ALU pipe is the
-  // limit and the round with the fewest ALU instructions wins.
-  if (n <= 32 * kSmCount)
+  // Up to two producer/consumer pairs per SM, each warp has a scheduler to
+  // itself: the latency-tuned round (both recurrences three operations
+  // deep), all 64 rounds unrolled, and 8 chunks of loads in flight per lane
+  // (8192 chains: 610 GB/s against 523 for the other form).  Beyond that,
+  // warps share schedulers, the ALU pipe is the limit and the round with the
+  // fewest ALU instructions wins (12288 chains: 526 against 490).
+  if (n <= 2 * 32 * kSmCount)
     return launch_sha256_pipelined<1, 4, 1, 64, 8>(
         d_ptrs, d_sizes, n, d_digests, d_state, c_begin, c_end, s);
   return launch_sha256_pipelined<2, 3, 0, 16, 0>(d_ptrs, d_sizes, n, d_digests,

@@ -125,3 +125,24 @@ def dedup_sequence(n_blocks: int, seed: int, pool=512, sessions=256,
             nxt += 1
             pre.append(False)
     return np.asarray(seq, dtype=np.int64), np.asarray(pre, dtype=bool)
+
+
+def materialise(seq, pool, uniq):
+    """One CUDA row per entry of ``seq`` (``dedup_sequence``): row i is a
+    byte copy of pool block seq[i], or unique block seq[i] - len(pool).
+    Copies live in their own rows, as the KV blocks of two sessions that
+    share a prefix live in two buffers."""
+    import torch
+    n, npool = len(seq), pool.shape[0]
+    out = torch.empty((n, pool.shape[1]), dtype=torch.uint8, device=pool.device)
+    idx = torch.as_tensor(np.asarray(seq), device=pool.device)
+    shared = torch.nonzero(idx < npool).flatten()
+    own = torch.nonzero(idx >= npool).flatten()
+    step = 256
+    for a in range(0, shared.numel(), step):
+        j = shared[a:a + step]
+        out[j] = pool[idx[j]]
+    for a in range(0, own.numel(), step):
+        j = own[a:a + step]
+        out[j] = uniq[idx[j] - npool]
+    return out

@@ -69,18 +69,28 @@ def test_compute_block_ids_kv_blocks():
         assert full[i].tobytes() == hashlib.sha256(blocks[i].tobytes()).digest()
 
 
-def test_sha_many_chains_sample_checked():
-    # 4096 x 16 KiB: the many-chain regime; spot-check against OpenSSL.
-    n, s = 4096, 16384
+@pytest.mark.parametrize("n", [4096, 8192, 12288])
+def test_sha_many_chains_sample_checked(n):
+    # One warp pair per SM (4096), two per SM (8192) and the shared-scheduler
+    # form (12288): ragged sizes, every 7th block unaligned; spot-checked
+    # against OpenSSL across the batch, the last blocks included.
+    s = 4096
     g = torch.Generator(device=DEV)
     g.manual_seed(5)
-    data = torch.randint(0, 256, (n, s), dtype=torch.uint8, device=DEV,
+    data = torch.randint(0, 256, (n, s + 16), dtype=torch.uint8, device=DEV,
                          generator=g)
-    d = _gpu_digests([data[i] for i in range(n)])
+    sizes = [s - (i % 193) for i in range(n)]
+    offs = [(i % 13) if i % 7 == 0 else 0 for i in range(n)]
+    blocks = [data[i, offs[i]:offs[i] + sizes[i]] for i in range(n)]
+    d = _gpu_digests(blocks)
     host = data.cpu().numpy()
-    for i in (0, 1, 31, 32, 777, 4095):
-        assert d[i].tobytes() == hashlib.sha256(host[i].tobytes()).digest()
+    check = sorted(set(list(range(0, n, n // 40)) + [1, 7, 31, 32, 33, n - 2, n - 1]))
+    for i in check:
+        want = hashlib.sha256(host[i, offs[i]:offs[i] + sizes[i]].tobytes()).digest()
+        assert d[i].tobytes() == want, i
+    if n != 4096:
+        return
     # size-independent property: equal blocks, equal digests
-    d2 = _gpu_digests([data[7], data[7], data[8]])
+    d2 = _gpu_digests([blocks[7], blocks[7], blocks[8]])
     assert (d2[0] == d2[1]).all() and not (d2[0] == d2[2]).all()
     assert (d2[0] == d[7]).all()
