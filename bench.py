@@ -437,6 +437,17 @@ def main_ours(args):
             traffic = json.load(f)
 
     sha_gbps = total / (sha_ms * 1e-3) / 1e9
+    # The ceiling for n serial chains on their own schedulers: a round is
+    # 11 integer-ALU + 5 IMAD instructions, each issuing over 2 cycles on a
+    # 16-lane pipe, so a 64-byte chunk takes at least 64 x 22 cycles.
+    clk_sum = clk.summary()
+    mhz = clk_sum["sm_mhz"] or 1965.0
+    floor_gbps = min(n, 64 * 148) * 64 * mhz * 1e6 / (64 * 22) / 1e9
+    chain_floor = {"gbps": floor_gbps, "frac": sha_gbps / floor_gbps,
+                   "sm_mhz": mhz,
+                   "basis": "each chain's consumer warp alone on a scheduler: "
+                            "64 rounds x (11 ALU + 5 IMAD) x 2 issue cycles "
+                            "= 1408 cycles per 64-byte chunk"}
     q_bytes = total * 1.5 + 8 * n          # read S, write S/2 + header
     q_gbps = q_bytes / (q_ms * 1e-3) / 1e9
     line = {
@@ -455,7 +466,8 @@ def main_ours(args):
             "traffic": (traffic or {}).get("sha256_pipelined"),
             "note": f"{n} blocks = {n} serial chains = {(n + 31) // 32} "
                     "warps; per-chain issue latency, not the integer pipe, "
-                    "bounds 2 MiB blocks"},
+                    "bounds 2 MiB blocks",
+            "chain_floor": chain_floor},
         "roofline_quantise": {
             "kernel": "minmax_kernel+quantize_kernel", "bound": "hbm",
             "achieved": q_gbps, "peak": hbm_peak, "unit": "GB/s",
@@ -474,7 +486,7 @@ def main_ours(args):
                 ("pinned host -> HBM copy + ShardedCascadeStore.put_batch "
                  "per rank")},
         "gpu_launches": int(launches),
-        "clocks": clk.summary(),
+        "clocks": clk_sum,
     }
     if rank == 0:
         print(json.dumps(line), flush=True)
@@ -660,14 +672,21 @@ def run_extra(args):
         st = store.get_stats()
         store.close()
         hits = int(st.dedup_hits)
-        tot_hits, tot_distinct = hits, None
+        # expected: all blocks minus the distinct ones (pool blocks used by
+        # any GPU, plus every GPU's unique blocks)
+        used = np.zeros(512, np.int64)
+        used[np.unique(seq[seq < 512])] = 1
+        t = torch.tensor(np.concatenate([used, [uniq_n, hits]]),
+                         dtype=torch.int64, device=dev)
         if world > 1:
-            t = torch.tensor([hits], device=dev, dtype=torch.int64)
-            dist.all_reduce(t)
-            tot_hits = int(t.item())
+            every = [torch.empty_like(t) for _ in range(world)]
+            dist.all_gather(every, t)
         else:
-            tot_distinct = len(np.unique(seq))
-            assert hits == n - tot_distinct, (hits, n, tot_distinct)
+            every = [t]
+        ev = torch.stack(every).cpu().numpy()
+        tot_distinct = int((ev[:, :512].max(axis=0) > 0).sum()) + int(ev[:, 512].sum())
+        tot_hits = int(ev[:, 513].sum())
+        assert tot_hits == world * n - tot_distinct, (tot_hits, world * n, tot_distinct)
         line = {"workload": "prefix-dedup: 8192 x 2 MiB per GPU, 60% Zipf(1.1) "
                             "copies of 512 shared prefix blocks, 256 sessions; "
                             "every copy in its own buffer",
@@ -675,7 +694,7 @@ def run_extra(args):
                 "value": world * n * bb / (ms * 1e-3) / 1e9,
                 "ms_per_step": ms, "steps": args.steps, "warmup": args.warmup,
                 "dedup_hits_total": tot_hits,
-                "expected_hits": (n - tot_distinct) if world == 1 else None,
+                "expected_hits": world * n - tot_distinct,
                 "parallelism": f"sharded index x{world}" if world > 1 else "1 GPU"}
     if rank == 0:
         print(json.dumps(line), flush=True)
