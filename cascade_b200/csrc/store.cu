@@ -1991,11 +1991,14 @@ static int shard_get_end(Store &st, const uint8_t *d_back, size_t n,
     f.slot = kNoSlot;
     f.pad = 0;
     if (!r.found) continue;
-    const bool local = (int)r.holder == st.peer_rank;
     CB_CHECK((int)r.holder < world, CASCADE_ERR_INVALID,
              "shard_get_end: holder rank out of range");
-    CB_CHECK(local || (r.flags & kTierHbm), CASCADE_ERR_UNSUPPORTED,
-             "sharded get: the block is in another rank's DRAM tier");
+    // A location carries no index slot of this rank, so a DRAM block could
+    // not be promoted (relocated) here; a sharded store keeps its blocks
+    // in HBM.
+    CB_CHECK((r.flags & kTierHbm) && !(r.flags & kTierDram),
+             CASCADE_ERR_UNSUPPORTED,
+             "sharded get: the block is in a DRAM tier, not in HBM");
     bases[r.src_idx] = (uint64_t)(uintptr_t)st.peer_base[r.holder];
   }
   for (size_t i = 0; i < n; ++i) {
@@ -2008,8 +2011,6 @@ static int shard_get_end(Store &st, const uint8_t *d_back, size_t n,
     deliver[i] = (!f.found || size <= h_caps[i]) ? 1 : 0;
   }
   if (n_found) *n_found = found;
-  // A DRAM hit can only be local here; it is read (and promoted) from this
-  // store's own arena.
   return deliver_locked(st, n, h_out, deliver.data(), bases.data());
 }
 

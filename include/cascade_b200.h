@@ -294,7 +294,7 @@ int cascade_shard_put_end(cascade_store_t *s, const uint8_t *d_back,
  *              flags and gpu_hits / misses as in cascade_store_get_batch.
  * cascade_shard_attach_pools must have run on every rank first.  Blocks of
  * a sharded store live in HBM (a sharded put needs the whole batch to fit
- * there); a block found in another rank's DRAM tier is an error. */
+ * there); a block found in a DRAM tier is an error (CASCADE_ERR_UNSUPPORTED). */
 #define CASCADE_SHARD_QUERY_BYTES 32
 #define CASCADE_SHARD_LOCATION_BYTES 48
 #define CASCADE_IPC_HANDLE_BYTES 64
