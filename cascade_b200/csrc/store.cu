@@ -1502,14 +1502,20 @@ static int get_host_locked(Store &st, const Key &k, uint8_t *out,
 //
 // Other batches are copied block by block (directly from pinned memory,
 // through the pinned stage otherwise) and then put like device blocks.
-static int put_batch_host_locked(Store &st, size_t n,
-                                 const uint8_t *const *blocks,
-                                 const uint64_t *sizes, const uint8_t *keys,
-                                 const uint8_t *prefix, uint8_t *status,
-                                 uint8_t *digests, uint64_t *n_stored) {
+// Host blocks of one size at a constant pitch, in pinned memory: copied to
+// the device staging area in ~16 stripes on the copy stream while the hash
+// stream hashes each stripe as it lands (launch_sha256_range keeps the
+// running states).  On return the descriptors are uploaded, the digests are
+// being computed (st.ev2 marks the end) and the main stream waits for the
+// last stripe.  *taken = false when the layout does not qualify.
+static int stage_host_striped(Store &st, size_t n,
+                              const uint8_t *const *blocks,
+                              const uint64_t *sizes, bool *taken,
+                              uint64_t *max_size) {
+  *taken = false;
   const uint64_t S = sizes[0];
   const intptr_t pitch = n > 1 ? (intptr_t)(blocks[1] - blocks[0]) : (intptr_t)S;
-  bool uniform = keys == nullptr && S > 0 && pitch >= (intptr_t)S;
+  bool uniform = S > 0 && pitch >= (intptr_t)S;
   for (size_t i = 0; uniform && i < n; ++i)
     uniform = sizes[i] == S && blocks[i] == blocks[0] + (intptr_t)i * pitch;
   if (uniform) {
@@ -1522,59 +1528,62 @@ static int put_batch_host_locked(Store &st, size_t n,
     cudaGetLastError();
     uniform = p0 && p1;
   }
+  if (!uniform) return CASCADE_OK;
   int rc;
-  if (uniform) {
-    const uint64_t Pd = (S + 255) & ~uint64_t(255);
-    if ((rc = ensure_device_buf(st.d_stage, st.d_stage_cap, n * Pd, st.s)))
-      return rc;
-    if (n > st.sha_state_cap) {
-      CB_CUDA(cudaStreamSynchronize(st.s2));
-      if (st.sha_state) CB_CUDA(cudaFree(st.sha_state));
-      st.sha_state = nullptr;
-      st.sha_state_cap = 0;
-      CB_CUDA(cudaMalloc(&st.sha_state, n * 32));
-      st.sha_state_cap = n;
-    }
-    std::vector<uint64_t> ptrs(n);
-    for (size_t i = 0; i < n; ++i)
-      ptrs[i] = (uint64_t)(uintptr_t)(st.d_stage + i * Pd);
-    uint64_t max_size = 0;
-    if ((rc = upload_batch(st, n, ptrs.data(), sizes, nullptr, &max_size)))
-      return rc;
-    CB_CUDA(cudaEventRecord(st.ev, st.s));
-    CB_CUDA(cudaStreamWaitEvent(st.s2, st.ev, 0));
-    // ~16 stripes for large blocks, each a whole number of 64-byte chunks.
-    uint64_t K = std::min<uint64_t>(16, (S + 65535) / 65536);
-    if (K < 1) K = 1;
-    const uint64_t B = ((S + K - 1) / K + 63) & ~uint64_t(63);
-    K = (S + B - 1) / B;
-    for (uint64_t k = 0; k < K; ++k) {
-      const uint64_t off = k * B, w = std::min<uint64_t>(B, S - off);
-      CB_CUDA(cudaMemcpy2DAsync(st.d_stage + off, Pd, blocks[0] + off,
-                                (size_t)pitch, w, n, cudaMemcpyHostToDevice,
-                                st.s3));
-      CB_CUDA(cudaEventRecord(st.ev3, st.s3));
-      CB_CUDA(cudaStreamWaitEvent(st.s2, st.ev3, 0));
-      const uint64_t c0 = off / 64;
-      const uint64_t c1 = (k + 1 == K) ? ~0ull : (off + B) / 64;
-      rc = launch_sha256_range(st.sc.ptrs, st.sc.sizes, (int)n, st.sc.digests,
-                               st.sha_state, c0, c1, st.s2);
-      if (rc) return rc;
-    }
-    CB_CUDA(cudaEventRecord(st.ev2, st.s2));
-    CB_CUDA(cudaStreamWaitEvent(st.s, st.ev3, 0));  // every stripe is in
-    rc = put_uploaded(st, n, true, prefix, max_size, true);
-    if (rc) return rc;
-    return finish_put(st, n, true, status, digests, n_stored);
+  const uint64_t Pd = (S + 255) & ~uint64_t(255);
+  if ((rc = ensure_device_buf(st.d_stage, st.d_stage_cap, n * Pd, st.s)))
+    return rc;
+  if (n > st.sha_state_cap) {
+    CB_CUDA(cudaStreamSynchronize(st.s2));
+    if (st.sha_state) CB_CUDA(cudaFree(st.sha_state));
+    st.sha_state = nullptr;
+    st.sha_state_cap = 0;
+    CB_CUDA(cudaMalloc(&st.sha_state, n * 32));
+    st.sha_state_cap = n;
   }
+  std::vector<uint64_t> ptrs(n);
+  for (size_t i = 0; i < n; ++i)
+    ptrs[i] = (uint64_t)(uintptr_t)(st.d_stage + i * Pd);
+  if ((rc = upload_batch(st, n, ptrs.data(), sizes, nullptr, max_size)))
+    return rc;
+  CB_CUDA(cudaEventRecord(st.ev, st.s));
+  CB_CUDA(cudaStreamWaitEvent(st.s2, st.ev, 0));
+  // ~16 stripes for large blocks, each a whole number of 64-byte chunks.
+  uint64_t K = std::min<uint64_t>(16, (S + 65535) / 65536);
+  if (K < 1) K = 1;
+  const uint64_t B = ((S + K - 1) / K + 63) & ~uint64_t(63);
+  K = (S + B - 1) / B;
+  for (uint64_t k = 0; k < K; ++k) {
+    const uint64_t off = k * B, w = std::min<uint64_t>(B, S - off);
+    CB_CUDA(cudaMemcpy2DAsync(st.d_stage + off, Pd, blocks[0] + off,
+                              (size_t)pitch, w, n, cudaMemcpyHostToDevice,
+                              st.s3));
+    CB_CUDA(cudaEventRecord(st.ev3, st.s3));
+    CB_CUDA(cudaStreamWaitEvent(st.s2, st.ev3, 0));
+    const uint64_t c0 = off / 64;
+    const uint64_t c1 = (k + 1 == K) ? ~0ull : (off + B) / 64;
+    rc = launch_sha256_range(st.sc.ptrs, st.sc.sizes, (int)n, st.sc.digests,
+                             st.sha_state, c0, c1, st.s2);
+    if (rc) return rc;
+  }
+  CB_CUDA(cudaEventRecord(st.ev2, st.s2));
+  CB_CUDA(cudaStreamWaitEvent(st.s, st.ev3, 0));  // every stripe is in
+  *taken = true;
+  return CASCADE_OK;
+}
 
+// Any other host blocks: one copy each into the device staging area (pinned
+// blocks directly, pageable ones through the pinned stage); device
+// addresses to ptrs.
+static int stage_host_blocks(Store &st, size_t n, const uint8_t *const *blocks,
+                             const uint64_t *sizes, std::vector<uint64_t> &ptrs) {
   uint64_t total = 0;
   std::vector<uint64_t> offs(n);
   for (size_t i = 0; i < n; ++i) {
     offs[i] = total;
     total += (sizes[i] + 255) & ~uint64_t(255);
   }
-  rc = ensure_device_buf(st.d_stage, st.d_stage_cap, total, st.s);
+  int rc = ensure_device_buf(st.d_stage, st.d_stage_cap, total, st.s);
   if (rc) return rc;
   size_t pinned_need = 0;
   std::vector<uint8_t> pinned(n);
@@ -1586,7 +1595,7 @@ static int put_batch_host_locked(Store &st, size_t n,
     if (!pinned[i]) pinned_need = std::max<size_t>(pinned_need, sizes[i]);
   }
   if (pinned_need && (rc = ensure_host_stage(st, pinned_need))) return rc;
-  std::vector<uint64_t> ptrs(n);
+  ptrs.assign(n, 0);
   for (size_t i = 0; i < n; ++i) {
     ptrs[i] = (uint64_t)(uintptr_t)(st.d_stage + offs[i]);
     if (!sizes[i]) continue;
@@ -1600,6 +1609,28 @@ static int put_batch_host_locked(Store &st, size_t n,
                               cudaMemcpyHostToDevice, st.s));
     }
   }
+  return CASCADE_OK;
+}
+
+static int put_batch_host_locked(Store &st, size_t n,
+                                 const uint8_t *const *blocks,
+                                 const uint64_t *sizes, const uint8_t *keys,
+                                 const uint8_t *prefix, uint8_t *status,
+                                 uint8_t *digests, uint64_t *n_stored) {
+  int rc;
+  if (keys == nullptr) {
+    bool taken = false;
+    uint64_t max_size = 0;
+    if ((rc = stage_host_striped(st, n, blocks, sizes, &taken, &max_size)))
+      return rc;
+    if (taken) {
+      rc = put_uploaded(st, n, true, prefix, max_size, true);
+      if (rc) return rc;
+      return finish_put(st, n, true, status, digests, n_stored);
+    }
+  }
+  std::vector<uint64_t> ptrs;
+  if ((rc = stage_host_blocks(st, n, blocks, sizes, ptrs))) return rc;
   return put_batch_locked(st, n, ptrs.data(), sizes, keys, prefix, status,
                           digests, n_stored);
 }
@@ -1707,17 +1738,14 @@ inline int nblocks(size_t n) { return (int)((n + 255) / 256); }
 
 }  // namespace
 
-static int shard_begin(Store &st, size_t n, const uint64_t *h_ptrs,
-                       const uint64_t *h_sizes, const uint8_t *h_prefix,
-                       int world, int rank, uint64_t seq_base, uint8_t *d_send,
-                       uint64_t *h_counts) {
-  CB_CHECK(world >= 1 && world <= 256 && rank >= 0 && rank < world,
-           CASCADE_ERR_INVALID, "bad world/rank");
-  CB_CHECK(st.hbm, CASCADE_ERR_UNSUPPORTED,
-           "sharded puts need the HBM tier (use_gpu)");
-  uint64_t max_size = 0;
-  int rc = upload_batch(st, n, h_ptrs, h_sizes, nullptr, &max_size);
-  if (rc) return rc;
+// The batch's descriptors are uploaded (and, with digests_ready, its hash is
+// under way on the hash stream): store it speculatively and write the
+// records.
+static int shard_begin_staged(Store &st, size_t n, uint64_t max_size,
+                              bool digests_ready, const uint8_t *h_prefix,
+                              int world, int rank, uint64_t seq_base,
+                              uint8_t *d_send, uint64_t *h_counts) {
+  int rc;
   CB_CHECK(can_speculate(st, n), CASCADE_ERR_NOMEM,
            "sharded put: the HBM pool cannot hold the whole batch");
   // per-batch device space: n staged records, n owner ids, 2 x 256 counters
@@ -1729,7 +1757,8 @@ static int shard_begin(Store &st, size_t n, const uint64_t *h_ptrs,
   uint32_t *counts = reinterpret_cast<uint32_t *>(
       st.shard_aux + n * sizeof(ShardRecord) + ((n * sizeof(int) + 255) & ~size_t(255)));
   uint32_t *cursor = counts + 256;
-  if ((rc = speculate_local(st, n, h_prefix, max_size, false))) return rc;
+  if ((rc = speculate_local(st, n, h_prefix, max_size, digests_ready)))
+    return rc;
   cudaStream_t s = st.s;
   CB_CUDA(cudaStreamWaitEvent(s, st.ev2, 0));
   CB_CUDA(cudaMemsetAsync(counts, 0, 2 * 256 * sizeof(uint32_t), s));
@@ -1753,6 +1782,51 @@ static int shard_begin(Store &st, size_t n, const uint64_t *h_ptrs,
   st.shard_rank = rank;
   st.shard_open = n;
   return CASCADE_OK;
+}
+
+static int shard_begin(Store &st, size_t n, const uint64_t *h_ptrs,
+                       const uint64_t *h_sizes, const uint8_t *h_prefix,
+                       int world, int rank, uint64_t seq_base, uint8_t *d_send,
+                       uint64_t *h_counts) {
+  CB_CHECK(world >= 1 && world <= 256 && rank >= 0 && rank < world,
+           CASCADE_ERR_INVALID, "bad world/rank");
+  CB_CHECK(st.hbm, CASCADE_ERR_UNSUPPORTED,
+           "sharded puts need the HBM tier (use_gpu)");
+  uint64_t max_size = 0;
+  int rc = upload_batch(st, n, h_ptrs, h_sizes, nullptr, &max_size);
+  if (rc) return rc;
+  return shard_begin_staged(st, n, max_size, false, h_prefix, world, rank,
+                            seq_base, d_send, h_counts);
+}
+
+// Host blocks: staged to the device first.  Uniform pinned batches are
+// hashed stripe by stripe while they cross PCIe, as put_batch_host does.
+static int shard_begin_host(Store &st, size_t n, const uint8_t *const *blocks,
+                            const uint64_t *sizes, const uint8_t *h_prefix,
+                            int world, int rank, uint64_t seq_base,
+                            uint8_t *d_send, uint64_t *h_counts) {
+  CB_CHECK(world >= 1 && world <= 256 && rank >= 0 && rank < world,
+           CASCADE_ERR_INVALID, "bad world/rank");
+  CB_CHECK(st.hbm, CASCADE_ERR_UNSUPPORTED,
+           "sharded puts need the HBM tier (use_gpu)");
+  uint64_t need = 0;
+  for (size_t i = 0; i < n; ++i)
+    need += payload_bytes(sizes[i], q8_eligible(st, sizes[i], false));
+  CB_CHECK(st.gpu_used + need <= st.pool_cap, CASCADE_ERR_NOMEM,
+           "sharded put: the HBM pool cannot hold the whole batch");
+  bool taken = false;
+  uint64_t max_size = 0;
+  int rc = stage_host_striped(st, n, blocks, sizes, &taken, &max_size);
+  if (rc) return rc;
+  if (taken)
+    return shard_begin_staged(st, n, max_size, true, h_prefix, world, rank,
+                              seq_base, d_send, h_counts);
+  std::vector<uint64_t> ptrs;
+  if ((rc = stage_host_blocks(st, n, blocks, sizes, ptrs))) return rc;
+  if ((rc = upload_batch(st, n, ptrs.data(), sizes, nullptr, &max_size)))
+    return rc;
+  return shard_begin_staged(st, n, max_size, false, h_prefix, world, rank,
+                            seq_base, d_send, h_counts);
 }
 
 static int shard_resolve(Store &st, const uint8_t *d_recv, size_t m,
@@ -2255,6 +2329,26 @@ extern "C" int cascade_shard_put_begin(cascade_store_t *s, size_t n,
   if (int rc = join_caller(st, stream)) return rc;
   return cb::shard_begin(st, n, h_ptrs, h_sizes, h_prefix, world, rank,
                          seq_base, d_send, h_send_counts);
+}
+
+extern "C" int cascade_shard_put_begin_host(
+    cascade_store_t *s, size_t n, const uint8_t *const *h_blocks,
+    const uint64_t *h_sizes, const uint8_t *h_prefix, int world, int rank,
+    uint64_t seq_base, uint8_t *d_send, uint64_t *h_send_counts) {
+  STORE_ENTRY(s);
+  CB_CHECK(h_send_counts && (n == 0 || (h_blocks && h_sizes && d_send)),
+           CASCADE_ERR_INVALID, "null argument");
+  CB_CHECK(n <= (size_t)INT32_MAX, CASCADE_ERR_INVALID, "batch too large");
+  CB_CHECK(((uintptr_t)d_send & 15u) == 0, CASCADE_ERR_INVALID,
+           "d_send must be 16-byte aligned");
+  if (n == 0) {
+    for (int r = 0; r < world; ++r) h_send_counts[r] = 0;
+    st.shard_rank = rank;
+    st.shard_open = 0;
+    return CASCADE_OK;
+  }
+  return cb::shard_begin_host(st, n, h_blocks, h_sizes, h_prefix, world, rank,
+                              seq_base, d_send, h_send_counts);
 }
 
 extern "C" int cascade_shard_resolve(cascade_store_t *s, const uint8_t *d_recv,

@@ -53,6 +53,8 @@ _u64 = ctypes.c_uint64
 _int = ctypes.c_int
 _lib.register("cascade_shard_put_begin", _int,
               [_vp, _sz, _vp, _vp, _vp, _int, _int, _u64, _vp, _vp, _vp])
+_lib.register("cascade_shard_put_begin_host", _int,
+              [_vp, _sz, _vp, _vp, _vp, _int, _int, _u64, _vp, _vp])
 _lib.register("cascade_shard_resolve", _int, [_vp, _vp, _sz, _vp, _vp])
 _lib.register("cascade_shard_put_end", _int,
               [_vp, _vp, _sz, _vp, _vp, ctypes.POINTER(_u64), _vp])
@@ -110,6 +112,37 @@ class CudaShardOps:
             pf.ctypes.data if pf is not None else None, world, rank, seq_base,
             send.data_ptr() if n else None, counts.ctypes.data,
             self._stream()))
+        self._n = n
+        return send, [int(c) for c in counts]
+
+    def begin_host(self, blocks, is_prefix, world, rank, seq_base):
+        """begin for host blocks: a list of uint8 numpy arrays, or one 2-D
+        uint8 array (pinned rows are staged fastest)."""
+        import torch
+        if isinstance(blocks, np.ndarray) and blocks.ndim == 2:
+            rows = blocks
+            n = rows.shape[0]
+            ptrs = (np.arange(n, dtype=np.uint64) * np.uint64(rows.strides[0])
+                    + np.uint64(rows.ctypes.data))
+            sizes = np.full(n, rows.shape[1], np.uint64)
+            self._keep = rows
+        else:
+            arrs = [np.ascontiguousarray(b, dtype=np.uint8).reshape(-1)
+                    for b in blocks]
+            n = len(arrs)
+            ptrs = np.array([a.ctypes.data for a in arrs], dtype=np.uint64)
+            sizes = np.array([a.size for a in arrs], dtype=np.uint64)
+            self._keep = arrs
+        pf = (np.array([1 if p else 0 for p in is_prefix], dtype=np.uint8)
+              if is_prefix is not None else None)
+        send = torch.empty((n, RECORD_BYTES), dtype=torch.uint8,
+                           device=self.device)
+        counts = np.zeros(world, dtype=np.uint64)
+        check(_lib.load().cascade_shard_put_begin_host(
+            self.store._h, n, ptrs.ctypes.data if n else None,
+            sizes.ctypes.data if n else None,
+            pf.ctypes.data if pf is not None else None, world, rank, seq_base,
+            send.data_ptr() if n else None, counts.ctypes.data))
         self._n = n
         return send, [int(c) for c in counts]
 
@@ -242,11 +275,22 @@ class ShardedCascadeStore:
         GPU that the caller keeps alive until the call returns).  Returns
         the number of this rank's blocks stored or deduplicated (and, with
         ``return_status``, per-block status codes and 32-byte digests)."""
+        n = len(blocks[0]) if isinstance(blocks, tuple) else len(blocks)
+        return self._put(self.ops.begin, blocks, n, is_prefix, return_status)
+
+    def put_batch_host(self, blocks, is_prefix=None,
+                       return_status: bool = False):
+        """put_batch for blocks in host memory (a list of uint8 numpy arrays,
+        or one 2-D uint8 array with a block per row).  Pinned rows of one
+        size are copied to the GPU in stripes and hashed as they land."""
+        return self._put(self.ops.begin_host, blocks, len(blocks), is_prefix,
+                         return_status)
+
+    def _put(self, begin, blocks, n, is_prefix, return_status):
         import torch
         import torch.distributed as dist
         with self._lock:
             dev = self.ops.device
-            n = len(blocks[0]) if isinstance(blocks, tuple) else len(blocks)
             mine = torch.tensor([n], dtype=torch.int64, device=dev)
             every = [torch.zeros_like(mine) for _ in range(self.world)]
             dist.all_gather(every, mine, group=self.group)
@@ -254,8 +298,8 @@ class ShardedCascadeStore:
             seq_base = self._next_seq + sum(counts[:self.rank])
             self._next_seq += sum(counts)
 
-            send, send_splits = self.ops.begin(blocks, is_prefix, self.world,
-                                               self.rank, seq_base)
+            send, send_splits = begin(blocks, is_prefix, self.world,
+                                      self.rank, seq_base)
             sc = torch.tensor(send_splits, dtype=torch.int64, device=dev)
             rc = torch.empty(self.world, dtype=torch.int64, device=dev)
             dist.all_to_all_single(rc, sc, group=self.group)

@@ -269,6 +269,16 @@ int cascade_shard_put_begin(cascade_store_t *s, size_t n,
                             const uint8_t *h_prefix, int world, int rank,
                             uint64_t seq_base, uint8_t *d_send,
                             uint64_t *h_send_counts, void *stream);
+/* begin for blocks in host memory (the sharded form of
+ * cascade_store_put_batch_host): the blocks are copied to this rank's GPU
+ * first.  Pinned blocks of one size at a constant pitch are copied in
+ * stripes and hashed as each stripe lands.  Synchronous. */
+int cascade_shard_put_begin_host(cascade_store_t *s, size_t n,
+                                 const uint8_t *const *h_blocks,
+                                 const uint64_t *h_sizes,
+                                 const uint8_t *h_prefix, int world, int rank,
+                                 uint64_t seq_base, uint8_t *d_send,
+                                 uint64_t *h_send_counts);
 int cascade_shard_resolve(cascade_store_t *s, const uint8_t *d_recv,
                           size_t m, uint8_t *d_reply, void *stream);
 int cascade_shard_put_end(cascade_store_t *s, const uint8_t *d_back,

@@ -72,6 +72,9 @@ class CpuShardOps:
         self._blocks = [np.ascontiguousarray(b) for b in blocks]
         return send, counts
 
+    def begin_host(self, blocks, is_prefix, world, rank, seq_base):
+        return self.begin(blocks, is_prefix, world, rank, seq_base)
+
     def resolve(self, recv):
         import torch
         recs = recv.numpy().reshape(-1).view(REC) if recv.numel() else np.zeros(0, REC)

@@ -63,9 +63,15 @@ def _rank_main(rank, world, port, out_dir, q8):
         store = ShardedCascadeStore(cfg)
         res = []
         for batch in range(2):
-            blocks = torch.from_numpy(np.stack(_blocks(rank, batch))).to(dev)
-            stored, status, digests = store.put_batch(
-                [blocks[i] for i in range(blocks.shape[0])], return_status=True)
+            if batch == 0:       # device blocks
+                blocks = torch.from_numpy(np.stack(_blocks(rank, batch))).to(dev)
+                stored, status, digests = store.put_batch(
+                    [blocks[i] for i in range(blocks.shape[0])],
+                    return_status=True)
+            else:                # pinned host rows: striped copy + hash
+                rows = torch.from_numpy(np.stack(_blocks(rank, batch))).pin_memory()
+                stored, status, digests = store.put_batch_host(
+                    rows.numpy(), return_status=True)
             res.append({"stored": stored, "status": status.tolist(),
                         "digests": [d.tobytes().hex() for d in digests]})
         s = store.get_stats()

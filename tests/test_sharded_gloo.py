@@ -48,9 +48,10 @@ def _rank_main(rank, world, port, out_dir):
     try:
         store = ShardedCascadeStore(ops=CpuShardOps(shared_dir=out_dir))
         res = []
-        for batch in range(2):
-            stored, status, digests = store.put_batch(_blocks(rank, batch),
-                                                      return_status=True)
+        for batch in range(2):   # the second batch through the host form
+            put = store.put_batch if batch == 0 else store.put_batch_host
+            stored, status, digests = put(_blocks(rank, batch),
+                                          return_status=True)
             res.append({"stored": stored, "status": status.tolist()})
         # every rank reads every block of batch 0 (held on any rank), an id
         # that was never stored, and one block into a too-small buffer
