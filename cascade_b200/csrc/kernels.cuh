@@ -7,6 +7,17 @@
 
 namespace cb {
 
+// Unused shared memory (bytes per CTA) that a kernel running beside a
+// SHA-256 launch requests so that it cannot share an SM with the hash
+// chains: when a launch of one CTA per SM leaves SMs idle, the SHA-256 CTAs
+// fill their SMs' shared memory to within less than this.
+constexpr size_t kHashNeighbourSmem = 16 * 1024;
+
+// kHashNeighbourSmem when a SHA-256 launch over n blocks fills its SMs (one
+// CTA per SM, at least 16 SMs spare), else 0: what a kernel launched beside
+// that hash should request.
+size_t sha256_neighbour_smem(int n);
+
 int launch_sha256(const uint64_t *d_ptrs, const uint64_t *d_sizes, int n,
                   uint8_t *d_digests, cudaStream_t s);
 
@@ -19,15 +30,19 @@ int launch_sha256_range(const uint64_t *d_ptrs, const uint64_t *d_sizes,
                         int n, uint8_t *d_digests, uint32_t *d_state,
                         uint64_t c_begin, uint64_t c_end, cudaStream_t s);
 
+// smem_pad (bytes of unused dynamic shared memory per CTA) keeps the
+// payload kernels off SMs whose shared memory a concurrent SHA-256 launch
+// has filled; see launch_sha256_range.
 int launch_minmax(const uint64_t *d_ptrs, const uint64_t *d_sizes, int n,
-                  uint64_t max_size, int2 *d_mnmx, cudaStream_t s);
+                  uint64_t max_size, int2 *d_mnmx, cudaStream_t s,
+                  size_t smem_pad = 0);
 
 // header_inline=1: the reference layout (8-byte header, then codes) at
 // d_dsts[b]; header_inline=0: codes at d_dsts[b], header at d_headers+8*b.
 int launch_quantize(const uint64_t *d_ptrs, const uint64_t *d_sizes, int n,
                     uint64_t max_size, const int2 *d_mnmx,
                     const uint64_t *d_dsts, uint8_t *d_headers,
-                    int header_inline, cudaStream_t s);
+                    int header_inline, cudaStream_t s, size_t smem_pad = 0);
 
 int launch_dequantize(const uint64_t *d_srcs, const uint8_t *d_headers,
                       int header_inline, const uint64_t *d_out_sizes, int n,
@@ -36,7 +51,7 @@ int launch_dequantize(const uint64_t *d_srcs, const uint8_t *d_headers,
 
 int launch_copy(const uint64_t *d_srcs, const uint64_t *d_dsts,
                 const uint64_t *d_sizes, int n, uint64_t max_size,
-                cudaStream_t s);
+                cudaStream_t s, size_t smem_pad = 0);
 
 // out[i] = in[i] + delta
 int launch_offset_ptrs(const uint64_t *d_in, uint64_t delta, uint64_t *d_out,

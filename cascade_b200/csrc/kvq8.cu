@@ -249,14 +249,16 @@ __global__ void __launch_bounds__(kThreads)
 
 // ------------------------------------------------------------- launchers
 int launch_minmax(const uint64_t *d_ptrs, const uint64_t *d_sizes, int n,
-                  uint64_t max_size, int2 *d_mnmx, cudaStream_t s) {
+                  uint64_t max_size, int2 *d_mnmx, cudaStream_t s,
+                  size_t smem_pad) {
   if (n <= 0) return CASCADE_OK;
   init_minmax_kernel<<<(n + 255) / 256, 256, 0, s>>>(d_mnmx, n);
   count_launches(1);
   CB_CUDA(cudaGetLastError());
   const int tiles = (int)std::max<uint64_t>(1, div_up(max_size / 2, kTileElems));
   const int grid = grid_for((uint64_t)n * tiles, 1, 4);
-  minmax_kernel<<<grid, kThreads, 0, s>>>(d_ptrs, d_sizes, n, tiles, d_mnmx);
+  minmax_kernel<<<grid, kThreads, smem_pad, s>>>(d_ptrs, d_sizes, n, tiles,
+                                                 d_mnmx);
   count_launches(1);
   CB_CUDA(cudaGetLastError());
   return CASCADE_OK;
@@ -265,12 +267,12 @@ int launch_minmax(const uint64_t *d_ptrs, const uint64_t *d_sizes, int n,
 int launch_quantize(const uint64_t *d_ptrs, const uint64_t *d_sizes, int n,
                     uint64_t max_size, const int2 *d_mnmx,
                     const uint64_t *d_dsts, uint8_t *d_headers,
-                    int header_inline, cudaStream_t s) {
+                    int header_inline, cudaStream_t s, size_t smem_pad) {
   if (n <= 0) return CASCADE_OK;
   const int tiles = (int)std::max<uint64_t>(1, div_up(max_size / 2, kTileElems));
   const int grid = grid_for((uint64_t)n * tiles, 1, 4);
-  quantize_kernel<<<grid, kThreads, 0, s>>>(d_ptrs, d_sizes, n, tiles, d_mnmx,
-                                            d_dsts, d_headers, header_inline);
+  quantize_kernel<<<grid, kThreads, smem_pad, s>>>(
+      d_ptrs, d_sizes, n, tiles, d_mnmx, d_dsts, d_headers, header_inline);
   count_launches(1);
   CB_CUDA(cudaGetLastError());
   return CASCADE_OK;
@@ -295,11 +297,12 @@ int launch_dequantize(const uint64_t *d_srcs, const uint8_t *d_headers,
 
 int launch_copy(const uint64_t *d_srcs, const uint64_t *d_dsts,
                 const uint64_t *d_sizes, int n, uint64_t max_size,
-                cudaStream_t s) {
+                cudaStream_t s, size_t smem_pad) {
   if (n <= 0) return CASCADE_OK;
   const int tiles = (int)std::max<uint64_t>(1, div_up(max_size, kCopyTile));
   const int grid = grid_for((uint64_t)n * tiles, 1, 4);
-  copy_kernel<<<grid, kThreads, 0, s>>>(d_srcs, d_dsts, d_sizes, n, tiles);
+  copy_kernel<<<grid, kThreads, smem_pad, s>>>(d_srcs, d_dsts, d_sizes, n,
+                                               tiles);
   count_launches(1);
   CB_CUDA(cudaGetLastError());
   return CASCADE_OK;

@@ -11,6 +11,7 @@
 #include <mutex>
 
 #include "common.cuh"
+#include "kernels.cuh"
 #include "sha256.cuh"
 
 namespace cb {
@@ -358,6 +359,12 @@ static int smem_limits(SmemLimits *out) {
   return CASCADE_OK;
 }
 
+// One CTA per SM and at least 16 SMs spare: the launch fills its SMs'
+// shared memory so that neighbours run on the spare SMs only.
+static bool fills_sms(const SmemLimits &lim, int blocks) {
+  return blocks <= lim.sms && lim.sms - blocks >= 16;
+}
+
 template <int G, int S, int R, int U, int A>
 int launch_sha256_pipelined(const uint64_t *d_ptrs, const uint64_t *d_sizes,
                             int n, uint8_t *d_digests, uint32_t *d_state,
@@ -384,6 +391,21 @@ int launch_sha256_pipelined(const uint64_t *d_ptrs, const uint64_t *d_sizes,
   if (slice > own && (size_t)want * slice <= (size_t)lim.per_sm &&
       attr.sharedSizeBytes + (slice - own) <= (size_t)lim.optin)
     pad = slice - own;
+  // One CTA per SM with >= 16 SMs spare: the CTAs also fill their SMs'
+  // shared memory to within 6 KiB.  Kernels launched beside the hash with
+  // kHashNeighbourSmem of shared memory then run only on the spare SMs and
+  // take no issue slots from the chains (when the hash ends they may use
+  // every SM).  4096 chains of 2 MiB with the put's INT8 payload beside
+  // them: 28.0 ms per step, the hash's own time, against 29.7 sharing SMs.
+  // With two CTAs per SM the payload is twice as large per unit of hash
+  // time and the spare SMs fall behind (8192 chains: 36 against 32 ms).
+  if (fills_sms(lim, blocks)) {
+    const size_t fill = ((size_t)lim.per_sm - own - 6 * 1024) & ~size_t(1023);
+    static_assert(6 * 1024 < kHashNeighbourSmem + 1024,
+                  "the leftover must not fit a neighbour CTA");
+    if (fill > pad && attr.sharedSizeBytes + fill <= (size_t)lim.optin)
+      pad = fill;
+  }
   if (pad > (size_t)attr.maxDynamicSharedSizeBytes)
     CB_CUDA(cudaFuncSetAttribute(kernel,
                                  cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -410,6 +432,13 @@ int launch_sha256_range(const uint64_t *d_ptrs, const uint64_t *d_sizes,
         d_ptrs, d_sizes, n, d_digests, d_state, c_begin, c_end, s);
   return launch_sha256_pipelined<2, 3, 0, 16, 0>(d_ptrs, d_sizes, n, d_digests,
                                                  d_state, c_begin, c_end, s);
+}
+
+size_t sha256_neighbour_smem(int n) {
+  SmemLimits lim;
+  if (n <= 0 || smem_limits(&lim) != CASCADE_OK) return 0;
+  const int per_cta = n <= 2 * 32 * kSmCount ? 32 : 64;  // chains per CTA
+  return fills_sms(lim, (n + per_cta - 1) / per_cta) ? kHashNeighbourSmem : 0;
 }
 
 int launch_sha256(const uint64_t *d_ptrs, const uint64_t *d_sizes, int n,

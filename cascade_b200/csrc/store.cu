@@ -844,13 +844,20 @@ static int speculate_local(Store &st, size_t n, const uint8_t *h_prefix,
                                     st.sc.eff_raw, st.sc.eff_q8);
   count_launches(1);
   CB_CUDA(cudaGetLastError());
+  // These run while the hash is still running.  When the hash launch fills
+  // its SMs, an unused shared-memory request keeps them on the spare SMs,
+  // so they take no issue slots from the serial chains.  With two hash
+  // CTAs per SM they share the SMs (the spare SMs alone fall behind).
+  const size_t pad = sha256_neighbour_smem((int)n);
   if (any_q8) {
-    rc = launch_minmax(st.sc.ptrs, st.sc.eff_q8, (int)n, max_size, st.sc.mnmx, s);
+    rc = launch_minmax(st.sc.ptrs, st.sc.eff_q8, (int)n, max_size, st.sc.mnmx,
+                       s, pad);
     if (!rc) rc = launch_quantize(st.sc.ptrs, st.sc.eff_q8, (int)n, max_size,
-                                  st.sc.mnmx, st.sc.dst, st.sc.hdr, 0, s);
+                                  st.sc.mnmx, st.sc.dst, st.sc.hdr, 0, s, pad);
   }
   if (!rc && any_raw)
-    rc = launch_copy(st.sc.ptrs, st.sc.dst, st.sc.eff_raw, (int)n, max_size, s);
+    rc = launch_copy(st.sc.ptrs, st.sc.dst, st.sc.eff_raw, (int)n, max_size, s,
+                     pad);
   return rc;
 }
 
