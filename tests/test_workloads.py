@@ -28,3 +28,29 @@ def test_dedup_sequence_mix():
     # unique blocks are unique
     u = seq[seq >= 512]
     assert len(np.unique(u)) == u.size
+
+
+def test_materialise_copies_in_own_rows():
+    import torch
+    seq, _ = workloads.dedup_sequence(600, 3, pool=16, sessions=8,
+                                      shared_frac=0.3)
+    g = torch.Generator().manual_seed(0)
+    pool = torch.randint(0, 256, (16, 64), dtype=torch.uint8, generator=g)
+    n_uniq = int((seq >= 16).sum())
+    uniq = torch.randint(0, 256, (n_uniq, 64), dtype=torch.uint8, generator=g)
+    rows = workloads.materialise(seq, pool, uniq)
+    assert rows.shape == (600, 64) and rows.is_contiguous()
+    for i, k in enumerate(seq):
+        want = pool[k] if k < 16 else uniq[k - 16]
+        assert torch.equal(rows[i], want)
+    # copies of one pool block are equal bytes in distinct rows
+    k = int(seq[seq < 16][0])
+    idx = np.nonzero(seq == k)[0]
+    assert len(idx) >= 1 and all(torch.equal(rows[j], pool[k]) for j in idx)
+
+
+def test_dedup_sequence_shared_fraction_parameter():
+    seq, pre = workloads.dedup_sequence(8192, 2, pool=1024, sessions=256,
+                                        shared_frac=0.3)
+    assert abs((seq < 1024).mean() - 0.3) < 0.01
+    assert pre.sum() == (seq < 1024).sum()
