@@ -51,10 +51,11 @@ int cascade_abi_version(void);
  * compute_block_id, cascade_core.cpp:43-53 (bound at bindings.cpp:173-176);
  * the block id is the lowercase hex of digest bytes 0..15.
  * Each block is one serial chain, so large blocks need many blocks in one
- * call to fill the GPU.  The launch spreads its CTAs evenly by reserving
- * unused shared memory; with up to 32 blocks per SM it fills those SMs'
- * shared memory to within 6 KiB, so kernels the caller runs concurrently
- * use the other SMs unless they need almost no shared memory. */
+ * call to fill the GPU.  The launch spreads its CTAs (32 blocks each)
+ * evenly by reserving unused shared memory.  When n <= 32 x (SMs - 16) it
+ * runs one CTA per SM and fills those SMs' shared memory to within 6 KiB,
+ * so kernels the caller runs concurrently use the other SMs unless they
+ * need almost no shared memory. */
 int cascade_sha256_batch(const uint64_t *d_ptrs, const uint64_t *d_sizes,
                          size_t n, uint8_t *d_digests, void *stream);
 
