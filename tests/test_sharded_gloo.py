@@ -127,3 +127,53 @@ def test_sharded_get_reads_blocks_held_on_any_rank(tmp_path, world):
             else:
                 assert got["sha"][i] == hashlib.sha256(blocks[k].tobytes()).hexdigest()
         assert got["sizes"][-1] == 0
+
+
+def _uneven_main(rank, world, port, out_dir):
+    import torch.distributed as dist
+    from cascade_b200.sharded import ShardedCascadeStore
+    from oracle.shard_model import CpuShardOps
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        store = ShardedCascadeStore(ops=CpuShardOps(shared_dir=out_dir))
+        # rank 0 puts 20 blocks, every other rank an empty batch
+        mine = _blocks(0, 0)[:20] if rank == 0 else []
+        stored, status, _ = store.put_batch(mine, return_status=True)
+        # rank 0 reads nothing; the others read rank 0's blocks plus ids that
+        # were never stored
+        if rank == 0:
+            ids, outs = [], []
+        else:
+            ids = [hashlib.sha256(b.tobytes()).hexdigest()[:32]
+                   for b in _blocks(0, 0)[:20]] + ["00" * 16, "ff" * 16]
+            outs = [np.zeros(300, np.uint8) for _ in ids]
+        found, sizes = store.get_batch(ids, outs)
+        res = {"stored": stored, "status": status.tolist(),
+               "found": found.tolist(), "sizes": sizes.tolist(),
+               "sha": [hashlib.sha256(o.tobytes()).hexdigest() for o in outs]}
+        store.close()
+        with open(os.path.join(out_dir, f"u{rank}.json"), "w") as f:
+            json.dump(res, f)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_sharded_uneven_and_empty_batches(tmp_path):
+    world = 3
+    mp.spawn(_uneven_main, args=(world, _free_port(), str(tmp_path)),
+             nprocs=world, join=True)
+    blocks = _blocks(0, 0)[:20]
+    distinct = len({hashlib.sha256(b.tobytes()).digest()[:16] for b in blocks})
+    r0 = json.load(open(tmp_path / "u0.json"))
+    assert r0["stored"] == 20 and r0["status"].count(STORED) == distinct
+    assert r0["found"] == [] and r0["sizes"] == []
+    for rank in (1, 2):
+        r = json.load(open(tmp_path / f"u{rank}.json"))
+        assert r["stored"] == 0 and r["status"] == []
+        assert r["found"] == [1] * 20 + [0, 0]
+        assert r["sizes"] == [300] * 20 + [0, 0]
+        for i, b in enumerate(blocks):
+            assert r["sha"][i] == hashlib.sha256(b.tobytes()).hexdigest()
+        assert r["sha"][20] == r["sha"][21] == hashlib.sha256(bytes(300)).hexdigest()
