@@ -292,9 +292,9 @@ class ShardedCascadeStore:
         with self._lock:
             dev = self.ops.device
             mine = torch.tensor([n], dtype=torch.int64, device=dev)
-            every = torch.zeros(self.world, dtype=torch.int64, device=dev)
-            dist.all_gather_into_tensor(every, mine, group=self.group)
-            counts = every.tolist()          # one device-to-host copy
+            every = [torch.zeros_like(mine) for _ in range(self.world)]
+            dist.all_gather(every, mine, group=self.group)
+            counts = [int(t.item()) for t in every]
             seq_base = self._next_seq + sum(counts[:self.rank])
             self._next_seq += sum(counts)
 
