@@ -98,3 +98,25 @@ def test_dropin_module_names():
     finally:
         sys.path.remove(d)
         sys.modules.pop("cascade_cpp", None)
+
+
+def test_ctypes_signatures_match_header_arity():
+    """Every entry point the Python layer binds (cascade_cpp, sharded) is
+    declared in the header with the same number of parameters, so a
+    binding cannot drift from the C ABI."""
+    import re
+
+    from cascade_b200 import _lib
+    from cascade_b200 import cascade_cpp  # noqa: F401  (registers its entry points)
+    from cascade_b200 import sharded  # noqa: F401
+    text = open(_lib.HEADER_PATH).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    arity = {}
+    for name, params in re.findall(r"\b(cascade_\w+)\s*\(([^;{]*?)\)\s*;",
+                                   text, flags=re.S):
+        ps = [p for p in params.split(",") if p.strip() not in ("", "void")]
+        arity[name] = len(ps)
+    assert len(arity) >= 30
+    for name, (_, argtypes) in _lib._SIGS.items():
+        assert name in arity, name
+        assert len(argtypes) == arity[name], (name, len(argtypes), arity[name])
