@@ -581,7 +581,9 @@ static int put_placed(Store &st, size_t n, bool use_digests,
   // (evict_gpu_to_shm, cascade_core.cpp:998-1036): after the batch, HBM
   // holds its prefix blocks and then its latest blocks.  That end state is
   // placed directly, without writing blocks to HBM only to demote them
-  // within the same batch.
+  // within the same batch.  (With blocks of one size it is the serial end
+  // state exactly; with mixed sizes an older block small enough to fit the
+  // remaining room is kept too, where serial puts would have demoted it.)
   std::vector<char> hbm_pick(n, 0);
   if (allow_hbm && st.hbm) {
     std::vector<size_t> order;
