@@ -308,9 +308,11 @@ int cascade_shard_put_end(cascade_store_t *s, const uint8_t *d_back,
  *              copy or dequantise each block from its holder's pool (this
  *              GPU's own or a peer's) into h_out_ptrs[i]; sizes, found
  *              flags and gpu_hits / misses as in cascade_store_get_batch.
- * cascade_shard_attach_pools must have run on every rank first.  Blocks of
- * a sharded store live in HBM (a sharded put needs the whole batch to fit
- * there); a block found in a DRAM tier is an error (CASCADE_ERR_UNSUPPORTED). */
+ * cascade_shard_attach_pools must have run on every rank first.  As for a
+ * put, a rank must not run other operations on the store between get_begin
+ * and get_end.  Blocks of a sharded store live in HBM (a sharded put needs
+ * the whole batch to fit there); a block found in a DRAM tier is an error
+ * (CASCADE_ERR_UNSUPPORTED). */
 #define CASCADE_SHARD_QUERY_BYTES 32
 #define CASCADE_SHARD_LOCATION_BYTES 48
 #define CASCADE_IPC_HANDLE_BYTES 64
