@@ -47,14 +47,14 @@ def parse():
     ap.add_argument("--layers", type=int, default=32,
                     help="layers per KV block (32 = 2 MiB; smaller for "
                          "profiling captures)")
-    ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--workload", default="llama3-8b",
-                    choices=["llama3-8b", "sweep", "dedup", "llama3-70b-zipf"],
-                    help="llama3-8b: the headline line; sweep / dedup: the "
-                         "block-size sweep and the prefix-dedup mix; "
-                         "llama3-70b-zipf: 8192 x 5 MiB blocks per GPU, 30%% "
-                         "Zipf copies of a pool shared by all GPUs")
+                    choices=["llama3-8b", "llama3-70b-zipf"],
+                    help="llama3-8b: the headline line (it also carries the "
+                         "1 MiB round trip, the block-size sweep and the "
+                         "prefix-dedup mix); llama3-70b-zipf: 8192 x 5 MiB "
+                         "blocks per GPU, 30%% Zipf copies of a pool shared "
+                         "by all GPUs")
     ap.add_argument("--cap-gib", type=float, default=120.0,
                     help="llama3-70b-zipf: HBM pool per GPU (GiB); below the "
                          "stored bytes, 1-GPU runs demote to the DRAM tier")
@@ -151,18 +151,22 @@ class ClockSampler:
 
 
 # -------------------------------------------------------------- reference
-def cpu_reference(blocks_np, threads, min_seconds, steps=0, warmup=1):
-    """Times oracle/_ref (the reference's own code) in a child process."""
+def cpu_reference(blocks_np, threads, min_seconds, steps=0, warmup=1,
+                  lib=""):
+    """Times a build of the reference's own code (oracle/_ref) in a child
+    process."""
     import numpy as np
     fd, path = tempfile.mkstemp(suffix=".npy", dir="/dev/shm")
     os.close(fd)
     try:
         np.save(path, blocks_np)
-        out = subprocess.run(
-            [sys.executable, "-m", "oracle.ref_bench", "--input", path,
-             "--threads", str(threads), "--min-seconds", str(min_seconds),
-             "--steps", str(steps), "--warmup", str(warmup)],
-            cwd=ROOT, capture_output=True, text=True, timeout=600)
+        cmd = [sys.executable, "-m", "oracle.ref_bench", "--input", path,
+               "--threads", str(threads), "--min-seconds", str(min_seconds),
+               "--steps", str(steps), "--warmup", str(warmup)]
+        if lib:
+            cmd += ["--lib", lib]
+        out = subprocess.run(cmd, cwd=ROOT, capture_output=True, text=True,
+                             timeout=600)
         if out.returncode != 0:
             raise RuntimeError(out.stderr[-2000:])
         return json.loads(out.stdout.strip().splitlines()[-1])
@@ -170,20 +174,38 @@ def cpu_reference(blocks_np, threads, min_seconds, steps=0, warmup=1):
         os.unlink(path)
 
 
+def reference_build():
+    """(path, description) of the reference build to time on this host: the
+    -march=native build when it was made for exactly this host's options,
+    else the portable -march=x86-64-v3 build."""
+    import oracle
+    if oracle.native_build_matches_host():
+        return oracle.REF_NATIVE_SO, ("-O3 -march=native (built with this "
+                                      "host's exact -march=native options)")
+    return oracle.REF_SO, ("-O3 -march=x86-64-v3 (portable build; this "
+                           "host's -march=native differs from the native "
+                           "build's)")
+
+
+def host_cpu():
+    import oracle
+    return {"model": oracle.cpu_model(), "nproc": os.cpu_count()}
+
+
 def run_reference(args):
     """--impl reference: the reference's CPU path on all host threads."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    import numpy as np
     from cascade_b200 import workloads
     threads = os.cpu_count() or 1
     sample = workloads.kv_blocks_np(SAMPLE_BLOCKS, SEED)
     bb = sample.shape[1]
+    lib, build = reference_build()
     # Each step = one put_batch of the sample into an emptied store: W
     # untimed steps, then exactly K timed ones.
     res = cpu_reference(sample, threads, 0.0, steps=args.steps,
-                        warmup=args.warmup)
+                        warmup=args.warmup, lib=lib)
     value = res["gbps"]
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT,
@@ -193,7 +215,8 @@ def run_reference(args):
         "dtype": "u32 (SHA-256), f32 (INT8 scale math)", "data": "synthetic",
         "config": workload_config(args, bb),
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads,
-                         "kind": "reference",
+                         "kind": "reference", "build": build,
+                         "cpu": host_cpu(),
                          "sample": f"{SAMPLE_BLOCKS} blocks x {bb} B per step, "
                                    f"{res['passes']} steps"},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0,
@@ -204,63 +227,309 @@ def run_reference(args):
 
 
 # --------------------------------------------------------------------- ours
+class Ctx:
+    """Rank, device and the collective helpers of one bench process."""
+
+    def __init__(self):
+        import torch
+        import torch.distributed as dist
+        self.torch, self.dist = torch, dist
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        torch.cuda.set_device(self.local)
+        self.dev = torch.device("cuda", self.local)
+        if self.world > 1:
+            from datetime import timedelta
+            dist.init_process_group("nccl", device_id=self.dev,
+                                    timeout=timedelta(seconds=120))
+        self.stream = torch.cuda.current_stream(self.dev).cuda_stream
+
+    def barrier(self):
+        if self.world > 1:
+            self.dist.barrier()
+
+    def max(self, x):
+        if self.world == 1:
+            return x
+        t = self.torch.tensor([x], dtype=self.torch.float64, device=self.dev)
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def all_true(self, ok):
+        if self.world == 1:
+            return bool(ok)
+        t = self.torch.tensor([1 if ok else 0], dtype=self.torch.int32,
+                              device=self.dev)
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.MIN)
+        return bool(t.item())
+
+    def gather_rows(self, t):
+        """Every rank's int64 vector t, stacked (numpy, on every rank)."""
+        if self.world == 1:
+            return t.cpu().numpy()[None]
+        every = [self.torch.empty_like(t) for _ in range(self.world)]
+        self.dist.all_gather(every, t)
+        return self.torch.stack(every).cpu().numpy()
+
+    def timed(self, fn, warm, steps):
+        """fn() W times untimed, then `steps` times between CUDA events on
+        the current stream; ms per call, max over ranks."""
+        torch = self.torch
+        for _ in range(warm):
+            fn()
+        torch.cuda.synchronize()
+        self.barrier()
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(steps):
+            out = fn()
+        b.record()
+        torch.cuda.synchronize()
+        return self.max(a.elapsed_time(b) / steps), out
+
+
+def _addr_table(torch, rows, dev, stride=None):
+    n = rows.shape[0]
+    stride = stride or rows.stride(0) * rows.element_size()
+    return (torch.arange(n, dtype=torch.int64, device=dev) * stride
+            + rows.data_ptr())
+
+
+def compress_roundtrip(ctx, rows):
+    """The stateless compress -> decompress of CUDA rows [n, S] (the bytes
+    a GET of INT8-stored blocks must return)."""
+    from cascade_b200 import _lib
+    torch = ctx.torch
+    n, bb = rows.shape
+    cb = 8 + bb // 2
+    cstride = (cb + 255) // 256 * 256
+    comp = torch.empty(n * cstride, dtype=torch.uint8, device=ctx.dev)
+    out = torch.empty_like(rows)
+    sizes = torch.full((n,), bb, dtype=torch.int64, device=ctx.dev)
+    src = _addr_table(torch, rows, ctx.dev)
+    mid = torch.arange(n, dtype=torch.int64, device=ctx.dev) * cstride + comp.data_ptr()
+    dst = _addr_table(torch, out, ctx.dev)
+    _lib.call("cascade_kv_compress_batch", src.data_ptr(), sizes.data_ptr(),
+              mid.data_ptr(), n, bb, ctx.stream)
+    _lib.call("cascade_kv_decompress_batch", mid.data_ptr(), sizes.data_ptr(),
+              dst.data_ptr(), n, bb, ctx.stream)
+    torch.cuda.synchronize()
+    return out
+
+
+def make_cfg(cc, local, cap_bytes, q8=True, shm=0, slots=1 << 16):
+    cfg = cc.CascadeConfig()
+    cfg.gpu_device_id = local
+    cfg.gpu_capacity_bytes = cap_bytes
+    cfg.shm_capacity_bytes = shm
+    cfg.kv_compression = q8
+    cfg.gpu_q8 = q8
+    cfg.index_slots = slots
+    return cfg
+
+
+def section_cfg1(ctx, args):
+    """The reference's CPU-runnable workload on one GPU: 256 x 1 MiB of
+    seeded uniform bytes, is_prefix on blocks 0..127, content-addressed PUT
+    into a default (raw-format) store, then GET of every block.  Digests
+    are checked against hashlib (OpenSSL) and the round trip byte for byte."""
+    import hashlib
+
+    import numpy as np
+    from cascade_b200 import cascade_cpp as cc
+    from cascade_b200 import workloads
+    torch = ctx.torch
+    n, size = 256, 1 << 20
+    host = workloads.random_bytes(n, size, SEED)
+    rows = torch.from_numpy(host).to(ctx.dev)
+    cfg = cc.CascadeConfig()                    # the reference's defaults
+    cfg.gpu_device_id = ctx.local
+    cfg.gpu_capacity_bytes = 1 << 30
+    cfg.shm_capacity_bytes = 0
+    store = cc.CascadeStore(cfg)
+    ptrs = np.arange(n, dtype=np.uint64) * np.uint64(size) + np.uint64(rows.data_ptr())
+    sizes = np.full(n, size, np.uint64)
+    prefix = [i < n // 2 for i in range(n)]
+
+    def put():
+        store.clear()
+        return store._put_batch_raw(n, ptrs, sizes, None, prefix, True,
+                                    ctx.stream)
+
+    ms, (stored, status, dig) = ctx.timed(put, 2, 5)
+    want = [hashlib.sha256(host[i].tobytes()).digest() for i in range(n)]
+    digests_ok = all(dig[i].tobytes() == want[i] for i in range(n))
+    outs = torch.zeros_like(rows)
+    keys16 = np.ascontiguousarray(dig[:, :16]).reshape(-1)
+    optrs = np.arange(n, dtype=np.uint64) * np.uint64(size) + np.uint64(outs.data_ptr())
+    caps = np.full(n, size, np.uint64)
+    gms, (found, gsz) = ctx.timed(
+        lambda: store._get_batch_raw(n, keys16, optrs, caps, ctx.stream), 1, 3)
+    roundtrip_ok = bool(found.all()) and bool((gsz == size).all()) and \
+        bool(torch.equal(outs, rows))
+    s = store.get_stats()
+    store.close()
+    assert digests_ok and roundtrip_ok and stored == n, (digests_ok, roundtrip_ok)
+    return {"workload": "256 x 1 MiB seeded uniform bytes, is_prefix on "
+                        "blocks 0..127, content-addressed put_batch + "
+                        "get_batch, default (raw) store",
+            "put_gbps": n * size / (ms * 1e-3) / 1e9, "put_ms": ms,
+            "get_gbps": n * size / (gms * 1e-3) / 1e9, "get_ms": gms,
+            "digests_equal_hashlib": digests_ok,
+            "roundtrip_bit_exact": roundtrip_ok,
+            "gpu_used": int(s.gpu_used), "gpu_hits": int(s.gpu_hits),
+            "note": "256 serial SHA-256 chains of 1 MiB: the per-chain "
+                    "issue rate bounds this workload (8 warps)"}
+
+
+def section_sweep(ctx, args, sha_peak):
+    """Block-size sweep on one GPU: 64 KiB .. 16 MiB KV blocks, 1 GiB per
+    size, content-addressed INT8 PUT."""
+    import numpy as np
+    from cascade_b200 import cascade_cpp as cc
+    from cascade_b200 import workloads
+    torch = ctx.torch
+    hbm = hbm_peak()[0]
+    res = []
+    for layers in (1, 4, 16, 64, 256):
+        bb = workloads.kv_block_bytes(layers, 8, 16, 128)
+        n = (1 << 30) // bb
+        blocks = workloads.kv_blocks_torch(n, SEED + layers, ctx.dev,
+                                           layers=layers)
+        store = cc.CascadeStore(make_cfg(cc, ctx.local,
+                                         int(n * bb // 2 * 1.1) + (64 << 20)))
+        ptrs = np.arange(n, dtype=np.uint64) * np.uint64(bb) + np.uint64(blocks.data_ptr())
+        sizes = np.full(n, bb, np.uint64)
+
+        def put():
+            store.clear()
+            return store._put_batch_raw(n, ptrs, sizes, None, None, False,
+                                        ctx.stream)
+
+        ms, stored = ctx.timed(put, 2, 3)
+        assert stored == n
+        store.close()
+        del store, blocks
+        torch.cuda.empty_cache()
+        gbps = n * bb / (ms * 1e-3) / 1e9
+        # Bounds: the serial chains (each chain's consumer warp issues
+        # 1408 cycles per 64-byte chunk; at most 64 x SMs chains run at
+        # once, beyond that the measured all-scheduler SHA peak) and HBM
+        # (hash read + compress 1.5 S + payload write: 3.5 S).
+        chain = min(n, 64 * 148) * 64 * 1965e6 / 1408 / 1e9
+        sha_bound = min(chain, sha_peak)
+        hbm_bound = hbm / 3.5
+        bound = min(sha_bound, hbm_bound)
+        res.append({"block_bytes": bb, "blocks": n, "ms_per_step": ms,
+                    "gbps": gbps, "blocks_per_s": n / (ms * 1e-3),
+                    "bound_gbps": bound,
+                    "bound": "sha chains" if sha_bound < hbm_bound else "hbm",
+                    "frac_of_bound": gbps / bound})
+    return {"workload": "FP16 N(0,1) KV blocks of 64 KiB, 256 KiB, 1 MiB, "
+                        "4 MiB, 16 MiB; 1 GiB per size; content-addressed "
+                        "INT8 put_batch", "sizes": res}
+
+
+def section_dedup(ctx, args):
+    """Prefix-dedup workload: 8192 x 2 MiB per GPU, 60% of them Zipf(1.1)
+    copies of 512 shared prefix blocks in 256 sessions, every copy in its
+    own buffer.  Sharded index across the GPUs at N > 1.  The dedup hit
+    count must equal N - #distinct exactly."""
+    import numpy as np
+    from cascade_b200 import cascade_cpp as cc
+    from cascade_b200 import workloads
+    torch = ctx.torch
+    n = 8192
+    seq, pre = workloads.dedup_sequence(n, SEED + ctx.rank, pool=512,
+                                        sessions=256)
+    pool = workloads.kv_blocks_torch(512, SEED, ctx.dev)        # shared
+    uniq_n = int((seq >= 512).sum())
+    uniq = workloads.kv_blocks_torch(uniq_n, SEED + 1000 + ctx.rank, ctx.dev)
+    rows = workloads.materialise(seq, pool, uniq)
+    del pool, uniq
+    torch.cuda.empty_cache()
+    bb = rows.shape[1]
+    cfg = make_cfg(cc, ctx.local, int(n * bb // 2 * 1.1) + (256 << 20))
+    if ctx.world > 1:
+        from cascade_b200.sharded import ShardedCascadeStore
+        store = ShardedCascadeStore(cfg)
+
+        def put():
+            store.clear()
+            return store.put_batch(rows)
+    else:
+        store = cc.CascadeStore(cfg)
+        ptrs = np.arange(n, dtype=np.uint64) * np.uint64(bb) + np.uint64(rows.data_ptr())
+        sizes = np.full(n, bb, np.uint64)
+
+        def put():
+            store.clear()
+            return store._put_batch_raw(n, ptrs, sizes, None, None, False,
+                                        ctx.stream)
+
+    ms, stored = ctx.timed(put, 2, 5)
+    hits = int(store.get_stats().dedup_hits)
+    store.close()
+    del rows
+    torch.cuda.empty_cache()
+    used = np.zeros(512, np.int64)
+    used[np.unique(seq[seq < 512])] = 1
+    ev = ctx.gather_rows(torch.tensor(np.concatenate([used, [uniq_n, hits]]),
+                                      dtype=torch.int64, device=ctx.dev))
+    distinct = int((ev[:, :512].max(axis=0) > 0).sum()) + int(ev[:, 512].sum())
+    total_hits = int(ev[:, 513].sum())
+    expected = ctx.world * n - distinct
+    assert total_hits == expected, (total_hits, expected)
+    return {"workload": "prefix-dedup: 8192 x 2 MiB per GPU, 60% Zipf(1.1) "
+                        "copies of 512 shared prefix blocks, 256 sessions, "
+                        "every copy in its own buffer; content-addressed "
+                        "INT8 put_batch" + (", sharded index" if ctx.world > 1
+                                            else ""),
+            "gbps": ctx.world * n * bb / (ms * 1e-3) / 1e9, "ms_per_step": ms,
+            "dedup_hits": total_hits, "expected_hits": expected,
+            "hits_exact": total_hits == expected}
+
+
+def hbm_peak():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return (float(json.load(f)["hbm_gbs"]),
+                    "MEASURED_PEAKS.json hbm_gbs (of measured)")
+    except (OSError, KeyError, ValueError):
+        return 6650.0, "profiling-recipe fallback (of fallback)"
+
+
 def main_ours(args):
     import numpy as np
-    import torch
-    import torch.distributed as dist
 
     from cascade_b200 import _lib
     from cascade_b200 import cascade_cpp as cc
     from cascade_b200 import workloads
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
-        from datetime import timedelta
-        dist.init_process_group("nccl", device_id=dev,
-                                timeout=timedelta(seconds=120))
-
-    def barrier():
-        if world > 1:
-            dist.barrier()
-
-    def max_over_ranks(x):
-        if world == 1:
-            return x
-        t = torch.tensor([x], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
-
+    ctx = Ctx()
+    torch = ctx.torch
+    world, rank, local, dev = ctx.world, ctx.rank, ctx.local, ctx.dev
+    stream = ctx.stream
     L = _lib.load()
     blocks = workloads.kv_blocks_torch(args.blocks, SEED + rank, dev,
                                        layers=args.layers)
     n, bb = blocks.shape
     total = n * bb
-    cfg = cc.CascadeConfig()
-    cfg.gpu_device_id = local
-    cfg.gpu_capacity_bytes = int(n * (bb // 2) * 1.1) + (256 << 20)
-    cfg.shm_capacity_bytes = 1 << 30
-    cfg.kv_compression = True
-    cfg.gpu_q8 = True
-    cfg.index_slots = 1 << 15
+    cfg = make_cfg(cc, local, int(n * (bb // 2) * 1.1) + (256 << 20),
+                   shm=1 << 30, slots=1 << 15)
     ptrs = np.arange(n, dtype=np.uint64) * np.uint64(bb) + np.uint64(blocks.data_ptr())
     sizes = np.full(n, bb, np.uint64)
-    stream = torch.cuda.current_stream(dev).cuda_stream
     if world > 1:
         # the dedup index is sharded over the ranks (NCCL all-to-all)
         from cascade_b200.sharded import ShardedCascadeStore
         sharded = ShardedCascadeStore(cfg)
         store = sharded.store
 
-        def put_rows(rows):
-            return sharded.put_batch(rows)
-
         def step():
             sharded.clear()
-            return put_rows(blocks)
+            return sharded.put_batch(blocks)
     else:
         store = cc.CascadeStore(cfg)
 
@@ -269,11 +538,12 @@ def main_ours(args):
             return store._put_batch_raw(n, ptrs, sizes, None, None, False,
                                         stream)
 
+    # ---- the headline: W untimed steps, then exactly K timed ones
     with ClockSampler(local) as clk:   # sampling runs from warm-up on
         for _ in range(args.warmup):
             assert step() == n
         torch.cuda.synchronize()
-        barrier()
+        ctx.barrier()
         launches0 = L.cascade_diag_launch_count()
         clk.mark("t_begin")
         e0 = torch.cuda.Event(enable_timing=True)
@@ -284,9 +554,9 @@ def main_ours(args):
         e1.record()
         torch.cuda.synchronize()
         clk.mark("t_end")
-        barrier()
+        ctx.barrier()
     launches = L.cascade_diag_launch_count() - launches0
-    ms = max_over_ranks(e0.elapsed_time(e1))
+    ms = ctx.max(e0.elapsed_time(e1))
     assert stored == n
     s = store.get_stats()
     assert s.gpu_used == total // 2 and s.dedup_hits == 0
@@ -321,74 +591,67 @@ def main_ours(args):
     peak_gbps, peak_ms = ctypes.c_double(), ctypes.c_double()
     _lib.call("cascade_diag_sha_peak", local, 256, ctypes.byref(peak_gbps),
               ctypes.byref(peak_ms))
-    del qdst
+    del qdst, qptrs
     host = torch.empty((n, bb), dtype=torch.uint8, pin_memory=True)
     host.copy_(blocks)          # the e2e inputs, before GET overwrites blocks
-    # ---- GET: lookup + INT8 dequantise of the whole workload into device
-    # buffers (the blocks' own memory is the output)
-    store.clear() if world == 1 else sharded.clear()
+
+    # ---- GET of every block into device buffers (the blocks' own memory is
+    # the output), with a byte-exact check of a sample against the stateless
+    # compress -> decompress of the source rows
+    sample = min(256, n)
     if world == 1:
+        want = compress_roundtrip(ctx, blocks[:sample])
+        store.clear()
         _, _, dig = store._put_batch_raw(n, ptrs, sizes, None, None, True,
                                          stream)
         keys16 = np.ascontiguousarray(dig[:, :16]).reshape(-1)
         caps = np.full(n, bb, np.uint64)
-        for _ in range(2):
-            store._get_batch_raw(n, keys16, ptrs, caps, stream)
-        torch.cuda.synchronize()
-        ga = torch.cuda.Event(enable_timing=True)
-        gb_ = torch.cuda.Event(enable_timing=True)
-        ga.record()
-        for _ in range(3):
-            found, gsz = store._get_batch_raw(n, keys16, ptrs, caps, stream)
-        gb_.record()
-        torch.cuda.synchronize()
+        get_ms, (found, gsz) = ctx.timed(
+            lambda: store._get_batch_raw(n, keys16, ptrs, caps, stream), 2, 3)
         assert found.all() and (gsz == bb).all()
-        get_ms = ga.elapsed_time(gb_) / 3
+        exact = bool(torch.equal(blocks[:sample], want))
         get_info = {"value": total / (get_ms * 1e-3) / 1e9, "unit": UNIT,
                     "ms": get_ms, "what": "get_batch of every block: index "
                     "lookup + INT8 dequantise into device buffers (FP16 bytes "
                     "out per second)"}
     else:
-        # every rank reads the 4096 blocks its neighbour stored: each payload
-        # is dequantised straight out of the peer's pool (NVLink reads)
+        # every rank reads the blocks its neighbour stored: each payload is
+        # dequantised straight out of the peer's pool (NVLink reads)
+        nb = (rank + 1) % world
+        want = compress_roundtrip(
+            ctx, workloads.kv_blocks_torch(sample, SEED + nb, dev,
+                                           layers=args.layers))
+        sharded.clear()
         _, _, dig = sharded.put_batch(blocks, return_status=True)
         mine = torch.from_numpy(np.ascontiguousarray(dig[:, :16])).to(dev)
         every = [torch.empty_like(mine) for _ in range(world)]
-        dist.all_gather(every, mine)
-        ids = every[(rank + 1) % world].cpu().numpy()      # (n, 16) keys
-        outs = blocks                                      # a block per row
-        for _ in range(2):
-            sharded.get_batch(ids, outs)
-        torch.cuda.synchronize()
-        barrier()
-        ga = torch.cuda.Event(enable_timing=True)
-        gb_ = torch.cuda.Event(enable_timing=True)
-        ga.record()
-        for _ in range(3):
-            found, gsz = sharded.get_batch(ids, outs)
-        gb_.record()
-        torch.cuda.synchronize()
+        ctx.dist.all_gather(every, mine)
+        ids = every[nb].cpu().numpy()      # (n, 16) keys
+        get_ms, (found, gsz) = ctx.timed(lambda: sharded.get_batch(ids, blocks),
+                                         2, 3)
         assert found.all() and (gsz == bb).all()
-        get_ms = max_over_ranks(ga.elapsed_time(gb_) / 3)
+        exact = bool(torch.equal(blocks[:sample], want))
         get_info = {"value": world * total / (get_ms * 1e-3) / 1e9,
                     "unit": UNIT, "ms": get_ms,
                     "what": "ShardedCascadeStore.get_batch: every rank reads "
                     "the blocks its neighbour rank stored (owner lookup by "
                     "all-to-all, INT8 dequantise from the peer's pool over "
                     "NVLink); FP16 bytes out per second, all ranks"}
-    try:
-        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
-            hbm_peak = float(json.load(f)["hbm_gbs"])
-        hbm_src = "MEASURED_PEAKS.json hbm_gbs (of measured)"
-    except (OSError, KeyError, ValueError):
-        hbm_peak, hbm_src = 6650.0, "profiling-recipe fallback (of fallback)"
+    exact = ctx.all_true(exact)
+    assert exact, "GET bytes differ from compress -> decompress of the source"
+    get_info["byte_exact_sample"] = {
+        "blocks_per_rank": sample, "equal": exact,
+        "against": "stateless compress -> decompress of the source rows"
+                   + (" (the neighbour rank's blocks, regenerated)"
+                      if world > 1 else "")}
+    hbm, hbm_src = hbm_peak()
+    del want
 
-    # ---- e2e: host buffers through the public API
+    # ---- e2e: host buffers through the public API, the same K steps
     del blocks, dptrs, dsizes, digests
     torch.cuda.empty_cache()
     host_np = host.numpy()
     rows = [host_np[i] for i in range(n)]
-    e2e_steps = max(1, min(args.e2e_steps, args.steps))
     if world > 1:
         def e2e_step():
             sharded.clear()
@@ -398,31 +661,48 @@ def main_ours(args):
             store.clear()
             return store.put_batch_host(rows)
 
-    e2e_step()
-    torch.cuda.synchronize()
-    barrier()
-    a = torch.cuda.Event(enable_timing=True)
-    b = torch.cuda.Event(enable_timing=True)
-    a.record()
-    for _ in range(e2e_steps):   # each call returns after its own sync
-        assert e2e_step() == n
-    b.record()
-    torch.cuda.synchronize()
-    e2e_s = max_over_ranks(a.elapsed_time(b)) * 1e-3
-    e2e_value = world * e2e_steps * total / e2e_s / 1e9
+    e2e_ms, got = ctx.timed(e2e_step, 1, args.steps)
+    assert got == n
+    e2e_value = world * total / (e2e_ms * 1e-3) / 1e9
+    # The roofline under e2e: plain pinned host -> device copies of the same
+    # bytes, every rank at once.
+    h2d_dst = torch.empty((n, bb), dtype=torch.uint8, device=dev)
+    h2d_ms, _ = ctx.timed(lambda: h2d_dst.copy_(host, non_blocking=True), 1, 3)
+    del h2d_dst
+    torch.cuda.empty_cache()
+    h2d_gbps = world * total / (h2d_ms * 1e-3) / 1e9
+
+    # ---- the other reference configurations
+    if world > 1:
+        sharded.close()       # every rank unmaps the peers' pools first
+    store.close()
+    del host, host_np, rows
+    torch.cuda.empty_cache()
+    extra = {}
+    if world == 1:
+        extra["cfg1"] = section_cfg1(ctx, args)
+        extra["sweep"] = section_sweep(ctx, args, peak_gbps.value)
+    extra["dedup"] = section_dedup(ctx, args)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        sample = host_np[:SAMPLE_BLOCKS].copy()
+        smp = workloads.kv_blocks_np(SAMPLE_BLOCKS, SEED)
+        lib, build = reference_build()
         try:
-            res = cpu_reference(sample, os.cpu_count() or 1, CPU_MIN_SECONDS)
-            one = cpu_reference(sample[:64], 1, 2.0)
+            res = cpu_reference(smp, os.cpu_count() or 1, CPU_MIN_SECONDS,
+                                lib=lib)
+            one = cpu_reference(smp[:64], 1, 2.0, lib=lib)
             cpu = {"value": res["gbps"], "unit": UNIT,
                    "cores": res["threads"], "kind": "reference",
-                   "sample": f"{SAMPLE_BLOCKS} of the {n} blocks "
+                   "build": build, "cpu": host_cpu(),
+                   "sample": f"{SAMPLE_BLOCKS} blocks of the same workload "
                              f"({SAMPLE_BLOCKS * bb >> 20} MiB) x "
                              f"{res['passes']} passes",
                    "single_core_value": one["gbps"]}
+            import oracle
+            if lib != oracle.REF_SO:   # the portable build, for comparison
+                port = cpu_reference(smp, os.cpu_count() or 1, 3.0)
+                cpu["portable_build_value"] = port["gbps"]
         except Exception as e:  # the line still reports the GPU numbers
             cpu = {"value": None, "unit": UNIT, "cores": None,
                    "kind": "reference", "sample": f"failed: {e}"[:300]}
@@ -466,238 +746,115 @@ def main_ours(args):
                     "bounds 2 MiB blocks",
             "chain_floor": chain_floor},
         "roofline_quantise": {
-            "kernel": "minmax_kernel+quantize_kernel", "bound": "hbm",
-            "achieved": q_gbps, "peak": hbm_peak, "unit": "GB/s",
-            "frac": q_gbps / hbm_peak, "peak_source": hbm_src,
-            "algorithmic_bytes": "1.5 x block bytes (min/max re-read not counted)",
-            "traffic": (traffic or {}).get("quantize_kernel")},
+            "kernel": "compress_fused_kernel (single pass: one HBM read, "
+                      "clusters of 8 exchanging min/max through DSMEM)",
+            "bound": "hbm",
+            "achieved": q_gbps, "peak": hbm, "unit": "GB/s",
+            "frac": q_gbps / hbm, "peak_source": hbm_src,
+            "algorithmic_bytes": "1.5 x block bytes + 8-byte headers",
+            "traffic": (traffic or {}).get("compress_fused_kernel")},
         "stage_ms": {"sha256": sha_ms, "compress": q_ms},
         "get": get_info,
         "cpu_baseline": cpu,
         "e2e": {"value": e2e_value, "unit": UNIT,
                 "h2d_bytes_per_step": total, "d2h_bytes_per_step": n * 33,
-                "steps": e2e_steps,
+                "steps": args.steps,
                 "api": ("CascadeStore.put_batch_host (pinned host blocks, "
                         "striped H2D with hashing under the copy)")
                 if world == 1 else
                 ("ShardedCascadeStore.put_batch_host (pinned host blocks, "
-                 "striped H2D with hashing under the copy, per rank)")},
+                 "striped H2D with hashing under the copy, per rank)"),
+                "roofline": {"bound": "h2d", "achieved": e2e_value,
+                             "peak": h2d_gbps, "unit": "GB/s",
+                             "frac": e2e_value / h2d_gbps,
+                             "peak_source": "measured in this run: plain "
+                             "pinned host -> device copies of the same "
+                             f"{total >> 30} GiB per rank, all ranks at once"}},
         "gpu_launches": int(launches),
         "clocks": clk_sum,
     }
+    line.update(extra)
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
-        sharded.close()       # every rank unmaps the peers' pools first
-    store.close()
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
+        ctx.dist.barrier()
+        ctx.dist.destroy_process_group()
 
 
 # ------------------------------------------------------- extra workloads
 def run_extra(args):
-    """--workload sweep | dedup | llama3-70b-zipf: the other reference
-    configurations, one JSON line each (not the headline line)."""
+    """--workload llama3-70b-zipf: 8192 x 5 MiB blocks per GPU, 30% Zipf
+    copies of a pool every GPU draws from (one JSON line, not the headline
+    line)."""
     import numpy as np
-    import torch
-    import torch.distributed as dist
-
     from cascade_b200 import cascade_cpp as cc
     from cascade_b200 import workloads
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
-        from datetime import timedelta
-        dist.init_process_group("nccl", device_id=dev,
-                                timeout=timedelta(seconds=120))
-    stream = torch.cuda.current_stream(dev).cuda_stream
+    ctx = Ctx()
+    torch = ctx.torch
+    n, pool_n = 8192, 1024
+    seq, pre = workloads.dedup_sequence(n, SEED + ctx.rank, pool=pool_n,
+                                        sessions=256, shared_frac=0.3)
+    geo = workloads.LLAMA3_70B
+    pool = workloads.kv_blocks_torch(pool_n, SEED, ctx.dev, **geo)
+    uniq_n = int((seq >= pool_n).sum())
+    uniq = workloads.kv_blocks_torch(uniq_n, SEED + 1000 + ctx.rank, ctx.dev,
+                                     **geo)
+    rows = workloads.materialise(seq, pool, uniq)   # copies in own rows
+    del pool, uniq
+    torch.cuda.empty_cache()
+    bb = rows.shape[1]
+    cap = int(args.cap_gib * (1 << 30))
+    cfg = make_cfg(cc, ctx.local, cap, shm=(64 << 30) if ctx.world == 1 else 0)
+    if ctx.world > 1:
+        from cascade_b200.sharded import ShardedCascadeStore
+        store = ShardedCascadeStore(cfg)
 
-    def timed_steps(step, warm, steps):
-        for _ in range(warm):
-            step()
-        torch.cuda.synchronize()
-        if world > 1:
-            dist.barrier()
-        a = torch.cuda.Event(enable_timing=True)
-        b = torch.cuda.Event(enable_timing=True)
-        a.record()
-        for _ in range(steps):
-            out = step()
-        b.record()
-        torch.cuda.synchronize()
-        ms = a.elapsed_time(b) / steps
-        if world > 1:
-            t = torch.tensor([ms], device=dev, dtype=torch.float64)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            ms = float(t.item())
-        return ms, out
-
-    def make_store(cap_bytes):
-        cfg = cc.CascadeConfig()
-        cfg.gpu_device_id = local
-        cfg.gpu_capacity_bytes = cap_bytes
-        cfg.shm_capacity_bytes = 0
-        cfg.kv_compression = True
-        cfg.gpu_q8 = True
-        cfg.index_slots = 1 << 16
-        if world > 1:
-            from cascade_b200.sharded import ShardedCascadeStore
-            return ShardedCascadeStore(cfg)
-        return cc.CascadeStore(cfg)
-
-    def put_fn(store, rows_or_list, n, ptrs, sizes):
-        if world > 1:
-            def step():
-                store.clear()
-                return store.put_batch(rows_or_list)
-        else:
-            def step():
-                store.clear()
-                return store._put_batch_raw(n, ptrs, sizes, None, None, False,
-                                            stream)
-        return step
-
-    if args.workload == "sweep":
-        res = []
-        for layers in (1, 4, 16, 64, 256):          # 64 KiB .. 16 MiB
-            bb = workloads.kv_block_bytes(layers, 8, 16, 128)
-            n = (1 << 30) // bb
-            blocks = workloads.kv_blocks_torch(n, SEED + rank + layers, dev,
-                                               layers=layers)
-            ptrs = np.arange(n, dtype=np.uint64) * np.uint64(bb) + np.uint64(blocks.data_ptr())
-            sizes = np.full(n, bb, np.uint64)
-            store = make_store(int(n * bb // 2 * 1.1) + (64 << 20))
-            ms, stored = timed_steps(put_fn(store, blocks, n, ptrs, sizes),
-                                     args.warmup, args.steps)
-            assert stored == n
-            res.append({"block_bytes": bb, "blocks_per_gpu": n,
-                        "ms_per_step": ms,
-                        "gbps": world * n * bb / (ms * 1e-3) / 1e9,
-                        "blocks_per_s": world * n / (ms * 1e-3)})
-            store.close()     # N > 1: every rank unmaps the peers' pools
-            del store, blocks
-            torch.cuda.empty_cache()
-        line = {"workload": "variable block-size sweep, 1 GiB of FP16 KV per "
-                            "size per GPU, content-addressed INT8 PUT",
-                "metric": METRIC, "unit": UNIT, "n_gpus": world,
-                "steps": args.steps, "warmup": args.warmup, "sweep": res}
-    elif args.workload == "llama3-70b-zipf":
-        # 65536 x 5 MiB over 8 GPUs (8192 per GPU), 30 % of them Zipf(1.1)
-        # copies of a 1024-block pool that every GPU draws from, so copies
-        # repeat inside a GPU's batch and across GPUs
-        n, pool_n = 8192, 1024
-        seq, pre = workloads.dedup_sequence(n, SEED + rank, pool=pool_n,
-                                            sessions=256, shared_frac=0.3)
-        geo = workloads.LLAMA3_70B
-        pool = workloads.kv_blocks_torch(pool_n, SEED, dev, **geo)
-        uniq_n = int((seq >= pool_n).sum())
-        uniq = workloads.kv_blocks_torch(uniq_n, SEED + 1000 + rank, dev,
-                                         **geo)
-        rows = workloads.materialise(seq, pool, uniq)   # copies in own rows
-        del pool, uniq
-        torch.cuda.empty_cache()
-        bb = rows.shape[1]
+        def put():
+            store.clear()
+            return store.put_batch(rows)
+    else:
+        store = cc.CascadeStore(cfg)
         ptrs = np.arange(n, dtype=np.uint64) * np.uint64(bb) + np.uint64(rows.data_ptr())
         sizes = np.full(n, bb, np.uint64)
-        cap = int(args.cap_gib * (1 << 30))
-        if world > 1:
-            store = make_store(cap)
-        else:
-            cfg = cc.CascadeConfig()
-            cfg.gpu_device_id = local
-            cfg.gpu_capacity_bytes = cap
-            cfg.shm_capacity_bytes = 64 << 30     # the demotion target
-            cfg.kv_compression = True
-            cfg.gpu_q8 = True
-            cfg.index_slots = 1 << 16
-            store = cc.CascadeStore(cfg)
-        ms, stored = timed_steps(put_fn(store, rows, n, ptrs, sizes),
-                                 args.warmup, args.steps)
-        assert stored == n, stored
-        st = store.get_stats()
-        store.close()
-        # expected hits: all blocks minus the distinct ones (the pool blocks
-        # used by any GPU, plus every GPU's unique blocks)
-        used = np.zeros(pool_n, np.int32)
-        used[np.unique(seq[seq < pool_n])] = 1
-        t = torch.tensor(np.concatenate([used, [uniq_n, int(st.dedup_hits),
-                                                int(st.gpu_evictions)]]),
-                         dtype=torch.int64, device=dev)
-        if world > 1:
-            every = [torch.empty_like(t) for _ in range(world)]
-            dist.all_gather(every, t)
-        else:
-            every = [t]
-        ev = torch.stack(every).cpu().numpy()
-        distinct = int((ev[:, :pool_n].max(axis=0) > 0).sum()) + int(ev[:, pool_n].sum())
-        hits = int(ev[:, pool_n + 1].sum())
-        assert hits == world * n - distinct, (hits, world * n, distinct)
-        line = {"workload": "llama3-70b KV: 8192 x 5 MiB per GPU, 30% "
-                            "Zipf(1.1) copies of a 1024-block pool shared by "
-                            "all GPUs, every copy in its own buffer; "
-                            "content-addressed INT8 PUT",
-                "metric": METRIC, "unit": UNIT, "n_gpus": world,
-                "value": world * n * bb / (ms * 1e-3) / 1e9,
-                "ms_per_step": ms, "steps": args.steps, "warmup": args.warmup,
-                "blocks_total": world * n, "block_bytes": bb,
-                "hbm_pool_gib_per_gpu": args.cap_gib,
-                "dedup_hits_total": hits, "expected_hits": world * n - distinct,
-                "gpu_evictions_total": int(ev[:, pool_n + 2].sum()),
-                "parallelism": f"sharded index x{world}" if world > 1 else "1 GPU"}
-    else:   # dedup: 8192 blocks, 60 % Zipf copies of 512 shared prefixes
-        n = 8192
-        seq, pre = workloads.dedup_sequence(n, SEED + rank, pool=512,
-                                            sessions=256)
-        pool = workloads.kv_blocks_torch(512, SEED, dev)        # shared
-        uniq_n = int((seq >= 512).sum())
-        uniq = workloads.kv_blocks_torch(uniq_n, SEED + 1000 + rank, dev)
-        rows = workloads.materialise(seq, pool, uniq)   # copies in own rows
-        del pool, uniq
-        bb = rows.shape[1]
-        ptrs = np.arange(n, dtype=np.uint64) * np.uint64(bb) + np.uint64(rows.data_ptr())
-        sizes = np.full(n, bb, np.uint64)
-        # room for the whole batch: a put stores every block speculatively
-        # while its keys resolve, then frees the duplicates' slots
-        store = make_store(int(n * bb // 2 * 1.1) + (256 << 20))
-        ms, stored = timed_steps(put_fn(store, rows, n, ptrs, sizes),
-                                 args.warmup, args.steps)
-        st = store.get_stats()
-        store.close()
-        hits = int(st.dedup_hits)
-        # expected: all blocks minus the distinct ones (pool blocks used by
-        # any GPU, plus every GPU's unique blocks)
-        used = np.zeros(512, np.int64)
-        used[np.unique(seq[seq < 512])] = 1
-        t = torch.tensor(np.concatenate([used, [uniq_n, hits]]),
-                         dtype=torch.int64, device=dev)
-        if world > 1:
-            every = [torch.empty_like(t) for _ in range(world)]
-            dist.all_gather(every, t)
-        else:
-            every = [t]
-        ev = torch.stack(every).cpu().numpy()
-        tot_distinct = int((ev[:, :512].max(axis=0) > 0).sum()) + int(ev[:, 512].sum())
-        tot_hits = int(ev[:, 513].sum())
-        assert tot_hits == world * n - tot_distinct, (tot_hits, world * n, tot_distinct)
-        line = {"workload": "prefix-dedup: 8192 x 2 MiB per GPU, 60% Zipf(1.1) "
-                            "copies of 512 shared prefix blocks, 256 sessions; "
-                            "every copy in its own buffer",
-                "metric": METRIC, "unit": UNIT, "n_gpus": world,
-                "value": world * n * bb / (ms * 1e-3) / 1e9,
-                "ms_per_step": ms, "steps": args.steps, "warmup": args.warmup,
-                "dedup_hits_total": tot_hits,
-                "expected_hits": world * n - tot_distinct,
-                "parallelism": f"sharded index x{world}" if world > 1 else "1 GPU"}
-    if rank == 0:
+
+        def put():
+            store.clear()
+            return store._put_batch_raw(n, ptrs, sizes, None, None, False,
+                                        ctx.stream)
+
+    ms, stored = ctx.timed(put, args.warmup, args.steps)
+    assert stored == n, stored
+    st = store.get_stats()
+    store.close()
+    used = np.zeros(pool_n, np.int64)
+    used[np.unique(seq[seq < pool_n])] = 1
+    ev = ctx.gather_rows(torch.tensor(
+        np.concatenate([used, [uniq_n, int(st.dedup_hits),
+                               int(st.gpu_evictions)]]),
+        dtype=torch.int64, device=ctx.dev))
+    distinct = int((ev[:, :pool_n].max(axis=0) > 0).sum()) + int(ev[:, pool_n].sum())
+    hits = int(ev[:, pool_n + 1].sum())
+    assert hits == ctx.world * n - distinct, (hits, ctx.world * n, distinct)
+    line = {"workload": "llama3-70b KV: 8192 x 5 MiB per GPU, 30% "
+                        "Zipf(1.1) copies of a 1024-block pool shared by "
+                        "all GPUs, every copy in its own buffer; "
+                        "content-addressed INT8 PUT",
+            "metric": METRIC, "unit": UNIT, "n_gpus": ctx.world,
+            "value": ctx.world * n * bb / (ms * 1e-3) / 1e9,
+            "ms_per_step": ms, "steps": args.steps, "warmup": args.warmup,
+            "blocks_total": ctx.world * n, "block_bytes": bb,
+            "hbm_pool_gib_per_gpu": args.cap_gib,
+            "dedup_hits_total": hits,
+            "expected_hits": ctx.world * n - distinct,
+            "gpu_evictions_total": int(ev[:, pool_n + 2].sum()),
+            "parallelism": f"sharded index x{ctx.world}" if ctx.world > 1
+            else "1 GPU"}
+    if ctx.rank == 0:
         print(json.dumps(line), flush=True)
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
+    if ctx.world > 1:
+        ctx.dist.barrier()
+        ctx.dist.destroy_process_group()
 
 
 def main():

@@ -41,6 +41,21 @@ __global__ void __launch_bounds__(256)
 
 void count_launches(int k) { g_launches.fetch_add((uint64_t)k); }
 
+int sm_count() {
+  constexpr int kMaxDevices = 64;
+  static std::atomic<int> cached[kMaxDevices];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
+    dev = 0;
+  int v = cached[dev].load(std::memory_order_relaxed);
+  if (v > 0) return v;
+  if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) !=
+          cudaSuccess || v <= 0)
+    v = 1;  // the launch that follows reports the device error
+  cached[dev].store(v, std::memory_order_relaxed);
+  return v;
+}
+
 void set_error(const std::string &msg) { g_error = msg; }
 void clear_error() { g_error.clear(); }
 const char *last_error() { return g_error.c_str(); }
@@ -75,7 +90,7 @@ extern "C" int cascade_diag_sha_peak(int device, uint32_t chunks_per_thread,
   CB_CHECK(gbps && ms && chunks_per_thread > 0, CASCADE_ERR_INVALID,
            "bad argument");
   CB_CUDA(cudaSetDevice(device));
-  const int threads = 256, blocks = cb::kSmCount * 8;  // 64 warps per SM
+  const int threads = 256, blocks = cb::sm_count() * 8;  // 64 warps per SM
   uint32_t *sink = nullptr;
   CB_CUDA(cudaMalloc(&sink, sizeof(uint32_t)));
   cudaEvent_t a, b;

@@ -35,12 +35,14 @@ int cuda_fail(cudaError_t e, const char *what);
     }                                                                         \
   } while (0)
 
-constexpr int kSmCount = 148;  // B200: 2 dies x 74 SMs
+// Streaming multiprocessors of the current device (148 on a B200), read
+// from the device once per device and cached.
+int sm_count();
 
 // Grid size for a grid-stride kernel: a multiple of the SM count.
 inline int grid_for(uint64_t work_items, int per_block, int blocks_per_sm) {
   uint64_t want = (work_items + per_block - 1) / per_block;
-  uint64_t cap = (uint64_t)kSmCount * blocks_per_sm;
+  uint64_t cap = (uint64_t)sm_count() * blocks_per_sm;
   if (want > cap) want = cap;
   if (want < 1) want = 1;
   return (int)want;

@@ -44,6 +44,16 @@ int launch_quantize(const uint64_t *d_ptrs, const uint64_t *d_sizes, int n,
                     const uint64_t *d_dsts, uint8_t *d_headers,
                     int header_inline, cudaStream_t s, size_t smem_pad = 0);
 
+// Single-pass compression (min/max and codes in one HBM read, clusters of
+// CTAs exchanging their partial min/max through distributed shared memory).
+// Returns CASCADE_ERR_UNSUPPORTED, launching nothing, when max_size is too
+// large for the blocks in flight to stay in L2; the caller then uses
+// launch_minmax + launch_quantize.
+int launch_compress_fused(const uint64_t *d_ptrs, const uint64_t *d_sizes,
+                          int n, uint64_t max_size, const uint64_t *d_dsts,
+                          uint8_t *d_headers, int header_inline,
+                          cudaStream_t s);
+
 int launch_dequantize(const uint64_t *d_srcs, const uint8_t *d_headers,
                       int header_inline, const uint64_t *d_out_sizes, int n,
                       uint64_t max_out_size, const uint64_t *d_dsts,

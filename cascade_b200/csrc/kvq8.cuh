@@ -22,16 +22,22 @@ namespace q8 {
 
 struct Params {
   float scale;
-  float inv;    // 1 / scale, correctly rounded
-  float min_f;  // (float)min
+  float inv;       // 1 / scale, correctly rounded
+  float min_f;     // (float)min
+  uint32_t mn_u;   // min as a 16-bit pattern, for modular differences
   int8_t zp;
 };
+
+// 2^23 as a float and its bit pattern: for 0 <= k < 2^23,
+// __int_as_float(kMagicBits | k) == 2^23 + k exactly.
+constexpr float kMagic = 8388608.0f;
+constexpr uint32_t kMagicBits = 0x4B000000u;
 
 __device__ __forceinline__ Params params_from_minmax(int mn, int mx,
                                                      bool empty) {
   Params p;
   if (empty) {  // no elements: defined here as scale 1, zp 0
-    p.scale = 1.0f; p.inv = 1.0f; p.min_f = 0.0f; p.zp = 0;
+    p.scale = 1.0f; p.inv = 1.0f; p.min_f = 0.0f; p.mn_u = 0; p.zp = 0;
     return p;
   }
   float range = __fsub_rn((float)mx, (float)mn);
@@ -40,27 +46,46 @@ __device__ __forceinline__ Params params_from_minmax(int mn, int mx,
       __fdiv_rn((float)mn, p.scale));
   p.inv = __fdiv_rn(1.0f, p.scale);
   p.min_f = (float)mn;
+  p.mn_u = (uint32_t)mn & 0xffffu;
   return p;
 }
 
+// The code of one value, from d = v - min (0 <= d <= 65535, v from the
+// block the min was taken over), without integer/float conversion
+// instructions (a quarter-rate pipe on this GPU):
+//   x = 2^23 + d - 2^23           == (float)v - (float)min, exactly
+//   r = fma(x, inv, 0.5)          the reference's rounding, one FMA
+//   floor(r) = bits(RD(r + 2^23)) - bits(2^23), exact for 0 <= r < 2^23
+// and r = d * inv + 0.5 stays below 256 (d <= max - min, inv ~ 255 / range),
+// so the clamp to [0, 255] reduces to min(q, 255).  Returns the 32-bit
+// pattern of RD(r + 2^23) clamped, whose low byte is q (0..255).
+__device__ __forceinline__ uint32_t code_bits(uint32_t d, const Params &p) {
+  const float x = __fsub_rn(__uint_as_float(kMagicBits | d), kMagic);
+  const float r = __fmaf_rn(x, p.inv, 0.5f);
+  return min(__float_as_uint(__fadd_rd(r, kMagic)), kMagicBits | 255u);
+}
+
 __device__ __forceinline__ uint32_t code(int v, const Params &p) {
-  int q = __float2int_rz(__fmaf_rn(__fsub_rn((float)v, p.min_f), p.inv, 0.5f));
-  q = q < 0 ? 0 : (q > 255 ? 255 : q);
-  return (uint32_t)(q - 128) & 0xffu;
+  const uint32_t d = ((uint32_t)v - p.mn_u) & 0xffffu;
+  return (code_bits(d, p) & 0xffu) ^ 0x80u;  // (q - 128) as a byte
 }
 
 // Eight int16 values packed in a uint4 -> eight code bytes in a uint2.
 __device__ __forceinline__ uint2 codes8(uint4 v, const Params &p) {
-  uint32_t w[4] = {v.x, v.y, v.z, v.w};
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+  const uint32_t mhi = p.mn_u << 16;
   uint32_t c[8];
 #pragma unroll
   for (int k = 0; k < 4; ++k) {
-    c[2 * k] = code((int)(int16_t)(w[k] & 0xffffu), p);
-    c[2 * k + 1] = code((int)(int16_t)(w[k] >> 16), p);
+    c[2 * k] = code_bits((w[k] - p.mn_u) & 0xffffu, p);
+    c[2 * k + 1] = code_bits((w[k] - mhi) >> 16, p);
   }
+  // Low bytes of c[0..3] and c[4..7], then q - 128 on all four bytes.
   uint2 r;
-  r.x = c[0] | (c[1] << 8) | (c[2] << 16) | (c[3] << 24);
-  r.y = c[4] | (c[5] << 8) | (c[6] << 16) | (c[7] << 24);
+  r.x = __byte_perm(__byte_perm(c[0], c[1], 0x0040),
+                    __byte_perm(c[2], c[3], 0x0040), 0x5410) ^ 0x80808080u;
+  r.y = __byte_perm(__byte_perm(c[4], c[5], 0x0040),
+                    __byte_perm(c[6], c[7], 0x0040), 0x5410) ^ 0x80808080u;
   return r;
 }
 
@@ -76,9 +101,13 @@ __device__ __forceinline__ DeParams deparams(uint32_t scale_bits, int8_t zp) {
   return d;
 }
 
+// (float)code + 128 is the integer code ^ 0x80 (0..255), made exactly
+// with the 2^23 pattern instead of a conversion instruction.
 __device__ __forceinline__ uint32_t value(uint32_t code_byte,
                                           const DeParams &d) {
-  float x = __fadd_rn((float)(int8_t)(uint8_t)code_byte, 128.0f);
+  const float x =
+      __fsub_rn(__uint_as_float(kMagicBits | ((code_byte & 0xffu) ^ 0x80u)),
+                kMagic);
   return (uint32_t)__float2int_rz(__fmaf_rn(x, d.scale, d.min_f)) & 0xffffu;
 }
 

@@ -427,7 +427,7 @@ int launch_sha256_range(const uint64_t *d_ptrs, const uint64_t *d_sizes,
   // (8192 chains: 610 GB/s against 523 for the other form).  Beyond that,
   // warps share schedulers, the ALU pipe is the limit and the round with the
   // fewest ALU instructions wins (12288 chains: 526 against 490).
-  if (n <= 2 * 32 * kSmCount)
+  if (n <= 2 * 32 * sm_count())
     return launch_sha256_pipelined<1, 4, 1, 64, 8>(
         d_ptrs, d_sizes, n, d_digests, d_state, c_begin, c_end, s);
   return launch_sha256_pipelined<2, 3, 0, 16, 0>(d_ptrs, d_sizes, n, d_digests,
@@ -437,7 +437,7 @@ int launch_sha256_range(const uint64_t *d_ptrs, const uint64_t *d_sizes,
 size_t sha256_neighbour_smem(int n) {
   SmemLimits lim;
   if (n <= 0 || smem_limits(&lim) != CASCADE_OK) return 0;
-  const int per_cta = n <= 2 * 32 * kSmCount ? 32 : 64;  // chains per CTA
+  const int per_cta = n <= 2 * 32 * lim.sms ? 32 : 64;  // chains per CTA
   return fills_sms(lim, (n + per_cta - 1) / per_cta) ? kHashNeighbourSmem : 0;
 }
 

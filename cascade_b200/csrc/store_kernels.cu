@@ -176,30 +176,64 @@ __global__ void scan_kernel(const Slot *__restrict__ slots, uint64_t nslots,
   }
 }
 
+// Bump space is claimed with compare-and-swap, advancing only when the
+// request fits, so a request that fails never moves the bump offset and
+// cannot make a smaller concurrent request fail.  Each warp claims its
+// lanes' total in one CAS loop; if the total does not fit, the lanes try
+// one at a time in lane order.  Every failed CAS means another warp
+// advanced the offset, so the loops end.
+__device__ __forceinline__ uint64_t claim_bump(PoolDev *pool, uint64_t bytes) {
+  unsigned long long *bp = reinterpret_cast<unsigned long long *>(&pool->bump);
+  unsigned long long cur = *reinterpret_cast<volatile unsigned long long *>(bp);
+  while (cur + bytes <= pool->capacity) {
+    const unsigned long long prev = atomicCAS(bp, cur, cur + bytes);
+    if (prev == cur) return cur;
+    cur = prev;
+  }
+  return kInvalidOffset;
+}
+
 __global__ void pool_alloc_kernel(PoolDev *pool, const uint64_t *__restrict__ req,
                                   int n, uint64_t *__restrict__ offsets) {
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= n) return;
-  const uint64_t want = req[i];
-  if (want == kNoRequest) { offsets[i] = kInvalidOffset; return; }
-  const int c = size_class(want);
-  const uint64_t bytes = class_bytes(c);
-  const uint32_t k = atomicAdd(&pool->taken[c], 1u);
-  const uint32_t top = pool->top[c];  // not written by this kernel
-  if (k < top) {
-    offsets[i] = pool->stack[c][top - 1 - k];
-    return;
-  }
-  unsigned long long off =
-      atomicAdd(reinterpret_cast<unsigned long long *>(&pool->bump),
-                (unsigned long long)bytes);
-  if (off + bytes > pool->capacity) {
-    atomicAdd(reinterpret_cast<unsigned long long *>(&pool->bump),
-              (unsigned long long)(0ull - bytes));
+  const int lane = threadIdx.x & 31;
+  const uint64_t want = i < n ? req[i] : kNoRequest;
+  bool need_bump = false;
+  uint64_t bytes = 0;
+  if (want != kNoRequest) {
+    const int c = size_class(want);
+    bytes = class_bytes(c);
+    const uint32_t k = atomicAdd(&pool->taken[c], 1u);
+    const uint32_t top = pool->top[c];  // not written by this kernel
+    if (k < top)
+      offsets[i] = pool->stack[c][top - 1 - k];
+    else
+      need_bump = true;
+  } else if (i < n) {
     offsets[i] = kInvalidOffset;
+  }
+  const unsigned m = __ballot_sync(0xffffffffu, need_bump);
+  if (!m) return;
+  // Inclusive prefix of the bump requests' bytes in lane order.
+  uint64_t incl = need_bump ? bytes : 0;
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    const uint64_t up = __shfl_up_sync(0xffffffffu, incl, d);
+    if (lane >= d) incl += up;
+  }
+  const uint64_t total = __shfl_sync(0xffffffffu, incl, 31);
+  const int leader = __ffs(m) - 1;
+  uint64_t base = 0;
+  if (lane == leader) base = claim_bump(pool, total);
+  base = __shfl_sync(0xffffffffu, base, leader);
+  if (base != kInvalidOffset) {
+    if (need_bump) offsets[i] = base + incl - bytes;
     return;
   }
-  offsets[i] = off;
+  for (int l = 0; l < 32; ++l) {
+    if (lane == l && need_bump) offsets[i] = claim_bump(pool, bytes);
+    __syncwarp();
+  }
 }
 
 __global__ void pool_alloc_finish_kernel(PoolDev *pool) {

@@ -72,16 +72,19 @@ int cascade_kv_compress_batch(const uint64_t *d_src, const uint64_t *d_sizes,
  * engine that reserved nearly all of HBM for its own KV cache at start-up,
  * or an ingest loop that cannot risk an allocator call stalling or failing
  * mid-step.  It calls no cudaMalloc, cudaFree or other allocating routine;
- * its per-block scratch is a fixed 512 KiB array built into the library,
- * present on every GPU that loads the library until the process exits.
+ * its per-block scratch is a fixed 512 KiB array built into the library.
  * Limits and rules:
  *   - at most 65536 blocks per call; larger n fails with
  *     CASCADE_ERR_INVALID and an explanatory cascade_last_error();
+ *   - CUDA places the array on a GPU lazily, at the first call on that GPU
+ *     (which also looks up the array's device address, a one-time set-up),
+ *     and it stays there until the process exits.  A call with n = 0 does
+ *     only this set-up: make it on each GPU before reserving that GPU's
+ *     memory and before any stream capture.  The set-up is redone by
+ *     itself after the device's context changes (cudaDeviceReset);
  *   - all calls on a GPU share that one array, so calls whose work overlaps
  *     on the same GPU race: keep them on one stream;
- *   - the first call on each GPU looks up the array's device address (a
- *     one-time set-up); make that first call before any stream capture;
- *   - `stream` must belong to the current device. */
+ *   - `stream` must belong to the current device (else CASCADE_ERR_INVALID). */
 int cascade_kv_compress_batch_noalloc(const uint64_t *d_src,
                                       const uint64_t *d_sizes,
                                       const uint64_t *d_dst, size_t n,

@@ -23,6 +23,45 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 ORACLE_SO = os.path.join(HERE, "_build", "liboracle.so")
 REF_SO = os.path.join(HERE, "_ref", "libcascade_ref.so")
+# The same reference sources built with the bench host's -march=native
+# expansion (oracle/native_march.txt); the timed CPU baseline there.
+REF_NATIVE_SO = os.path.join(HERE, "_ref", "native", "libcascade_ref.so")
+NATIVE_MARCH_TXT = os.path.join(HERE, "native_march.txt")
+
+
+def host_march() -> Optional[str]:
+    """The options GCC's -march=native expands to on this host (one line),
+    or None when no compiler is available."""
+    import subprocess
+    try:
+        out = subprocess.run(["sh", os.path.join(HERE, "probe_march.sh")],
+                             capture_output=True, text=True, timeout=60)
+    except (OSError, subprocess.TimeoutExpired):
+        return None
+    line = out.stdout.strip()
+    return line if out.returncode == 0 and line else None
+
+
+def native_build_matches_host() -> bool:
+    """Whether oracle/_ref/native was built with exactly this host's
+    -march=native options (so it is the reference's own native build)."""
+    if not os.path.exists(REF_NATIVE_SO):
+        return False
+    here = host_march()
+    with open(NATIVE_MARCH_TXT) as f:
+        built = f.read().strip()
+    return here is not None and here.split() == built.split()
+
+
+def cpu_model() -> str:
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
 
 _u8p = ctypes.POINTER(ctypes.c_uint8)
 _lib = None

@@ -25,12 +25,15 @@ import numpy as np
 
 
 def run(blocks: np.ndarray, threads: int, min_seconds: float,
-        max_passes: int = 1000, warmup: int = 1, steps: int = 0):
+        max_passes: int = 1000, warmup: int = 1, steps: int = 0,
+        lib_path: str = ""):
     """Times put passes over `blocks` (each into an emptied store): exactly
     `steps` passes when steps > 0, else passes until min_seconds."""
     import oracle
+    if lib_path:
+        oracle.REF_SO = lib_path
     if oracle.ref() is None:
-        raise SystemExit("oracle/_ref/libcascade_ref.so is not built")
+        raise SystemExit(f"{oracle.REF_SO} is not built")
     n, size = blocks.shape
     rows = [blocks[i] for i in range(n)]
     shm_dir = tempfile.mkdtemp(prefix="cascade_ref_", dir="/dev/shm")
@@ -70,11 +73,13 @@ def main():
     ap.add_argument("--max-passes", type=int, default=1000)
     ap.add_argument("--warmup", type=int, default=1)
     ap.add_argument("--steps", type=int, default=0)
+    ap.add_argument("--lib", default="",
+                    help="reference build to time (default oracle/_ref)")
     a = ap.parse_args()
     blocks = np.load(a.input, mmap_mode="r")
     blocks = np.ascontiguousarray(blocks)
     print(json.dumps(run(blocks, a.threads, a.min_seconds, a.max_passes,
-                         a.warmup, a.steps)))
+                         a.warmup, a.steps, a.lib)))
 
 
 if __name__ == "__main__":

@@ -213,10 +213,15 @@ def store_scenarios():
 
 
 def main():
-    if not os.path.isdir("/root/reference"):
-        sys.exit("needs the reference tree to build oracle/_ref")
-    subprocess.check_call(["make", "-s", "-C", os.path.join(ROOT, "oracle"),
-                           "oracle", "ref"])
+    # The reference's C++ tree: oracle/Makefile's REF, or the directory in
+    # CASCADE_REFERENCE_CPP.
+    make = ["make", "-s", "-C", os.path.join(ROOT, "oracle")]
+    if os.environ.get("CASCADE_REFERENCE_CPP"):
+        make.append("REF=" + os.environ["CASCADE_REFERENCE_CPP"])
+    if subprocess.run(make + ["-n", "ref"], capture_output=True).returncode:
+        sys.exit("needs the reference tree to build oracle/_ref "
+                 "(set CASCADE_REFERENCE_CPP)")
+    subprocess.check_call(make + ["oracle", "ref"])
     sha_cases()
     kvq8_cases()
     store_scenarios()

@@ -104,3 +104,30 @@ def test_copy_batch_ragged():
             h = d.cpu().numpy()
             assert np.array_equal(h[:x.size], x)
             assert not h[x.size:].any()   # nothing written past the end
+
+
+@pytest.mark.parametrize("misalign", [0, 2, 8])
+def test_single_pass_compress_mixed_batch_vs_oracle(misalign):
+    # Batches whose largest block is 1-2 MiB take the single-pass cluster
+    # kernel.  64 blocks (several per cluster, so the look-ahead and the
+    # pair exchange run in steady state) of ragged sizes: odd, tiny, empty
+    # and not a multiple of the 16-byte groups; misaligned sources take the
+    # kernel's direct path.
+    rng = np.random.default_rng(40 + misalign)
+    sizes = [2 << 20, (2 << 20) - 2, (1 << 20) + 6, 0, 1, 100,
+             (3 << 19) + 3, 1 << 20]
+    xs = []
+    for i in range(64):
+        n = sizes[i % len(sizes)]
+        if i % 3 == 0:      # KV-like values with outliers
+            x = (rng.standard_normal(n // 2 + 1) * 3).astype(np.float16)
+            x[::997] *= 20
+            xs.append(x.view(np.uint8)[:n].copy())
+        else:               # arbitrary int16 ranges
+            lo = int(rng.integers(-32768, 32767))
+            hi = int(rng.integers(lo, 32768))
+            xs.append(rng.integers(lo, hi + 1, n // 2 + 1)
+                      .astype(np.int16).view(np.uint8)[:n].copy())
+    got = _compress(xs, misalign)
+    for i, x in enumerate(xs):
+        _assert_same_comp(got[i], oracle.kv_compress(x))
