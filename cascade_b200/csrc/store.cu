@@ -133,6 +133,7 @@ struct Store {
   int shard_rank = 0;            // this store's rank in the open batch
   size_t shard_open = 0;         // blocks of the open sharded batch
   size_t shard_get_open = 0;     // keys of the open sharded get
+  size_t resolve_pending = 0;    // records of a resolve not yet counted
   // Pools of the other ranks mapped into this process (CUDA IPC); entry
   // peer_rank is this store's own pool.
   std::vector<uint8_t *> peer_base;
@@ -1645,18 +1646,24 @@ static int put_batch_host_locked(Store &st, size_t n,
 }
 
 // ------------------------------------------------------- sharded dedup
+// Exchange buffers are padded: `world` segments of `cap` entries, segment r
+// for rank r, so that both all-to-alls move equal splits and no rank needs
+// to learn the others' counts.  An entry whose src_idx is kUnused (the
+// buffers are filled with 0xff bytes) carries nothing.
 namespace {
 
+// One record per block, written into its owner's segment.  A segment that
+// overflows `cap` is an error (the caller's cap is below the batch size).
 __global__ void shard_records_kernel(int n, int world, uint32_t rank,
-                                     uint64_t seq_base,
+                                     uint64_t seq_base, uint32_t cap,
                                      const uint64_t *__restrict__ digests,
                                      const uint64_t *__restrict__ off,
                                      const uint64_t *__restrict__ sizes,
                                      const uint32_t *__restrict__ flags,
                                      const uint8_t *__restrict__ hdr,
-                                     ShardRecord *__restrict__ tmp,
-                                     int *__restrict__ owner,
-                                     uint32_t *__restrict__ counts) {
+                                     uint32_t *__restrict__ cursor,
+                                     ShardRecord *__restrict__ out,
+                                     int *__restrict__ err) {
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n) return;
   ShardRecord r;
@@ -1673,28 +1680,16 @@ __global__ void shard_records_kernel(int n, int world, uint32_t rank,
                 ((uint32_t)h[2] << 16) | ((uint32_t)h[3] << 24);
   r.hdr_zp = h[4];
   r.pad = 0;
-  tmp[i] = r;
   const int o = owner_of(r.k0, world);
-  owner[i] = o;
-  atomicAdd(&counts[o], 1u);
+  const uint32_t k = atomicAdd(&cursor[o], 1u);
+  if (k < cap)
+    out[(size_t)o * cap + k] = r;
+  else
+    atomicExch(err, CASCADE_ERR_INVALID);
 }
 
-// Groups the records by owner rank (order inside a group is free: the
-// owner decides by sequence number).
-__global__ void shard_scatter_kernel(int n, int world,
-                                     const ShardRecord *__restrict__ tmp,
-                                     const int *__restrict__ owner,
-                                     const uint32_t *__restrict__ counts,
-                                     uint32_t *__restrict__ cursor,
-                                     ShardRecord *__restrict__ out) {
-  const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= n) return;
-  const int o = owner[i];
-  uint32_t base = 0;
-  for (int j = 0; j < o; ++j) base += counts[j];
-  out[base + atomicAdd(&cursor[o], 1u)] = tmp[i];
-}
-
+// Unused records get no key and the sequence number kNoSeq, which the
+// claim step skips (their status becomes FAILED and is never sent back).
 __global__ void shard_unpack_kernel(int m, uint32_t rank,
                                     const ShardRecord *__restrict__ in,
                                     uint64_t *__restrict__ keys,
@@ -1706,13 +1701,15 @@ __global__ void shard_unpack_kernel(int m, uint32_t rank,
   const int j = blockIdx.x * blockDim.x + threadIdx.x;
   if (j >= m) return;
   const ShardRecord r = in[j];
+  const bool used = r.src_idx != kUnused;
   keys[2 * (size_t)j] = r.k0;
   keys[2 * (size_t)j + 1] = r.k1;
-  seqs[j] = r.seq;
-  off[j] = r.offset;
-  sizes[j] = r.size;
-  flags[j] = (r.flags & 0xffffu) | ((r.holder & 0xffu) << 16) |
-             (r.holder != rank ? (uint32_t)kFlagRemote : 0u);
+  seqs[j] = used ? r.seq : kNoSeq;
+  off[j] = used ? r.offset : kInvalidOffset;
+  sizes[j] = used ? r.size : 0;
+  flags[j] = used ? ((r.flags & 0xffffu) | ((r.holder & 0xffu) << 16) |
+                     (r.holder != rank ? (uint32_t)kFlagRemote : 0u))
+                  : 0u;
   uint8_t *h = hdr + 8 * (size_t)j;
   h[0] = r.hdr_scale & 0xff; h[1] = (r.hdr_scale >> 8) & 0xff;
   h[2] = (r.hdr_scale >> 16) & 0xff; h[3] = r.hdr_scale >> 24;
@@ -1726,7 +1723,7 @@ __global__ void shard_reply_kernel(int m, const ShardRecord *__restrict__ in,
   if (j >= m) return;
   ShardReply r;
   r.src_idx = in[j].src_idx;
-  r.status = status[j];
+  r.status = r.src_idx == kUnused ? kUnused : status[j];
   out[j] = r;
 }
 
@@ -1737,6 +1734,7 @@ __global__ void shard_apply_kernel(int m, int n,
   const int j = blockIdx.x * blockDim.x + threadIdx.x;
   if (j >= m) return;
   const ShardReply r = back[j];
+  if (r.src_idx == kUnused) return;
   if (r.src_idx < (uint32_t)n && r.status <= CASCADE_PUT_FAILED)
     status[r.src_idx] = (uint8_t)r.status;
   else
@@ -1747,65 +1745,101 @@ inline int nblocks(size_t n) { return (int)((n + 255) / 256); }
 
 }  // namespace
 
+// Counts the keys the last cascade_shard_resolve stored, once its device
+// work is done (it returns without waiting), and reports an index that ran
+// out of probes there.
+static int settle_resolve(Store &st) {
+  if (!st.resolve_pending) return CASCADE_OK;
+  const size_t m = st.resolve_pending;
+  st.resolve_pending = 0;
+  CB_CUDA(cudaStreamSynchronize(st.s));
+  for (size_t j = 0; j < m; ++j)
+    st.claimed += st.oc.h_status[j] == CASCADE_PUT_STORED;
+  if (*st.oc.h_err) {
+    set_error("device index is full: raise index_slots");
+    return CASCADE_ERR_FULL;
+  }
+  return CASCADE_OK;
+}
+
+// The caller's stream waits for the store's main stream: outputs written
+// there (exchange buffers) are ready on `stream` when an ABI call returns
+// without synchronising.
+static int join_back(Store &st, void *stream) {
+  CB_CUDA(cudaEventRecord(st.ev, st.s));
+  CB_CUDA(cudaStreamWaitEvent(static_cast<cudaStream_t>(stream), st.ev, 0));
+  return CASCADE_OK;
+}
+
 // The batch's descriptors are uploaded (and, with digests_ready, its hash is
 // under way on the hash stream): store it speculatively and write the
-// records.
+// records.  Does not wait for the device.
 static int shard_begin_staged(Store &st, size_t n, uint64_t max_size,
                               bool digests_ready, const uint8_t *h_prefix,
                               int world, int rank, uint64_t seq_base,
-                              uint8_t *d_send, uint64_t *h_counts) {
+                              size_t cap, uint8_t *d_send) {
   int rc;
   CB_CHECK(can_speculate(st, n), CASCADE_ERR_NOMEM,
            "sharded put: the HBM pool cannot hold the whole batch");
-  // per-batch device space: n staged records, n owner ids, 2 x 256 counters
-  const size_t need = n * sizeof(ShardRecord) + n * sizeof(int) + 2048;
-  static_assert(sizeof(ShardRecord) % 16 == 0, "record alignment");
-  if ((rc = ensure_device_buf(st.shard_aux, st.oc_aux_cap, need, st.s))) return rc;
-  ShardRecord *tmp = reinterpret_cast<ShardRecord *>(st.shard_aux);
-  int *owner = reinterpret_cast<int *>(st.shard_aux + n * sizeof(ShardRecord));
-  uint32_t *counts = reinterpret_cast<uint32_t *>(
-      st.shard_aux + n * sizeof(ShardRecord) + ((n * sizeof(int) + 255) & ~size_t(255)));
-  uint32_t *cursor = counts + 256;
+  if ((rc = ensure_device_buf(st.shard_aux, st.oc_aux_cap, 2048, st.s)))
+    return rc;
+  uint32_t *cursor = reinterpret_cast<uint32_t *>(st.shard_aux);
   if ((rc = speculate_local(st, n, h_prefix, max_size, digests_ready)))
     return rc;
   cudaStream_t s = st.s;
   CB_CUDA(cudaStreamWaitEvent(s, st.ev2, 0));
-  CB_CUDA(cudaMemsetAsync(counts, 0, 2 * 256 * sizeof(uint32_t), s));
+  CB_CUDA(cudaMemsetAsync(cursor, 0, 256 * sizeof(uint32_t), s));
+  CB_CUDA(cudaMemsetAsync(st.sc.err, 0, sizeof(int), s));
   shard_records_kernel<<<nblocks(n), 256, 0, s>>>(
-      (int)n, world, (uint32_t)rank, seq_base,
+      (int)n, world, (uint32_t)rank, seq_base, (uint32_t)cap,
       reinterpret_cast<const uint64_t *>(st.sc.digests), st.sc.off,
-      st.sc.sizes, st.sc.flags, st.sc.hdr, tmp, owner, counts);
-  count_launches(1);
-  shard_scatter_kernel<<<nblocks(n), 256, 0, s>>>(
-      (int)n, world, tmp, owner, counts, cursor,
-      reinterpret_cast<ShardRecord *>(d_send));
+      st.sc.sizes, st.sc.flags, st.sc.hdr, cursor,
+      reinterpret_cast<ShardRecord *>(d_send), st.sc.err);
   count_launches(1);
   CB_CUDA(cudaGetLastError());
-  uint32_t hc[256];
-  CB_CUDA(cudaMemcpyAsync(hc, counts, world * sizeof(uint32_t),
-                          cudaMemcpyDeviceToHost, s));
   CB_CUDA(cudaMemcpyAsync(st.sc.h_off, st.sc.off, n * 8,
                           cudaMemcpyDeviceToHost, s));
-  CB_CUDA(cudaStreamSynchronize(s));
-  for (int r = 0; r < world; ++r) h_counts[r] = hc[r];
+  CB_CUDA(cudaMemcpyAsync(st.sc.h_err, st.sc.err, sizeof(int),
+                          cudaMemcpyDeviceToHost, s));
   st.shard_rank = rank;
   st.shard_open = n;
   return CASCADE_OK;
 }
 
-static int shard_begin(Store &st, size_t n, const uint64_t *h_ptrs,
-                       const uint64_t *h_sizes, const uint8_t *h_prefix,
-                       int world, int rank, uint64_t seq_base, uint8_t *d_send,
-                       uint64_t *h_counts) {
+static int shard_check(const Store &st, size_t n, int world, int rank,
+                       size_t cap) {
   CB_CHECK(world >= 1 && world <= 256 && rank >= 0 && rank < world,
            CASCADE_ERR_INVALID, "bad world/rank");
+  CB_CHECK(cap >= n && cap <= (size_t)INT32_MAX / (size_t)world,
+           CASCADE_ERR_INVALID,
+           "cap must be at least the batch size (and world * cap < 2^31)");
   CB_CHECK(st.hbm, CASCADE_ERR_UNSUPPORTED,
            "sharded puts need the HBM tier (use_gpu)");
+  return CASCADE_OK;
+}
+
+// Fills the padded send buffer with unused entries on the main stream.
+static int fill_unused(Store &st, uint8_t *d_send, size_t bytes) {
+  CB_CUDA(cudaMemsetAsync(d_send, 0xff, bytes, st.s));
+  return CASCADE_OK;
+}
+
+static int shard_begin(Store &st, size_t n, const uint64_t *h_ptrs,
+                       const uint64_t *h_sizes, const uint8_t *h_prefix,
+                       int world, int rank, uint64_t seq_base, size_t cap,
+                       uint8_t *d_send) {
+  int rc = shard_check(st, n, world, rank, cap);
+  if (!rc) rc = fill_unused(st, d_send, (size_t)world * cap * sizeof(ShardRecord));
+  if (rc || n == 0) {
+    st.shard_rank = rank;
+    st.shard_open = 0;
+    return rc;
+  }
   uint64_t max_size = 0;
-  int rc = upload_batch(st, n, h_ptrs, h_sizes, nullptr, &max_size);
-  if (rc) return rc;
+  if ((rc = upload_batch(st, n, h_ptrs, h_sizes, nullptr, &max_size)))
+    return rc;
   return shard_begin_staged(st, n, max_size, false, h_prefix, world, rank,
-                            seq_base, d_send, h_counts);
+                            seq_base, cap, d_send);
 }
 
 // Host blocks: staged to the device first.  Uniform pinned batches are
@@ -1813,11 +1847,14 @@ static int shard_begin(Store &st, size_t n, const uint64_t *h_ptrs,
 static int shard_begin_host(Store &st, size_t n, const uint8_t *const *blocks,
                             const uint64_t *sizes, const uint8_t *h_prefix,
                             int world, int rank, uint64_t seq_base,
-                            uint8_t *d_send, uint64_t *h_counts) {
-  CB_CHECK(world >= 1 && world <= 256 && rank >= 0 && rank < world,
-           CASCADE_ERR_INVALID, "bad world/rank");
-  CB_CHECK(st.hbm, CASCADE_ERR_UNSUPPORTED,
-           "sharded puts need the HBM tier (use_gpu)");
+                            size_t cap, uint8_t *d_send) {
+  int rc = shard_check(st, n, world, rank, cap);
+  if (!rc) rc = fill_unused(st, d_send, (size_t)world * cap * sizeof(ShardRecord));
+  if (rc || n == 0) {
+    st.shard_rank = rank;
+    st.shard_open = 0;
+    return rc;
+  }
   uint64_t need = 0;
   for (size_t i = 0; i < n; ++i)
     need += payload_bytes(sizes[i], q8_eligible(st, sizes[i], false));
@@ -1825,19 +1862,22 @@ static int shard_begin_host(Store &st, size_t n, const uint8_t *const *blocks,
            "sharded put: the HBM pool cannot hold the whole batch");
   bool taken = false;
   uint64_t max_size = 0;
-  int rc = stage_host_striped(st, n, blocks, sizes, &taken, &max_size);
-  if (rc) return rc;
+  if ((rc = stage_host_striped(st, n, blocks, sizes, &taken, &max_size)))
+    return rc;
   if (taken)
     return shard_begin_staged(st, n, max_size, true, h_prefix, world, rank,
-                              seq_base, d_send, h_counts);
+                              seq_base, cap, d_send);
   std::vector<uint64_t> ptrs;
   if ((rc = stage_host_blocks(st, n, blocks, sizes, ptrs))) return rc;
   if ((rc = upload_batch(st, n, ptrs.data(), sizes, nullptr, &max_size)))
     return rc;
   return shard_begin_staged(st, n, max_size, false, h_prefix, world, rank,
-                            seq_base, d_send, h_counts);
+                            seq_base, cap, d_send);
 }
 
+// As owner: decides the received records and writes one reply per record.
+// Does not wait for the device; the keys it stored are counted by the next
+// call on the store (settle_resolve).
 static int shard_resolve(Store &st, const uint8_t *d_recv, size_t m,
                          uint8_t *d_reply) {
   if (m == 0) return CASCADE_OK;
@@ -1871,26 +1911,30 @@ static int shard_resolve(Store &st, const uint8_t *d_recv, size_t m,
   CB_CUDA(cudaGetLastError());
   CB_CUDA(cudaMemcpyAsync(oc.h_status, oc.status, m, cudaMemcpyDeviceToHost, s));
   CB_CUDA(cudaMemcpyAsync(oc.h_err, oc.err, sizeof(int), cudaMemcpyDeviceToHost, s));
-  CB_CUDA(cudaStreamSynchronize(s));
-  if (*oc.h_err) {
-    set_error("device index is full: raise index_slots");
-    return CASCADE_ERR_FULL;
-  }
-  for (size_t j = 0; j < m; ++j) st.claimed += oc.h_status[j] == CASCADE_PUT_STORED;
+  st.resolve_pending = m;
   return CASCADE_OK;
 }
 
-static int shard_end(Store &st, const uint8_t *d_back, size_t n,
+static int shard_end(Store &st, const uint8_t *d_back, size_t m, size_t n,
                      uint8_t *h_status, uint8_t *h_digests,
                      uint64_t *n_stored) {
   CB_CHECK(st.shard_open == n, CASCADE_ERR_INVALID,
            "shard_put_end: no open batch of this size");
+  if (n == 0) return CASCADE_OK;
   cudaStream_t s = st.s;
+  // The records kernel's error word (a segment over cap) is already on its
+  // way to sc.h_err; read it once the stream is done.
+  CB_CUDA(cudaStreamSynchronize(s));
+  if (*st.sc.h_err) {
+    st.shard_open = 0;
+    set_error("shard_put_begin: a segment of the send buffer overflowed cap");
+    return CASCADE_ERR_INVALID;
+  }
   // 0xff marks "no reply yet"; every block must get exactly one reply.
   CB_CUDA(cudaMemsetAsync(st.sc.status, 0xff, n, s));
   CB_CUDA(cudaMemsetAsync(st.sc.err, 0, sizeof(int), s));
-  shard_apply_kernel<<<nblocks(n), 256, 0, s>>>(
-      (int)n, (int)n, reinterpret_cast<const ShardReply *>(d_back),
+  shard_apply_kernel<<<nblocks(m), 256, 0, s>>>(
+      (int)m, (int)n, reinterpret_cast<const ShardReply *>(d_back),
       st.sc.status, st.sc.err);
   count_launches(1);
   CB_CUDA(cudaGetLastError());
@@ -1920,13 +1964,17 @@ static int shard_end(Store &st, const uint8_t *d_back, size_t n,
 // ------------------------------------------------------------ sharded get
 namespace {
 
+// Unused queries look up the one unstorable key (kKeyMask), which is never
+// found, so they touch no entry.
 __global__ void shard_query_keys_kernel(int m,
                                         const ShardQuery *__restrict__ in,
                                         uint64_t *__restrict__ keys) {
   const int j = blockIdx.x * blockDim.x + threadIdx.x;
   if (j >= m) return;
-  keys[2 * (size_t)j] = in[j].k0;
-  keys[2 * (size_t)j + 1] = in[j].k1;
+  const ShardQuery q = in[j];
+  const bool used = q.src_idx != kUnused;
+  keys[2 * (size_t)j] = used ? q.k0 : kKeyMask0;
+  keys[2 * (size_t)j + 1] = used ? q.k1 : kKeyMask1;
 }
 
 // Holder of a live entry: the rank recorded at put time when the payload
@@ -1940,7 +1988,7 @@ __global__ void shard_locate_kernel(int m, uint32_t rank,
   const LookupInfo f = info[j];
   ShardLocation r;
   r.src_idx = in[j].src_idx;
-  r.found = f.found;
+  r.found = r.src_idx == kUnused ? 0 : f.found;
   r.flags = f.flags;
   r.holder = (f.flags & kFlagRemote) ? ((f.flags >> 16) & 0xffu) : rank;
   r.offset = f.offset;
@@ -1983,37 +2031,41 @@ static int shard_attach(Store &st, int world, int rank,
   return CASCADE_OK;
 }
 
+// Routes each key to its owner: the padded query buffer is built in pinned
+// memory and copied to d_send on the main stream.  Does not wait for it.
 static int shard_get_begin(Store &st, size_t n, const uint8_t *h_keys,
-                           uint8_t *d_send, uint64_t *h_counts) {
+                           size_t cap, uint8_t *d_send) {
   const int world = (int)st.peer_base.size();
   CB_CHECK(world > 0, CASCADE_ERR_INVALID,
            "sharded get: attach the ranks' pools first");
-  std::vector<uint64_t> counts(world, 0), cursor(world, 0);
-  std::vector<int> owner(n);
-  for (size_t i = 0; i < n; ++i) {
-    owner[i] = owner_of(le64(h_keys + 16 * i), world);
-    ++counts[owner[i]];
-  }
-  for (int r = 1; r < world; ++r) cursor[r] = cursor[r - 1] + counts[r - 1];
-  int rc = ensure_host_stage(st, n * sizeof(ShardQuery));
+  CB_CHECK(cap >= n && cap <= (size_t)INT32_MAX / (size_t)world,
+           CASCADE_ERR_INVALID,
+           "cap must be at least the batch size (and world * cap < 2^31)");
+  const size_t m = (size_t)world * cap;
+  int rc = ensure_host_stage(st, m * std::max(sizeof(ShardQuery),
+                                              sizeof(ShardLocation)));
   if (rc) return rc;
+  // The stage may still be the source of the last get's copy.
+  CB_CUDA(cudaStreamSynchronize(st.s));
   ShardQuery *q = reinterpret_cast<ShardQuery *>(st.h_stage);
+  std::memset(q, 0xff, m * sizeof(ShardQuery));
+  std::vector<size_t> cursor(world, 0);
   for (size_t i = 0; i < n; ++i) {
-    ShardQuery &r = q[cursor[owner[i]]++];
+    const int o = owner_of(le64(h_keys + 16 * i), world);
+    ShardQuery &r = q[(size_t)o * cap + cursor[o]++];
     r.k0 = le64(h_keys + 16 * i);
     r.k1 = le64(h_keys + 16 * i + 8);
     r.src_idx = (uint32_t)i;
     r.pad0 = 0;
     r.pad1 = 0;
   }
-  CB_CUDA(cudaMemcpyAsync(d_send, st.h_stage, n * sizeof(ShardQuery),
+  CB_CUDA(cudaMemcpyAsync(d_send, st.h_stage, m * sizeof(ShardQuery),
                           cudaMemcpyHostToDevice, st.s));
-  CB_CUDA(cudaStreamSynchronize(st.s));
-  for (int r = 0; r < world; ++r) h_counts[r] = counts[r];
   st.shard_get_open = n;
   return CASCADE_OK;
 }
 
+// As owner: one location per received query.  Does not wait for the device.
 static int shard_lookup(Store &st, const uint8_t *d_recv, size_t m,
                         uint8_t *d_reply) {
   CB_CHECK(st.peer_rank >= 0, CASCADE_ERR_INVALID,
@@ -2037,21 +2089,21 @@ static int shard_lookup(Store &st, const uint8_t *d_recv, size_t m,
       reinterpret_cast<ShardLocation *>(d_reply));
   count_launches(1);
   CB_CUDA(cudaGetLastError());
-  CB_CUDA(cudaStreamSynchronize(s));
   return CASCADE_OK;
 }
 
-static int shard_get_end(Store &st, const uint8_t *d_back, size_t n,
+static int shard_get_end(Store &st, const uint8_t *d_back, size_t m, size_t n,
                          const uint64_t *h_out, const uint64_t *h_caps,
                          uint64_t *h_sizes, uint8_t *h_found,
                          uint64_t *n_found) {
   CB_CHECK(st.shard_get_open == n, CASCADE_ERR_INVALID,
            "shard_get_end: no open get of this size");
   st.shard_get_open = 0;
+  if (n == 0) return CASCADE_OK;
   int rc = ensure_scratch(st, n);
-  if (!rc) rc = ensure_host_stage(st, n * sizeof(ShardLocation));
+  if (!rc) rc = ensure_host_stage(st, m * sizeof(ShardLocation));
   if (rc) return rc;
-  CB_CUDA(cudaMemcpyAsync(st.h_stage, d_back, n * sizeof(ShardLocation),
+  CB_CUDA(cudaMemcpyAsync(st.h_stage, d_back, m * sizeof(ShardLocation),
                           cudaMemcpyDeviceToHost, st.s));
   CB_CUDA(cudaStreamSynchronize(st.s));
   const ShardLocation *loc = reinterpret_cast<const ShardLocation *>(st.h_stage);
@@ -2059,11 +2111,14 @@ static int shard_get_end(Store &st, const uint8_t *d_back, size_t n,
   std::vector<uint8_t> seen(n, 0), deliver(n, 0);
   std::vector<uint64_t> bases(n, 0);
   uint64_t found = 0;
-  for (size_t j = 0; j < n; ++j) {
+  size_t named = 0;
+  for (size_t j = 0; j < m; ++j) {
     const ShardLocation &r = loc[j];
+    if (r.src_idx == kUnused) continue;
     CB_CHECK(r.src_idx < n && !seen[r.src_idx], CASCADE_ERR_INVALID,
              "shard_get_end: the locations do not name each key once");
     seen[r.src_idx] = 1;
+    ++named;
     LookupInfo &f = st.sc.h_info[r.src_idx];
     f.found = r.found;
     f.flags = r.flags;
@@ -2084,6 +2139,8 @@ static int shard_get_end(Store &st, const uint8_t *d_back, size_t n,
              "sharded get: the block is in a DRAM tier, not in HBM");
     bases[r.src_idx] = (uint64_t)(uintptr_t)st.peer_base[r.holder];
   }
+  CB_CHECK(named == n, CASCADE_ERR_INVALID,
+           "shard_get_end: the locations do not name each key once");
   for (size_t i = 0; i < n; ++i) {
     const LookupInfo &f = st.sc.h_info[i];
     const uint64_t size =
@@ -2121,7 +2178,8 @@ int join_caller(cb::Store &st, void *stream) {
   CB_CHECK((s) && (s)->impl, CASCADE_ERR_INVALID, "null store");             \
   cb::Store &st = *(s)->impl;                                                \
   std::lock_guard<std::mutex> lock(st.mu);                                   \
-  cb::DeviceGuard guard(st.dev)
+  cb::DeviceGuard guard(st.dev);                                             \
+  if (int settle_rc = cb::settle_resolve(st)) return settle_rc
 
 extern "C" void cascade_struct_sizes(size_t *config_bytes,
                                      size_t *stats_bytes) {
@@ -2319,45 +2377,36 @@ extern "C" int cascade_shard_put_begin(cascade_store_t *s, size_t n,
                                        const uint64_t *h_ptrs,
                                        const uint64_t *h_sizes,
                                        const uint8_t *h_prefix, int world,
-                                       int rank, uint64_t seq_base,
-                                       uint8_t *d_send,
-                                       uint64_t *h_send_counts,
-                                       void *stream) {
+                                       int rank, uint64_t seq_base, size_t cap,
+                                       uint8_t *d_send, void *stream) {
   STORE_ENTRY(s);
-  CB_CHECK(h_send_counts && (n == 0 || (h_ptrs && h_sizes && d_send)),
-           CASCADE_ERR_INVALID, "null argument");
+  CB_CHECK(d_send && (n == 0 || (h_ptrs && h_sizes)), CASCADE_ERR_INVALID,
+           "null argument");
   CB_CHECK(n <= (size_t)INT32_MAX, CASCADE_ERR_INVALID, "batch too large");
   CB_CHECK(((uintptr_t)d_send & 15u) == 0, CASCADE_ERR_INVALID,
            "d_send must be 16-byte aligned");
-  if (n == 0) {
-    for (int r = 0; r < world; ++r) h_send_counts[r] = 0;
-    st.shard_rank = rank;
-    st.shard_open = 0;
-    return CASCADE_OK;
-  }
   if (int rc = join_caller(st, stream)) return rc;
-  return cb::shard_begin(st, n, h_ptrs, h_sizes, h_prefix, world, rank,
-                         seq_base, d_send, h_send_counts);
+  int rc = cb::shard_begin(st, n, h_ptrs, h_sizes, h_prefix, world, rank,
+                           seq_base, cap, d_send);
+  if (rc) return rc;
+  return cb::join_back(st, stream);
 }
 
 extern "C" int cascade_shard_put_begin_host(
     cascade_store_t *s, size_t n, const uint8_t *const *h_blocks,
     const uint64_t *h_sizes, const uint8_t *h_prefix, int world, int rank,
-    uint64_t seq_base, uint8_t *d_send, uint64_t *h_send_counts) {
+    uint64_t seq_base, size_t cap, uint8_t *d_send, void *stream) {
   STORE_ENTRY(s);
-  CB_CHECK(h_send_counts && (n == 0 || (h_blocks && h_sizes && d_send)),
-           CASCADE_ERR_INVALID, "null argument");
+  CB_CHECK(d_send && (n == 0 || (h_blocks && h_sizes)), CASCADE_ERR_INVALID,
+           "null argument");
   CB_CHECK(n <= (size_t)INT32_MAX, CASCADE_ERR_INVALID, "batch too large");
   CB_CHECK(((uintptr_t)d_send & 15u) == 0, CASCADE_ERR_INVALID,
            "d_send must be 16-byte aligned");
-  if (n == 0) {
-    for (int r = 0; r < world; ++r) h_send_counts[r] = 0;
-    st.shard_rank = rank;
-    st.shard_open = 0;
-    return CASCADE_OK;
-  }
-  return cb::shard_begin_host(st, n, h_blocks, h_sizes, h_prefix, world, rank,
-                              seq_base, d_send, h_send_counts);
+  if (int rc = join_caller(st, stream)) return rc;
+  int rc = cb::shard_begin_host(st, n, h_blocks, h_sizes, h_prefix, world,
+                                rank, seq_base, cap, d_send);
+  if (rc) return rc;
+  return cb::join_back(st, stream);
 }
 
 extern "C" int cascade_shard_resolve(cascade_store_t *s, const uint8_t *d_recv,
@@ -2367,19 +2416,22 @@ extern "C" int cascade_shard_resolve(cascade_store_t *s, const uint8_t *d_recv,
            "null argument");
   CB_CHECK(m <= (size_t)INT32_MAX, CASCADE_ERR_INVALID, "batch too large");
   if (int rc = join_caller(st, stream)) return rc;
-  return cb::shard_resolve(st, d_recv, m, d_reply);
+  int rc = cb::shard_resolve(st, d_recv, m, d_reply);
+  if (rc) return rc;
+  return cb::join_back(st, stream);
 }
 
 extern "C" int cascade_shard_put_end(cascade_store_t *s, const uint8_t *d_back,
-                                     size_t n, uint8_t *h_status,
+                                     size_t m, size_t n, uint8_t *h_status,
                                      uint8_t *h_digests, uint64_t *n_stored,
                                      void *stream) {
   STORE_ENTRY(s);
   if (n_stored) *n_stored = 0;
-  if (n == 0) return CASCADE_OK;
-  CB_CHECK(d_back, CASCADE_ERR_INVALID, "null argument");
+  CB_CHECK(n == 0 || d_back, CASCADE_ERR_INVALID, "null argument");
+  CB_CHECK(m >= n && m <= (size_t)INT32_MAX, CASCADE_ERR_INVALID,
+           "m: the padded reply count (world * cap)");
   if (int rc = join_caller(st, stream)) return rc;
-  return cb::shard_end(st, d_back, n, h_status, h_digests, n_stored);
+  return cb::shard_end(st, d_back, m, n, h_status, h_digests, n_stored);
 }
 
 extern "C" int cascade_shard_pool_handle(cascade_store_t *s,
@@ -2411,14 +2463,16 @@ extern "C" int cascade_shard_detach_pools(cascade_store_t *s) {
 }
 
 extern "C" int cascade_shard_get_begin(cascade_store_t *s, size_t n,
-                                       const uint8_t *h_keys, uint8_t *d_send,
-                                       uint64_t *h_send_counts, void *stream) {
+                                       const uint8_t *h_keys, size_t cap,
+                                       uint8_t *d_send, void *stream) {
   STORE_ENTRY(s);
-  CB_CHECK(h_send_counts && (n == 0 || (h_keys && d_send)),
-           CASCADE_ERR_INVALID, "null argument");
+  CB_CHECK(d_send && (n == 0 || h_keys), CASCADE_ERR_INVALID,
+           "null argument");
   CB_CHECK(n <= (size_t)INT32_MAX, CASCADE_ERR_INVALID, "batch too large");
   if (int rc = join_caller(st, stream)) return rc;
-  return cb::shard_get_begin(st, n, h_keys, d_send, h_send_counts);
+  int rc = cb::shard_get_begin(st, n, h_keys, cap, d_send);
+  if (rc) return rc;
+  return cb::join_back(st, stream);
 }
 
 extern "C" int cascade_shard_lookup(cascade_store_t *s, const uint8_t *d_recv,
@@ -2428,11 +2482,14 @@ extern "C" int cascade_shard_lookup(cascade_store_t *s, const uint8_t *d_recv,
            "null argument");
   CB_CHECK(m <= (size_t)INT32_MAX, CASCADE_ERR_INVALID, "batch too large");
   if (int rc = join_caller(st, stream)) return rc;
-  return cb::shard_lookup(st, d_recv, m, d_reply);
+  int rc = cb::shard_lookup(st, d_recv, m, d_reply);
+  if (rc) return rc;
+  return cb::join_back(st, stream);
 }
 
 extern "C" int cascade_shard_get_end(cascade_store_t *s, const uint8_t *d_back,
-                                     size_t n, const uint64_t *h_out_ptrs,
+                                     size_t m, size_t n,
+                                     const uint64_t *h_out_ptrs,
                                      const uint64_t *h_out_caps,
                                      uint64_t *h_sizes, uint8_t *h_found,
                                      uint64_t *n_found, void *stream) {
@@ -2440,11 +2497,9 @@ extern "C" int cascade_shard_get_end(cascade_store_t *s, const uint8_t *d_back,
   if (n_found) *n_found = 0;
   CB_CHECK(n == 0 || (d_back && h_out_ptrs && h_out_caps),
            CASCADE_ERR_INVALID, "null argument");
+  CB_CHECK(m >= n && m <= (size_t)INT32_MAX, CASCADE_ERR_INVALID,
+           "m: the padded location count (world * cap)");
   if (int rc = join_caller(st, stream)) return rc;
-  if (n == 0) {
-    st.shard_get_open = 0;
-    return CASCADE_OK;
-  }
-  return cb::shard_get_end(st, d_back, n, h_out_ptrs, h_out_caps, h_sizes,
+  return cb::shard_get_end(st, d_back, m, n, h_out_ptrs, h_out_caps, h_sizes,
                            h_found, n_found);
 }

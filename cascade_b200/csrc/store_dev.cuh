@@ -40,7 +40,12 @@ enum SlotFlags : uint32_t {
 
 // Sharded dedup exchange (one box, one rank per GPU).  A rank sends one
 // record per block of its batch to the rank that owns the block's key;
-// the owner answers with a reply per record.
+// the owner answers with a reply per record.  The exchange buffers are
+// padded to a fixed number of entries per rank; an entry whose src_idx is
+// kUnused (all bytes 0xff) carries nothing.
+constexpr uint32_t kUnused = 0xffffffffu;
+// Sequence number of a request that takes part in no claim.
+constexpr uint64_t kNoSeq = ~0ull;
 struct ShardRecord {
   uint64_t k0, k1;     // key: digest bytes 0..15, little-endian
   uint64_t seq;        // global sequence number: the smallest stores

@@ -32,6 +32,10 @@ __global__ void claim_kernel(Slot *slots, uint64_t mask,
                              uint32_t *__restrict__ slot_idx, int *err) {
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n) return;
+  if (seqs[i] == kNoSeq) {  // an unused entry: no key, status FAILED
+    slot_idx[i] = kNoSlot;
+    return;
+  }
   const uint64_t s0 = keys[(size_t)i * stride] ^ kKeyMask0;
   const uint64_t s1 = keys[(size_t)i * stride + 1] ^ kKeyMask1;
   const uint64_t h = slot_hash(s0, s1);

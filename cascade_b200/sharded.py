@@ -9,8 +9,11 @@ batch is exact at once:
 
 1. every rank hashes its blocks and stores them speculatively in its own
    HBM pool (``cascade_shard_put_begin``), writing one 64-byte record per
-   block, grouped by owner rank;
-2. the records go to their owners in one all-to-all (NCCL on GPUs);
+   block into its owner rank's segment of a padded send buffer (``world``
+   segments of ``cap`` entries, ``cap`` the largest batch of any rank, which
+   one all-gather of the batch sizes tells every rank);
+2. the records go to their owners in one all-to-all with equal splits
+   (NCCL on GPUs), with no host round trip for counts;
 3. each owner resolves the records it received against its slice of the
    index (``cascade_shard_resolve``): a key already stored is a dedup hit,
    and among new keys the smallest global sequence number stores, which is
@@ -52,19 +55,45 @@ _sz = ctypes.c_size_t
 _u64 = ctypes.c_uint64
 _int = ctypes.c_int
 _lib.register("cascade_shard_put_begin", _int,
-              [_vp, _sz, _vp, _vp, _vp, _int, _int, _u64, _vp, _vp, _vp])
+              [_vp, _sz, _vp, _vp, _vp, _int, _int, _u64, _sz, _vp, _vp])
 _lib.register("cascade_shard_put_begin_host", _int,
-              [_vp, _sz, _vp, _vp, _vp, _int, _int, _u64, _vp, _vp])
+              [_vp, _sz, _vp, _vp, _vp, _int, _int, _u64, _sz, _vp, _vp])
 _lib.register("cascade_shard_resolve", _int, [_vp, _vp, _sz, _vp, _vp])
 _lib.register("cascade_shard_put_end", _int,
-              [_vp, _vp, _sz, _vp, _vp, ctypes.POINTER(_u64), _vp])
+              [_vp, _vp, _sz, _sz, _vp, _vp, ctypes.POINTER(_u64), _vp])
 _lib.register("cascade_shard_pool_handle", _int, [_vp, _vp])
 _lib.register("cascade_shard_attach_pools", _int, [_vp, _int, _int, _vp])
 _lib.register("cascade_shard_detach_pools", _int, [_vp])
-_lib.register("cascade_shard_get_begin", _int, [_vp, _sz, _vp, _vp, _vp, _vp])
+_lib.register("cascade_shard_get_begin", _int, [_vp, _sz, _vp, _sz, _vp, _vp])
 _lib.register("cascade_shard_lookup", _int, [_vp, _vp, _sz, _vp, _vp])
 _lib.register("cascade_shard_get_end", _int,
-              [_vp, _vp, _sz, _vp, _vp, _vp, _vp, ctypes.POINTER(_u64), _vp])
+              [_vp, _vp, _sz, _sz, _vp, _vp, _vp, _vp, ctypes.POINTER(_u64),
+               _vp])
+
+# Byte offset of src_idx in a record (the first 32-bit field after k0, k1,
+# seq, offset, size, flags, holder).
+_RECORD_SRC = 48
+_PUT_FAILED = 3
+
+
+def unused(rows: int, width: int, device):
+    """A padded exchange buffer of `rows` entries that carry nothing."""
+    import torch
+    return torch.full((rows, width), 0xff, dtype=torch.uint8, device=device)
+
+
+def failed_replies(recv):
+    """The replies an owner sends when it could not resolve `recv`: every
+    record it received fails (the holders free those blocks' slots)."""
+    import torch
+    reply = unused(recv.shape[0], REPLY_BYTES, recv.device)
+    src = recv[:, _RECORD_SRC:_RECORD_SRC + 4]
+    used = (src != 0xff).any(dim=1)
+    reply[:, 0:4] = src
+    code = torch.tensor([_PUT_FAILED, 0, 0, 0], dtype=torch.uint8,
+                        device=recv.device)
+    reply[used, 4:8] = code
+    return reply
 
 
 class CudaShardOps:
@@ -80,7 +109,8 @@ class CudaShardOps:
         import torch
         return torch.cuda.current_stream(self.device).cuda_stream
 
-    def begin(self, blocks, is_prefix, world, rank, seq_base):
+    def begin(self, blocks, is_prefix, world, rank, seq_base, cap):
+        """Records for `world` segments of `cap` entries (device tensor)."""
         import torch
         if isinstance(blocks, tuple):    # (device addresses, sizes)
             ptrs = np.ascontiguousarray(blocks[0], dtype=np.uint64)
@@ -103,19 +133,17 @@ class CudaShardOps:
             sizes = np.array([b.numel() for b in blocks], dtype=np.uint64)
         pf = (np.array([1 if p else 0 for p in is_prefix], dtype=np.uint8)
               if is_prefix is not None else None)
-        send = torch.empty((n, RECORD_BYTES), dtype=torch.uint8,
+        send = torch.empty((world * cap, RECORD_BYTES), dtype=torch.uint8,
                            device=self.device)
-        counts = np.zeros(world, dtype=np.uint64)
         check(_lib.load().cascade_shard_put_begin(
             self.store._h, n, ptrs.ctypes.data if n else None,
             sizes.ctypes.data if n else None,
             pf.ctypes.data if pf is not None else None, world, rank, seq_base,
-            send.data_ptr() if n else None, counts.ctypes.data,
-            self._stream()))
+            cap, send.data_ptr(), self._stream()))
         self._n = n
-        return send, [int(c) for c in counts]
+        return send
 
-    def begin_host(self, blocks, is_prefix, world, rank, seq_base):
+    def begin_host(self, blocks, is_prefix, world, rank, seq_base, cap):
         """begin for host blocks: a list of uint8 numpy arrays, or one 2-D
         uint8 array (pinned rows are staged fastest)."""
         import torch
@@ -135,16 +163,15 @@ class CudaShardOps:
             self._keep = arrs
         pf = (np.array([1 if p else 0 for p in is_prefix], dtype=np.uint8)
               if is_prefix is not None else None)
-        send = torch.empty((n, RECORD_BYTES), dtype=torch.uint8,
+        send = torch.empty((world * cap, RECORD_BYTES), dtype=torch.uint8,
                            device=self.device)
-        counts = np.zeros(world, dtype=np.uint64)
         check(_lib.load().cascade_shard_put_begin_host(
             self.store._h, n, ptrs.ctypes.data if n else None,
             sizes.ctypes.data if n else None,
             pf.ctypes.data if pf is not None else None, world, rank, seq_base,
-            send.data_ptr() if n else None, counts.ctypes.data))
+            cap, send.data_ptr(), self._stream()))
         self._n = n
-        return send, [int(c) for c in counts]
+        return send
 
     def resolve(self, recv):
         import torch
@@ -157,16 +184,19 @@ class CudaShardOps:
         return reply
 
     def end(self, back):
-        n = self._n
+        n, m = self._n, back.shape[0]
         status = np.zeros(n, np.uint8)
         digests = np.zeros((n, 32), np.uint8)
         stored = _u64(0)
-        check(_lib.load().cascade_shard_put_end(
-            self.store._h, back.data_ptr() if n else None, n,
-            status.ctypes.data if n else None,
-            digests.ctypes.data if n else None, ctypes.byref(stored),
-            self._stream()))
-        self._keep = None
+        self._n = 0
+        try:
+            check(_lib.load().cascade_shard_put_end(
+                self.store._h, back.data_ptr() if m else None, m, n,
+                status.ctypes.data if n else None,
+                digests.ctypes.data if n else None, ctypes.byref(stored),
+                self._stream()))
+        finally:
+            self._keep = None
         return int(stored.value), status, digests
 
     # ---------------------------------------------------------------- get
@@ -185,18 +215,16 @@ class CudaShardOps:
     def detach(self):
         check(_lib.load().cascade_shard_detach_pools(self.store._h))
 
-    def get_begin(self, keys: bytes, world):
+    def get_begin(self, keys: bytes, world, cap):
         import torch
         n = len(keys) // 16
-        send = torch.empty((n, QUERY_BYTES), dtype=torch.uint8,
+        send = torch.empty((world * cap, QUERY_BYTES), dtype=torch.uint8,
                            device=self.device)
-        counts = np.zeros(world, dtype=np.uint64)
         kbuf = np.frombuffer(keys, np.uint8) if n else None
         check(_lib.load().cascade_shard_get_begin(
-            self.store._h, n, kbuf.ctypes.data if n else None,
-            send.data_ptr() if n else None, counts.ctypes.data,
-            self._stream()))
-        return send, [int(c) for c in counts]
+            self.store._h, n, kbuf.ctypes.data if n else None, cap,
+            send.data_ptr(), self._stream()))
+        return send
 
     def lookup(self, recv):
         import torch
@@ -226,8 +254,9 @@ class CudaShardOps:
         sizes = np.zeros(n, np.uint64)
         found = np.zeros(n, np.uint8)
         nf = _u64(0)
+        m = back.shape[0]
         check(_lib.load().cascade_shard_get_end(
-            self.store._h, back.data_ptr() if n else None, n,
+            self.store._h, back.data_ptr() if m else None, m, n,
             ptrs.ctypes.data if n else None, caps.ctypes.data if n else None,
             sizes.ctypes.data if n else None, found.ctypes.data if n else None,
             ctypes.byref(nf), self._stream()))
@@ -286,33 +315,51 @@ class ShardedCascadeStore:
         return self._put(self.ops.begin_host, blocks, len(blocks), is_prefix,
                          return_status)
 
+    def _sizes(self, n):
+        """Collective: every rank's batch size (one small all-gather)."""
+        import torch
+        import torch.distributed as dist
+        mine = torch.tensor([n], dtype=torch.int64, device=self.ops.device)
+        every = torch.zeros(self.world, dtype=torch.int64,
+                            device=self.ops.device)
+        dist.all_gather_into_tensor(every, mine, group=self.group)
+        return [int(x) for x in every.tolist()]
+
     def _put(self, begin, blocks, n, is_prefix, return_status):
+        """The put exchange.  A rank whose own step fails still takes part
+        in both all-to-alls (sending entries that carry nothing, or failed
+        replies for the records it received) and raises afterwards, so its
+        peers never wait on it; their blocks owned by a failed rank come
+        back FAILED."""
         import torch
         import torch.distributed as dist
         with self._lock:
             dev = self.ops.device
-            mine = torch.tensor([n], dtype=torch.int64, device=dev)
-            every = [torch.zeros_like(mine) for _ in range(self.world)]
-            dist.all_gather(every, mine, group=self.group)
-            counts = [int(t.item()) for t in every]
+            counts = self._sizes(n)
             seq_base = self._next_seq + sum(counts[:self.rank])
             self._next_seq += sum(counts)
-
-            send, send_splits = begin(blocks, is_prefix, self.world,
-                                      self.rank, seq_base)
-            sc = torch.tensor(send_splits, dtype=torch.int64, device=dev)
-            rc = torch.empty(self.world, dtype=torch.int64, device=dev)
-            dist.all_to_all_single(rc, sc, group=self.group)
-            recv_splits = [int(x) for x in rc.tolist()]
-            recv = torch.empty((sum(recv_splits), RECORD_BYTES),
-                               dtype=torch.uint8, device=dev)
-            dist.all_to_all_single(recv, send, recv_splits, send_splits,
-                                   group=self.group)
-            reply = self.ops.resolve(recv)
-            back = torch.empty((n, REPLY_BYTES), dtype=torch.uint8,
-                               device=dev)
-            dist.all_to_all_single(back, reply, send_splits, recv_splits,
-                                   group=self.group)
+            cap = max(counts)
+            if cap == 0:
+                empty = (0, np.zeros(0, np.uint8), np.zeros((0, 32), np.uint8))
+                return empty if return_status else 0
+            error = None
+            try:
+                send = begin(blocks, is_prefix, self.world, self.rank,
+                             seq_base, cap)
+            except Exception as e:       # noqa: BLE001 (re-raised below)
+                error = e
+                send = unused(self.world * cap, RECORD_BYTES, dev)
+            recv = torch.empty_like(send)
+            dist.all_to_all_single(recv, send, group=self.group)
+            try:
+                reply = self.ops.resolve(recv)
+            except Exception as e:       # noqa: BLE001
+                error = error or e
+                reply = failed_replies(recv)
+            back = torch.empty_like(reply)
+            dist.all_to_all_single(back, reply, group=self.group)
+            if error is not None:
+                raise error
             stored, status, digests = self.ops.end(back)
         if return_status:
             return stored, status, digests
@@ -325,7 +372,9 @@ class ShardedCascadeStore:
         (found[n] uint8, sizes[n] uint64) as CascadeStore.get_batch: a block
         larger than its output is reported with its size and not written.
         ``ids``: content ids (32 hex characters) or 16-byte keys, or all the
-        keys at once as a uint8 array of shape (n, 16)."""
+        keys at once as a uint8 array of shape (n, 16).  A rank whose own
+        step fails still takes part in both exchanges and raises afterwards;
+        its peers' reads of keys it owns then raise too."""
         import torch
         import torch.distributed as dist
         if isinstance(ids, np.ndarray) and ids.dtype == np.uint8 \
@@ -338,20 +387,26 @@ class ShardedCascadeStore:
             raise ValueError("one output per id")
         with self._lock:
             dev = self.ops.device
-            send, send_splits = self.ops.get_begin(keys, self.world)
-            sc = torch.tensor(send_splits, dtype=torch.int64, device=dev)
-            rc = torch.empty(self.world, dtype=torch.int64, device=dev)
-            dist.all_to_all_single(rc, sc, group=self.group)
-            recv_splits = [int(x) for x in rc.tolist()]
-            recv = torch.empty((sum(recv_splits), QUERY_BYTES),
-                               dtype=torch.uint8, device=dev)
-            dist.all_to_all_single(recv, send, recv_splits, send_splits,
-                                   group=self.group)
-            reply = self.ops.lookup(recv)
-            back = torch.empty((n_out, LOCATION_BYTES), dtype=torch.uint8,
-                               device=dev)
-            dist.all_to_all_single(back, reply, send_splits, recv_splits,
-                                   group=self.group)
+            cap = max(self._sizes(n_out))
+            if cap == 0:
+                return np.zeros(0, np.uint8), np.zeros(0, np.uint64)
+            error = None
+            try:
+                send = self.ops.get_begin(keys, self.world, cap)
+            except Exception as e:       # noqa: BLE001 (re-raised below)
+                error = e
+                send = unused(self.world * cap, QUERY_BYTES, dev)
+            recv = torch.empty_like(send)
+            dist.all_to_all_single(recv, send, group=self.group)
+            try:
+                reply = self.ops.lookup(recv)
+            except Exception as e:       # noqa: BLE001
+                error = error or e
+                reply = unused(recv.shape[0], LOCATION_BYTES, dev)
+            back = torch.empty_like(reply)
+            dist.all_to_all_single(back, reply, group=self.group)
+            if error is not None:
+                raise error
             # Synchronous: the reads of the peers' pools are complete when
             # this returns, and clear() / close() start with a barrier, so
             # no pool is reset or unmapped while another rank reads it.

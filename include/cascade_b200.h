@@ -261,38 +261,50 @@ int cascade_store_get_batch(cascade_store_t *s, size_t n,
 /* owner rank (the top bits of digest byte 0) and a batch is three      */
 /* calls around two all-to-all exchanges the caller runs (NCCL):         */
 /*   begin:   hash, store every block speculatively in this rank's HBM   */
-/*            pool, and write one 64-byte record per block to d_send,    */
-/*            grouped by owner rank (h_send_counts[r] records for r);    */
+/*            pool, and write one 64-byte record per block into the      */
+/*            owner rank's segment of d_send;                            */
 /*   resolve: as owner, decide each received record (the smallest global */
 /*            sequence number of a new key stores; later ones and keys   */
 /*            already stored are dedup hits) and write 8-byte replies;   */
 /*   end:     take the replies for this rank's blocks (in any order),    */
 /*            free the slots of duplicates and report per-block status.  */
-/* A rank must not run other operations on the store between begin and */
-/* end.  Blocks are content-addressed; HBM must hold the whole batch.    */
+/* The exchange buffers are padded: world segments of cap entries each  */
+/* (segment r goes to / comes from rank r), cap the same on every rank   */
+/* and at least every rank's batch size, so both all-to-alls have equal */
+/* splits and no rank needs the others' counts.  Entries that carry     */
+/* nothing are all 0xff bytes.  begin and resolve do not wait for the   */
+/* device: their outputs are ready on `stream` when they return (the     */
+/* caller's exchange must be ordered after `stream`).  end is           */
+/* synchronous.  A rank must not run other operations on the store      */
+/* between begin and end.  Blocks are content-addressed; HBM must hold  */
+/* the whole batch. */
 #define CASCADE_SHARD_RECORD_BYTES 64
 #define CASCADE_SHARD_REPLY_BYTES 8
 
+/* d_send: world * cap records (16-byte aligned). */
 int cascade_shard_put_begin(cascade_store_t *s, size_t n,
                             const uint64_t *h_ptrs, const uint64_t *h_sizes,
                             const uint8_t *h_prefix, int world, int rank,
-                            uint64_t seq_base, uint8_t *d_send,
-                            uint64_t *h_send_counts, void *stream);
+                            uint64_t seq_base, size_t cap, uint8_t *d_send,
+                            void *stream);
 /* begin for blocks in host memory (the sharded form of
  * cascade_store_put_batch_host): the blocks are copied to this rank's GPU
  * first.  Pinned blocks of one size at a constant pitch are copied in
- * stripes and hashed as each stripe lands.  Synchronous. */
+ * stripes and hashed as each stripe lands. */
 int cascade_shard_put_begin_host(cascade_store_t *s, size_t n,
                                  const uint8_t *const *h_blocks,
                                  const uint64_t *h_sizes,
                                  const uint8_t *h_prefix, int world, int rank,
-                                 uint64_t seq_base, uint8_t *d_send,
-                                 uint64_t *h_send_counts);
+                                 uint64_t seq_base, size_t cap,
+                                 uint8_t *d_send, void *stream);
+/* m = world * cap received records; d_reply: m replies. */
 int cascade_shard_resolve(cascade_store_t *s, const uint8_t *d_recv,
                           size_t m, uint8_t *d_reply, void *stream);
+/* d_back: the m = world * cap replies received; n: this rank's batch. */
 int cascade_shard_put_end(cascade_store_t *s, const uint8_t *d_back,
-                          size_t n, uint8_t *h_status, uint8_t *h_digests,
-                          uint64_t *n_stored, void *stream);
+                          size_t m, size_t n, uint8_t *h_status,
+                          uint8_t *h_digests, uint64_t *n_stored,
+                          void *stream);
 
 /* Sharded get: any rank reads any block of the sharded store.  The
  * reference reads a block another node holds through DistributedStore::get
@@ -300,9 +312,10 @@ int cascade_shard_put_end(cascade_store_t *s, const uint8_t *d_back,
  * table and a read of the holder's DRAM shadow).
  * Here the payload never leaves the holder's HBM pool until it is read:
  * every rank maps the other ranks' pools once (CUDA IPC, peer access over
- * NVLink), and a get is three calls around two all-to-all exchanges:
+ * NVLink), and a get is three calls around two all-to-all exchanges, with
+ * padded buffers as for a put (world segments of cap entries):
  *   get_begin: route each 16-byte key to its owner: one 32-byte query per
- *              key in d_send, grouped by owner rank;
+ *              key in the owner's segment of d_send;
  *   lookup:    as owner, look the received keys up in this rank's slice of
  *              the index (touching their LRU epochs) and write one 48-byte
  *              location per query (found, holder rank, offset, size, INT8
@@ -311,6 +324,7 @@ int cascade_shard_put_end(cascade_store_t *s, const uint8_t *d_back,
  *              copy or dequantise each block from its holder's pool (this
  *              GPU's own or a peer's) into h_out_ptrs[i]; sizes, found
  *              flags and gpu_hits / misses as in cascade_store_get_batch.
+ * get_begin and lookup do not wait for the device; get_end is synchronous.
  * cascade_shard_attach_pools must have run on every rank first.  As for a
  * put, a rank must not run other operations on the store between get_begin
  * and get_end.  Blocks of a sharded store live in HBM (a sharded put needs
@@ -330,13 +344,16 @@ int cascade_shard_pool_handle(cascade_store_t *s, uint8_t *h_handle);
 int cascade_shard_attach_pools(cascade_store_t *s, int world, int rank,
                                const uint8_t *h_handles);
 int cascade_shard_detach_pools(cascade_store_t *s);
+/* d_send: world * cap queries. */
 int cascade_shard_get_begin(cascade_store_t *s, size_t n,
-                            const uint8_t *h_keys, uint8_t *d_send,
-                            uint64_t *h_send_counts, void *stream);
+                            const uint8_t *h_keys, size_t cap,
+                            uint8_t *d_send, void *stream);
+/* m = world * cap received queries; d_reply: m locations. */
 int cascade_shard_lookup(cascade_store_t *s, const uint8_t *d_recv, size_t m,
                          uint8_t *d_reply, void *stream);
+/* d_back: the m = world * cap locations received; n: this rank's keys. */
 int cascade_shard_get_end(cascade_store_t *s, const uint8_t *d_back,
-                          size_t n, const uint64_t *h_out_ptrs,
+                          size_t m, size_t n, const uint64_t *h_out_ptrs,
                           const uint64_t *h_out_caps, uint64_t *h_sizes,
                           uint8_t *h_found, uint64_t *n_found, void *stream);
 

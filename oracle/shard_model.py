@@ -32,8 +32,23 @@ assert QUERY.itemsize == 32 and LOCATION.itemsize == 48
 TIER_HBM, FLAG_REMOTE = 1 << 2, 1 << 4
 
 
+UNUSED = 0xffffffff     # src_idx of a padded entry that carries nothing
+
+
 def owner_of(digest: bytes, world: int) -> int:
     return (digest[0] * world) >> 8
+
+
+def _padded(entries, owners, world, cap):
+    """`world` segments of `cap` entries, entries grouped by owner rank;
+    the rest all 0xff bytes."""
+    out = np.full(world * cap * entries.itemsize, 0xff, np.uint8)
+    view = out.view(entries.dtype)
+    for o in range(world):
+        mine = entries[owners == o]
+        assert len(mine) <= cap
+        view[o * cap:o * cap + len(mine)] = mine
+    return out.reshape(world * cap, entries.itemsize)
 
 
 class CpuShardOps:
@@ -49,7 +64,7 @@ class CpuShardOps:
         self.shared_dir = shared_dir
         self.store = None
 
-    def begin(self, blocks, is_prefix, world, rank, seq_base):
+    def begin(self, blocks, is_prefix, world, rank, seq_base, cap):
         import torch
         n = len(blocks)
         digests = [hashlib.sha256(np.ascontiguousarray(b).tobytes()).digest()
@@ -65,15 +80,12 @@ class CpuShardOps:
             recs[i]["holder"] = rank
             recs[i]["src_idx"] = i
             owners[i] = owner_of(d, world)
-        order = np.argsort(owners, kind="stable")
-        counts = np.bincount(owners, minlength=world).tolist()
-        send = torch.from_numpy(recs[order].view(np.uint8).reshape(n, 64).copy())
         self._digests = digests
         self._blocks = [np.ascontiguousarray(b) for b in blocks]
-        return send, counts
+        return torch.from_numpy(_padded(recs, owners, world, cap))
 
-    def begin_host(self, blocks, is_prefix, world, rank, seq_base):
-        return self.begin(blocks, is_prefix, world, rank, seq_base)
+    def begin_host(self, blocks, is_prefix, world, rank, seq_base, cap):
+        return self.begin(blocks, is_prefix, world, rank, seq_base, cap)
 
     def resolve(self, recv):
         import torch
@@ -82,6 +94,9 @@ class CpuShardOps:
         status = np.full(m, FAILED, np.uint32)
         seen = {}
         for j in np.argsort(recs["seq"], kind="stable"):
+            if recs[j]["src_idx"] == UNUSED:
+                status[j] = UNUSED
+                continue
             key = (int(recs[j]["k0"]), int(recs[j]["k1"]))
             if key in self.index:
                 status[j] = DUP_KNOWN
@@ -99,7 +114,10 @@ class CpuShardOps:
 
     def end(self, back):
         rep = back.numpy().reshape(-1).view(REPLY) if back.numel() else np.zeros(0, REPLY)
+        rep = rep[rep["src_idx"] != UNUSED]
         n = len(self._digests)
+        assert sorted(rep["src_idx"].tolist()) == list(range(n)), \
+            "every block gets one reply"
         status = np.full(n, FAILED, np.uint8)
         status[rep["src_idx"]] = rep["status"]
         digests = np.frombuffer(b"".join(self._digests), np.uint8).reshape(n, 32) \
@@ -131,7 +149,7 @@ class CpuShardOps:
     def detach(self):
         self._world = self._rank = None
 
-    def get_begin(self, keys: bytes, world):
+    def get_begin(self, keys: bytes, world, cap):
         import torch
         n = len(keys) // 16
         q = np.zeros(n, QUERY)
@@ -142,10 +160,8 @@ class CpuShardOps:
             q[i]["k1"] = int.from_bytes(k[8:], "little")
             q[i]["src_idx"] = i
             owners[i] = owner_of(k, world)
-        order = np.argsort(owners, kind="stable")
-        counts = np.bincount(owners, minlength=world).tolist()
         self._get_keys = [keys[16 * i:16 * i + 16] for i in range(n)]
-        return torch.from_numpy(q[order].view(np.uint8).reshape(n, 32).copy()), counts
+        return torch.from_numpy(_padded(q, owners, world, cap))
 
     def lookup(self, recv):
         import torch
@@ -153,6 +169,8 @@ class CpuShardOps:
         loc = np.zeros(len(q), LOCATION)
         for j, r in enumerate(q):
             loc[j]["src_idx"] = r["src_idx"]
+            if r["src_idx"] == UNUSED:
+                continue
             hit = self.index.get((int(r["k0"]), int(r["k1"])))
             if hit is None:
                 continue
@@ -166,6 +184,7 @@ class CpuShardOps:
     def get_end(self, back, outs):
         import os
         loc = back.numpy().reshape(-1).view(LOCATION) if back.numel() else np.zeros(0, LOCATION)
+        loc = loc[loc["src_idx"] != UNUSED]
         n = len(outs)
         found = np.zeros(n, np.uint8)
         sizes = np.zeros(n, np.uint64)

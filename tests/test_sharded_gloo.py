@@ -177,3 +177,125 @@ def test_sharded_uneven_and_empty_batches(tmp_path):
         for i, b in enumerate(blocks):
             assert r["sha"][i] == hashlib.sha256(b.tobytes()).hexdigest()
         assert r["sha"][20] == r["sha"][21] == hashlib.sha256(bytes(300)).hexdigest()
+
+
+# ------------------------------------------------------------ failures
+# Host-side fault injection: a rank's own step raises (a stand-in for an
+# error code from the device), or a rank never joins.  Nothing here touches
+# a GPU.
+
+def _failing_ops(fail_step, fail_batch, out_dir):
+    from oracle.shard_model import CpuShardOps
+
+    class FailingOps(CpuShardOps):
+        batch = 0
+
+        def begin(self, *a):
+            if fail_step == "begin" and self.batch == fail_batch:
+                self.batch += 1
+                raise RuntimeError("injected begin failure")
+            return super().begin(*a)
+
+        def resolve(self, recv):
+            if fail_step == "resolve" and self.batch == fail_batch:
+                self.batch += 1          # end() does not run for this batch
+                raise RuntimeError("injected resolve failure")
+            return super().resolve(recv)
+
+        def end(self, back):
+            self.batch += 1
+            return super().end(back)
+
+    return FailingOps(shared_dir=out_dir)
+
+
+def _failure_main(rank, world, port, out_dir, fail_step):
+    import datetime
+
+    import torch.distributed as dist
+    from cascade_b200.sharded import ShardedCascadeStore
+    from oracle.shard_model import CpuShardOps
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=30))
+    try:
+        ops = (_failing_ops(fail_step, 0, out_dir) if rank == 1
+               else CpuShardOps(shared_dir=out_dir))
+        store = ShardedCascadeStore(ops=ops)
+        res = []
+        for batch in range(2):
+            try:
+                stored, status, _ = store.put_batch(_blocks(rank, batch),
+                                                    return_status=True)
+                res.append({"status": status.tolist()})
+            except RuntimeError as e:
+                res.append({"error": str(e)})
+        store.close()
+        with open(os.path.join(out_dir, f"f{rank}.json"), "w") as f:
+            json.dump(res, f)
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("fail_step", ["begin", "resolve"])
+def test_sharded_put_survives_a_failing_rank(tmp_path, fail_step):
+    """Rank 1 fails in its first batch: it raises after both exchanges, the
+    other ranks finish that batch (their blocks that rank 1 owns come back
+    FAILED when rank 1 could not resolve them), and every rank's next batch
+    works."""
+    world = 3
+    mp.spawn(_failure_main, args=(world, _free_port(), str(tmp_path),
+                                  fail_step), nprocs=world, join=True)
+    from oracle.shard_model import FAILED, owner_of
+    res = [json.load(open(tmp_path / f"f{r}.json")) for r in range(world)]
+    assert res[1][0] == {"error": f"injected {fail_step} failure"}
+    for r in (0, 2):
+        status = res[r][0]["status"]
+        for b, s in zip(_blocks(r, 0), status):
+            owner = owner_of(hashlib.sha256(b.tobytes()).digest(), world)
+            if fail_step == "resolve" and owner == 1:
+                assert s == FAILED
+            else:
+                assert s != FAILED
+    for r in range(world):
+        assert "status" in res[r][1]
+        assert FAILED not in res[r][1]["status"]
+
+
+def _absent_main(rank, world, port, out_dir):
+    import datetime
+    import time
+
+    import torch.distributed as dist
+    from cascade_b200.sharded import ShardedCascadeStore
+    from oracle.shard_model import CpuShardOps
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=3))
+    store = ShardedCascadeStore(ops=CpuShardOps(shared_dir=out_dir))
+    if rank == 1:
+        # leaves between steps: never calls put_batch
+        with open(os.path.join(out_dir, "a1.json"), "w") as f:
+            json.dump({"left": True}, f)
+        time.sleep(8)
+        return
+    t0 = time.monotonic()
+    try:
+        store.put_batch(_blocks(rank, 0))
+        outcome = "returned"
+    except RuntimeError as e:
+        outcome = "raised: " + str(e)[:80]
+    with open(os.path.join(out_dir, "a0.json"), "w") as f:
+        json.dump({"outcome": outcome, "seconds": time.monotonic() - t0}, f)
+
+
+def test_sharded_put_raises_when_a_rank_never_joins(tmp_path):
+    """A rank that leaves makes its peers' next collective end with the
+    process group's timeout error instead of waiting for it."""
+    mp.spawn(_absent_main, args=(2, _free_port(), str(tmp_path)), nprocs=2,
+             join=True)
+    got = json.load(open(tmp_path / "a0.json"))
+    assert got["outcome"].startswith("raised"), got
+    assert got["seconds"] < 30
