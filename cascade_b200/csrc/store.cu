@@ -7,6 +7,7 @@
 // GPUBackend (gpu_backend.cu:166-528), ShmBackend (cascade_core.cpp:237-569).
 #include <algorithm>
 #include <cstring>
+#include <deque>
 #include <memory>
 #include <mutex>
 #include <string>
@@ -107,6 +108,8 @@ struct Scratch {
   int *err, *h_err;
 };
 
+constexpr int kDmaStreams = 4;  // copy streams per direction
+
 struct Store {
   cascade_config_t cfg;
   std::string shm_path, lustre_path;
@@ -146,8 +149,17 @@ struct Store {
   size_t d_q8stage_cap = 0;
   uint8_t *d_evstage = nullptr;  // INT8 forms of blocks being demoted
   size_t d_evstage_cap = 0;
-  uint8_t *scan_d = nullptr;     // live-slot scan for victim choice
+  uint8_t *scan_d = nullptr;     // demotion-candidate histogram and list
   size_t scan_cap = 0;           // bytes
+  // Copy streams between the device and the DRAM tier: [0] device to
+  // host, [1] host to device.
+  cudaStream_t dma[2][kDmaStreams] = {};
+  cudaEvent_t dma_done[2][kDmaStreams] = {};
+  cudaEvent_t dma_start = nullptr;
+  // Per block of the batch being placed: 1 when serial puts would have
+  // stored it in HBM and demoted it again within the batch (it goes to the
+  // DRAM tier directly and counts as a GPU eviction).
+  std::vector<uint8_t> demoted;
   std::mutex mu;
   uint64_t next_seq = 1, next_epoch = 1, next_name = 1;
   std::unordered_map<std::string, Key> names;
@@ -381,74 +393,171 @@ static void tally_put(Store &st, size_t n) {
     } else {
       bool q8 = (st.sc.h_flags[i] & kFlagQ8) != 0;
       st.shm_used += dram_accounted(size, q8);
-      ++st.shm_puts;
+      if (i < st.demoted.size() && st.demoted[i])
+        ++st.gpu_evictions;  // stored in HBM, then demoted, by serial puts
+      else
+        ++st.shm_puts;
     }
   }
+  st.demoted.clear();
 }
 
 
+// ------------------------------------------------------------ DMA fan-out
+// One copy between the device and the pinned DRAM arena.
+struct Dma {
+  void *dst;
+  const void *src;
+  uint64_t bytes;
+};
+
+// Spreads copies between the device and the DRAM tier over the store's copy
+// streams of one direction (0: device to host, 1: host to device), as the
+// reference spreads its transfers over a ring of streams
+// (gpu_backend.cu:191-225): each copy goes to the stream with the fewest
+// bytes queued.  The copies start after the work already on the main stream,
+// and the main stream waits for all of them.
+static int dma_fanout(Store &st, const std::vector<Dma> &jobs, int dir) {
+  if (jobs.empty()) return CASCADE_OK;
+  const cudaMemcpyKind kind =
+      dir == 0 ? cudaMemcpyDeviceToHost : cudaMemcpyHostToDevice;
+  const int k = (int)std::min<size_t>(kDmaStreams, jobs.size());
+  CB_CUDA(cudaEventRecord(st.dma_start, st.s));
+  uint64_t load[kDmaStreams] = {};
+  for (int q = 0; q < k; ++q)
+    CB_CUDA(cudaStreamWaitEvent(st.dma[dir][q], st.dma_start, 0));
+  for (const Dma &j : jobs) {
+    if (!j.bytes) continue;
+    int q = 0;
+    for (int r = 1; r < k; ++r)
+      if (load[r] < load[q]) q = r;
+    CB_CUDA(cudaMemcpyAsync(j.dst, j.src, j.bytes, kind, st.dma[dir][q]));
+    load[q] += j.bytes;
+  }
+  for (int q = 0; q < k; ++q) {
+    CB_CUDA(cudaEventRecord(st.dma_done[dir][q], st.dma[dir][q]));
+    CB_CUDA(cudaStreamWaitEvent(st.s, st.dma_done[dir][q], 0));
+  }
+  return CASCADE_OK;
+}
+
 // ------------------------------------------------------------- demotion
-// Moves least-recently-used HBM blocks to the DRAM tier until `deficit`
-// bytes of HBM are free (GPUBackend::evict_for_space + evict_lru_semantic,
-// gpu_backend.cu:432-487, and CascadeStore::evict_gpu_to_shm,
-// cascade_core.cpp:998-1018).  Victims are chosen by LRU epoch over the
-// whole pool (the reference takes the LRU tail of its largest shard), with
-// prefix blocks last when semantic_eviction is on.  A demoted block keeps
-// its index slot, which now points into the DRAM arena; blocks go to DRAM in
-// the DRAM tier's format (INT8 when kv_compression applies, compressed on
-// the device here; the reference demotes raw bytes).  Stops early when the
-// DRAM tier is full.  Uses the owner-side scratch, so it can run in the
-// middle of a put whose batch occupies the main scratch.
-static int evict_hbm(Store &st, uint64_t deficit) {
-  if (!st.dram_tier || !st.hbm || deficit == 0) return CASCADE_OK;
+// HBM blocks leave for the DRAM tier least recently used first, prefix
+// blocks last when semantic_eviction is on (GPUBackend::evict_for_space +
+// evict_lru_semantic, gpu_backend.cu:432-487, called by
+// CascadeStore::evict_gpu_to_shm, cascade_core.cpp:998-1018).  The
+// reference takes the LRU tail of its largest index shard; here the order
+// is by LRU epoch over the whole pool.  A demoted block keeps its index
+// slot, which then points into the DRAM arena, and goes to DRAM in the DRAM
+// tier's format (INT8 when kv_compression applies, compressed on the
+// device; the reference demotes raw bytes).
+
+// Demotion candidates per class (0: unprotected, 1: prefix), least recent
+// first: the leading part of each class that the device selected.
+struct Candidates {
+  std::vector<ScanRec> c[2];
+  bool complete[2] = {true, true};  // the whole class is listed
+};
+
+inline int victim_class(const Store &st, uint32_t flags) {
+  return (st.cfg.semantic_eviction && st.cfg.dedup_enabled &&
+          (flags & kFlagPrefix)) ? 1 : 0;
+}
+
+// The least recent candidates of each class whose HBM payloads add up to
+// at least `budget` bytes (whole epoch buckets; every candidate when the
+// class holds less): an epoch histogram on the device picks the buckets,
+// and only their slots come back to the host.
+static int select_candidates(Store &st, uint64_t budget, Candidates &out) {
   cudaStream_t s = st.s;
-  // 1. every live HBM slot
-  uint32_t count = 0;
-  for (int pass = 0; pass < 2; ++pass) {
-    size_t want = sizeof(uint32_t) * 64 +
-                  sizeof(ScanRec) * std::max<size_t>(st.claimed + 1024, 4096);
-    if (pass == 1) want = sizeof(uint32_t) * 64 + sizeof(ScanRec) * (count + 1024);
-    int rc = ensure_device_buf(st.scan_d, st.scan_cap, want, s);
-    if (rc) return rc;
-    uint32_t *d_count = reinterpret_cast<uint32_t *>(st.scan_d);
-    ScanRec *d_recs = reinterpret_cast<ScanRec *>(st.scan_d + 256);
-    const uint32_t cap = (uint32_t)((st.scan_cap - 256) / sizeof(ScanRec));
-    rc = launch_index_scan(st.slots, st.nslots, kTierHbm, d_count, d_recs,
-                           cap, s);
-    if (rc) return rc;
-    CB_CUDA(cudaMemcpyAsync(&count, d_count, 4, cudaMemcpyDeviceToHost, s));
-    CB_CUDA(cudaStreamSynchronize(s));
-    if (count <= cap) break;
-  }
-  std::vector<ScanRec> recs(count);
-  if (count)
-    CB_CUDA(cudaMemcpyAsync(recs.data(), st.scan_d + 256,
-                            count * sizeof(ScanRec), cudaMemcpyDeviceToHost, s));
+  constexpr size_t kHistBytes = 2 * kVictimBuckets * 8;
+  constexpr size_t kCountBytes = 2 * kVictimBuckets * 4;
+  constexpr size_t kRecBase = kHistBytes + kCountBytes + 256;
+  int rc = ensure_device_buf(st.scan_d, st.scan_cap, kRecBase + 4096, s);
+  if (rc) return rc;
+  auto *d_bytes = reinterpret_cast<unsigned long long *>(st.scan_d);
+  auto *d_count = reinterpret_cast<uint32_t *>(st.scan_d + kHistBytes);
+  auto *d_n = reinterpret_cast<uint32_t *>(st.scan_d + kHistBytes + kCountBytes);
+  const int semantic = st.cfg.semantic_eviction && st.cfg.dedup_enabled;
+  const uint64_t span = std::max<uint64_t>(st.next_epoch, 1);
+  if ((rc = launch_victim_hist(st.slots, st.nslots, semantic, span, d_bytes,
+                               d_count, s)))
+    return rc;
+  std::vector<uint64_t> hb(2 * kVictimBuckets);
+  std::vector<uint32_t> hc(2 * kVictimBuckets);
+  CB_CUDA(cudaMemcpyAsync(hb.data(), d_bytes, kHistBytes, cudaMemcpyDeviceToHost, s));
+  CB_CUDA(cudaMemcpyAsync(hc.data(), d_count, kCountBytes, cudaMemcpyDeviceToHost, s));
   CB_CUDA(cudaStreamSynchronize(s));
-  const bool semantic = st.cfg.semantic_eviction && st.cfg.dedup_enabled;
-  std::sort(recs.begin(), recs.end(), [&](const ScanRec &a, const ScanRec &b) {
-    const int pa = semantic && (a.flags & kFlagPrefix), pb = semantic && (b.flags & kFlagPrefix);
-    return pa != pb ? pa < pb : a.epoch < b.epoch;
-  });
-  // 2. victims, while the DRAM tier has room
-  struct Victim { ScanRec r; uint64_t dram_off, hbm; bool dq8; };
-  std::vector<Victim> vic;
-  uint64_t freed = 0, acc_total = 0;
-  for (const ScanRec &r : recs) {
-    if (freed >= deficit) break;
-    const bool hq8 = (r.flags & kFlagQ8) != 0;
-    const bool dq8 = hq8 || q8_eligible(st, r.size, true);
-    const uint64_t acc = dram_accounted(r.size, dq8);
-    if (st.shm_used + acc_total + acc > st.dram->capacity()) break;
-    const uint64_t off = st.dram->alloc(payload_bytes(r.size, dq8));
-    if (off == DramArena::kNone) break;
-    vic.push_back({r, off, payload_bytes(r.size, hq8), dq8});
-    freed += payload_bytes(r.size, hq8);
-    acc_total += acc;
+  int cut[2] = {-1, -1};
+  size_t total = 0;
+  for (int c = 0; c < 2; ++c) {
+    uint64_t cum = 0;
+    int last = -1;
+    for (int b = 0; b < kVictimBuckets; ++b)
+      if (hc[c * kVictimBuckets + b]) last = b;
+    for (int b = 0; b <= last; ++b) {
+      cum += hb[c * kVictimBuckets + b];
+      total += hc[c * kVictimBuckets + b];
+      cut[c] = b;
+      if (cum >= budget) break;
+    }
+    out.complete[c] = cut[c] == last;
+    out.c[c].clear();
   }
+  if (total == 0) return CASCADE_OK;
+  if ((rc = ensure_device_buf(st.scan_d, st.scan_cap,
+                              kRecBase + total * sizeof(ScanRec), s)))
+    return rc;
+  d_n = reinterpret_cast<uint32_t *>(st.scan_d + kHistBytes + kCountBytes);
+  ScanRec *d_recs = reinterpret_cast<ScanRec *>(st.scan_d + kRecBase);
+  if ((rc = launch_victim_collect(st.slots, st.nslots, semantic, span, cut[0],
+                                  cut[1], d_n, d_recs, (uint32_t)total, s)))
+    return rc;
+  std::vector<ScanRec> recs(total);
+  uint32_t got = 0;
+  CB_CUDA(cudaMemcpyAsync(&got, d_n, 4, cudaMemcpyDeviceToHost, s));
+  CB_CUDA(cudaMemcpyAsync(recs.data(), d_recs, total * sizeof(ScanRec),
+                          cudaMemcpyDeviceToHost, s));
+  CB_CUDA(cudaStreamSynchronize(s));
+  CB_CHECK(got == total, CASCADE_ERR_CUDA,
+           "demotion candidates changed between histogram and collection");
+  for (const ScanRec &r : recs) out.c[victim_class(st, r.flags)].push_back(r);
+  for (int c = 0; c < 2; ++c)
+    std::sort(out.c[c].begin(), out.c[c].end(),
+              [](const ScanRec &a, const ScanRec &b) {
+                return a.epoch != b.epoch ? a.epoch < b.epoch : a.slot < b.slot;
+              });
+  return CASCADE_OK;
+}
+
+// A block that leaves HBM, with its DRAM space already allocated.
+struct Demotion {
+  ScanRec r;
+  uint64_t dram_off;
+  bool dq8;  // DRAM format: INT8
+};
+
+// Returns arena space on every path that does not hand it to the index.
+struct ArenaGuard {
+  DramArena *arena;
+  std::vector<std::pair<uint64_t, uint64_t>> held;  // offset, bytes
+  ~ArenaGuard() {
+    for (auto &h : held) arena->free(h.first, h.second);
+  }
+  void keep() { held.clear(); }
+};
+
+// Moves `vic` from HBM to their DRAM places: INT8 forms of raw victims on
+// the device, payloads to the arena over the copy streams, slots relocated,
+// pool space returned.  Counts them as gpu_evictions.
+static int demote(Store &st, std::vector<Demotion> &vic) {
   if (vic.empty()) return CASCADE_OK;
+  ArenaGuard guard{st.dram.get(), {}};
+  for (const Demotion &v : vic)
+    guard.held.emplace_back(v.dram_off, payload_bytes(v.r.size, v.dq8));
+  cudaStream_t s = st.s;
   // raw blocks that become INT8 first: their quantise outputs index 0..nq-1
-  std::stable_partition(vic.begin(), vic.end(), [](const Victim &v) {
+  std::stable_partition(vic.begin(), vic.end(), [](const Demotion &v) {
     return v.dq8 && !(v.r.flags & kFlagQ8);
   });
   size_t nq = 0;
@@ -458,7 +567,6 @@ static int evict_hbm(Store &st, uint64_t deficit) {
   int rc = ensure_scratch_of(st, oc, k);
   if (rc) return rc;
   const uint64_t pool = (uint64_t)(uintptr_t)st.pool;
-  // 3. INT8 forms of raw victims, on the device
   std::vector<uint64_t> so(nq);
   uint64_t stage_bytes = 0, max_size = 0;
   for (size_t j = 0; j < nq; ++j) {
@@ -482,28 +590,31 @@ static int evict_hbm(Store &st, uint64_t deficit) {
                                   oc.dst, oc.hdr, 0, s);
     if (rc) return rc;
   }
-  // 4. payloads into the pinned arena
+  std::vector<Dma> jobs;
+  jobs.reserve(k);
   for (size_t j = 0; j < k; ++j) {
-    const Victim &v = vic[j];
-    const uint64_t bytes = payload_bytes(v.r.size, v.dq8);
-    if (!bytes) continue;
+    const Demotion &v = vic[j];
     const void *src = j < nq ? (const void *)(st.d_evstage + so[j])
                              : (const void *)(uintptr_t)(pool + v.r.offset);
-    CB_CUDA(cudaMemcpyAsync(st.dram->ptr(v.dram_off), src, bytes,
-                            cudaMemcpyDeviceToHost, s));
+    jobs.push_back({st.dram->ptr(v.dram_off), src,
+                    payload_bytes(v.r.size, v.dq8)});
   }
-  // 5. slots point into DRAM; the pool takes the space back
+  if ((rc = dma_fanout(st, jobs, 0))) return rc;
+  uint64_t freed = 0, acc_total = 0;
   for (size_t j = 0; j < k; ++j) {
-    const Victim &v = vic[j];
+    const Demotion &v = vic[j];
+    const bool hq8 = (v.r.flags & kFlagQ8) != 0;
     oc.h_slot[j] = v.r.slot;
     oc.h_off[j] = v.dram_off;
     oc.h_flags[j] = (v.r.flags & kFlagPrefix) | kTierDram | (v.dq8 ? kFlagQ8 : 0);
-    oc.h_req[j] = v.hbm;
+    oc.h_req[j] = payload_bytes(v.r.size, hq8);
     oc.h_seqs[j] = v.r.offset;
     uint8_t *h = oc.h_hdr + 8 * j;
     std::memcpy(h, &v.r.hdr_scale, 4);
     h[4] = (uint8_t)v.r.hdr_zp;
     h[5] = h[6] = h[7] = 0;
+    freed += payload_bytes(v.r.size, hq8);
+    acc_total += dram_accounted(v.r.size, v.dq8);
   }
   CB_CUDA(cudaMemcpyAsync(oc.slot, oc.h_slot, k * 4, cudaMemcpyHostToDevice, s));
   CB_CUDA(cudaMemcpyAsync(oc.off, oc.h_off, k * 8, cudaMemcpyHostToDevice, s));
@@ -520,10 +631,172 @@ static int evict_hbm(Store &st, uint64_t deficit) {
                                           oc.status, (int)k, s);
   if (rc) return rc;
   CB_CUDA(cudaStreamSynchronize(s));
+  guard.keep();
   st.gpu_used -= freed;
   st.shm_used += acc_total;
   st.gpu_evictions += k;
   return CASCADE_OK;
+}
+
+// A block entering HBM within a batch, in the order of the serial calls.
+struct Arrival {
+  uint64_t size;  // logical size
+  uint64_t pay;   // HBM payload bytes
+  int cls;        // demotion class
+  bool put;       // a put (else the promotion of a DRAM block)
+  uint64_t acc;   // promotion: the DRAM bytes accounted to the block now
+};
+
+// Where an arrival ends after the batch.
+enum Fate : uint8_t {
+  kFateHbm = 0,      // in HBM
+  kFateEvicted = 1,  // entered HBM, then left for DRAM within the batch
+  kFateDram = 2,     // a put that went to the DRAM tier directly
+  kFateNone = 3,     // no HBM and (put) no DRAM room: the put fails;
+                     // a promotion leaves the block where it is
+};
+
+struct Replay {
+  std::vector<uint8_t> fate;
+  std::vector<uint64_t> off;  // DRAM offset (kFateEvicted puts, kFateDram)
+  std::vector<uint8_t> dq8;   // DRAM format of those
+  std::vector<Demotion> old;  // older blocks demoted, in order
+  bool need_more = false;     // a class ran past its selected candidates
+};
+
+// Replays the serial puts / promotions of a batch (CascadeStore::put,
+// cascade_core.cpp:1097-1118, and promote_to_gpu, 1039-1056): an arrival
+// that does not fit demotes blocks until it has freed its own size -- older
+// blocks of class 0, then the batch's own class-0 arrivals already in HBM
+// in arrival order, then the same for class 1 -- and takes HBM if it then
+// fits; a put that gets no HBM goes to the DRAM tier while it has room.
+// Every demotion needs DRAM room (accounted bytes and arena space); a
+// demotion that finds none ends that arrival's demotions (the block stays
+// in HBM; nothing is dropped).  DRAM space is allocated here, in the serial
+// order; with need_more set, all of it is given back.
+static void replay(Store &st, const std::vector<Arrival> &arr,
+                   const Candidates &cand, bool allow_hbm, Replay &out) {
+  const size_t n = arr.size();
+  out.fate.assign(n, kFateNone);
+  out.off.assign(n, kInvalidOffset);
+  out.dq8.assign(n, 0);
+  out.old.clear();
+  out.need_more = false;
+  uint64_t used = st.gpu_used, shm = st.shm_used;
+  const uint64_t cap = st.pool_cap;
+  const uint64_t dcap = st.dram_tier ? st.dram->capacity() : 0;
+  std::vector<std::pair<uint64_t, uint64_t>> allocs;
+  auto alloc = [&](uint64_t size, bool q8) {
+    const uint64_t off = st.dram->alloc(payload_bytes(size, q8));
+    if (off != DramArena::kNone) allocs.emplace_back(off, payload_bytes(size, q8));
+    return off;
+  };
+  size_t oi[2] = {0, 0};
+  std::deque<size_t> fresh[2];
+  const bool hbm = allow_hbm && st.hbm;
+  for (size_t j = 0; j < n; ++j) {
+    const Arrival &a = arr[j];
+    if (hbm && st.dram_tier && used + a.pay > cap) {
+      uint64_t freed = 0;
+      while (freed < a.pay) {
+        int cls = -1;
+        bool old = false;
+        for (int c = 0; c < 2 && cls < 0; ++c) {
+          if (oi[c] < cand.c[c].size()) {
+            cls = c;
+            old = true;
+          } else if (!cand.complete[c]) {
+            out.need_more = true;
+            for (auto &h : allocs) st.dram->free(h.first, h.second);
+            return;
+          } else if (!fresh[c].empty()) {
+            cls = c;
+          }
+        }
+        if (cls < 0) break;
+        if (old) {
+          const ScanRec &r = cand.c[cls][oi[cls]];
+          const bool hq8 = (r.flags & kFlagQ8) != 0;
+          const bool dq8 = hq8 || q8_eligible(st, r.size, true);
+          const uint64_t acc = dram_accounted(r.size, dq8);
+          if (shm + acc > dcap) break;
+          const uint64_t off = alloc(r.size, dq8);
+          if (off == DramArena::kNone) break;
+          out.old.push_back({r, off, dq8});
+          ++oi[cls];
+          used -= payload_bytes(r.size, hq8);
+          freed += payload_bytes(r.size, hq8);
+          shm += acc;
+        } else {
+          const size_t k = fresh[cls].front();
+          const Arrival &b = arr[k];
+          uint64_t acc = b.acc;
+          if (b.put) {
+            const bool dq8 = q8_eligible(st, b.size, true);
+            acc = dram_accounted(b.size, dq8);
+            if (shm + acc > dcap) break;
+            const uint64_t off = alloc(b.size, dq8);
+            if (off == DramArena::kNone) break;
+            out.off[k] = off;
+            out.dq8[k] = dq8;
+          } else if (shm + acc > dcap) {
+            break;
+          }
+          fresh[cls].pop_front();
+          out.fate[k] = kFateEvicted;
+          used -= b.pay;
+          freed += b.pay;
+          shm += acc;
+        }
+      }
+    }
+    if (hbm && used + a.pay <= cap) {
+      out.fate[j] = kFateHbm;
+      used += a.pay;
+      fresh[a.cls].push_back(j);
+      if (!a.put) shm -= a.acc;
+      continue;
+    }
+    if (a.put && st.dram_tier) {
+      const bool dq8 = q8_eligible(st, a.size, true);
+      const uint64_t acc = dram_accounted(a.size, dq8);
+      if (shm + acc <= dcap) {
+        const uint64_t off = alloc(a.size, dq8);
+        if (off != DramArena::kNone) {
+          out.fate[j] = kFateDram;
+          out.off[j] = off;
+          out.dq8[j] = dq8;
+          shm += acc;
+        }
+      }
+    }
+  }
+}
+
+// Candidates enough for the batch, then the replay (more candidates if the
+// replay ran past them).  `deficit`: the HBM bytes the batch needs beyond
+// the free room if every arrival took HBM.
+static int plan_batch(Store &st, const std::vector<Arrival> &arr,
+                      bool allow_hbm, Replay &out) {
+  Candidates cand;
+  uint64_t need = 0;
+  for (const Arrival &a : arr) need += a.pay;
+  const bool may_demote = allow_hbm && st.hbm && st.dram_tier &&
+                          st.gpu_used + need > st.pool_cap;
+  uint64_t budget = 0;
+  if (may_demote) {
+    const uint64_t deficit = st.gpu_used + need - st.pool_cap;
+    budget = deficit + deficit / 2 + (16ull << 20);
+  }
+  for (;;) {
+    if (may_demote) {
+      int rc = select_candidates(st, budget, cand);
+      if (rc) return rc;
+    }
+    replay(st, arr, cand, allow_hbm, out);
+    if (!out.need_more) return CASCADE_OK;
+    budget = ~0ull;  // every candidate
+  }
 }
 
 // ----------------------------------------------------------------- put
@@ -557,65 +830,34 @@ static int put_placed(Store &st, size_t n, bool use_digests,
   CB_CUDA(cudaStreamSynchronize(s));
   if ((rc = check_device_err(st))) return rc;
 
-  // Placement (CascadeStore::put, cascade_core.cpp:1097-1124): HBM first;
-  // when the new blocks do not fit, older ones are demoted to DRAM to make
-  // room (1097-1105).  Blocks that still get no HBM go to the DRAM tier
-  // while its capacity holds (1108-1118), else they fail (the Lustre tier
-  // of 1121-1124 is not part of this library).
-  if (allow_hbm && st.hbm && st.dram_tier) {
-    uint64_t need = 0;
-    for (size_t i = 0; i < n; ++i)
-      if (st.sc.h_status[i] == CASCADE_PUT_STORED)
-        need += payload_bytes(st.sc.h_sizes[i],
-                              q8_eligible(st, st.sc.h_sizes[i], false));
-    if (st.gpu_used + need > st.pool_cap) {
-      const uint64_t fit = std::min<uint64_t>(need, st.pool_cap);
-      const uint64_t deficit = st.gpu_used + fit > st.pool_cap
-                                   ? st.gpu_used + fit - st.pool_cap : 0;
-      if ((rc = evict_hbm(st, deficit))) return rc;
-    }
+  // Placement: the batch's serial puts replayed (plan_batch): HBM first,
+  // older blocks demoted to make room (cascade_core.cpp:1097-1105), the
+  // DRAM tier for the rest while its capacity holds (1108-1118), FAILED
+  // when neither has room (the Lustre tier of 1121-1124 is not part of this
+  // library).  Only the end state is written: a block that serial puts
+  // would store in HBM and demote within the batch goes to DRAM directly.
+  std::vector<Arrival> arr;
+  for (size_t i = 0; i < n; ++i) {
+    if (st.sc.h_status[i] != CASCADE_PUT_STORED) continue;
+    const uint64_t size = st.sc.h_sizes[i];
+    const bool pre = h_prefix && h_prefix[i] && st.cfg.dedup_enabled;
+    arr.push_back({size, payload_bytes(size, st.hbm && q8_eligible(st, size, false)),
+                   victim_class(st, pre ? kFlagPrefix : 0u), true, 0});
   }
-  // Which new blocks get HBM.  Without a DRAM tier, the reference's serial
-  // puts store blocks while they fit and fail the rest (nothing can be
-  // demoted): first come, first placed.  With one, each serial put lands in
-  // HBM and demotes the least recently used blocks, prefix blocks last
-  // (evict_gpu_to_shm, cascade_core.cpp:998-1036): after the batch, HBM
-  // holds its prefix blocks and then its latest blocks.  That end state is
-  // placed directly, without writing blocks to HBM only to demote them
-  // within the same batch.  (With blocks of one size it is the serial end
-  // state exactly; with mixed sizes an older block small enough to fit the
-  // remaining room is kept too, where serial puts would have demoted it.)
-  std::vector<char> hbm_pick(n, 0);
-  if (allow_hbm && st.hbm) {
-    std::vector<size_t> order;
-    for (size_t i = 0; i < n; ++i)
-      if (st.sc.h_status[i] == CASCADE_PUT_STORED) order.push_back(i);
-    if (st.dram_tier) {
-      const bool semantic = st.cfg.semantic_eviction && st.cfg.dedup_enabled;
-      auto rank_of = [&](size_t i) {
-        return (semantic && h_prefix && h_prefix[i]) ? 0 : 1;
-      };
-      std::stable_sort(order.begin(), order.end(), [&](size_t a, size_t b) {
-        if (rank_of(a) != rank_of(b)) return rank_of(a) < rank_of(b);
-        return a > b;
-      });
-    }
-    uint64_t proj = st.gpu_used;
-    for (size_t i : order) {
-      const uint64_t size = st.sc.h_sizes[i];
-      const uint64_t pay = payload_bytes(size, q8_eligible(st, size, false));
-      if (proj + pay <= st.pool_cap) {
-        hbm_pick[i] = 1;
-        proj += pay;
-      }
-    }
-  }
-  uint64_t hbm_proj = st.gpu_used, dram_proj = st.shm_used;
+  Replay plan;
+  if ((rc = plan_batch(st, arr, allow_hbm, plan))) return rc;
+  ArenaGuard arena{st.dram.get(), {}};  // the batch's DRAM space, until placed
+  for (size_t j = 0; j < arr.size(); ++j)
+    if (plan.fate[j] == kFateEvicted || plan.fate[j] == kFateDram)
+      arena.held.emplace_back(plan.off[j],
+                              payload_bytes(arr[j].size, plan.dq8[j]));
+  if ((rc = demote(st, plan.old))) return rc;
   uint64_t q8stage_bytes = 0;
   std::vector<size_t> dram_raw, dram_q8;
   std::vector<uint64_t> q8stage_off;
   bool any_hbm = false, any_hbm_raw = false, any_q8 = false;
-  for (size_t i = 0; i < n; ++i) {
+  st.demoted.assign(n, 0);
+  for (size_t i = 0, j = 0; i < n; ++i) {
     st.sc.h_req[i] = kNoRequest;
     st.sc.h_off[i] = kInvalidOffset;
     st.sc.h_dst[i] = 0;
@@ -624,40 +866,30 @@ static int put_placed(Store &st, size_t n, bool use_digests,
         (h_prefix && h_prefix[i] && st.cfg.dedup_enabled) ? kFlagPrefix : 0;
     st.sc.h_flags[i] = prefix;
     if (st.sc.h_status[i] != CASCADE_PUT_STORED) continue;
-    const bool hq8 = st.hbm && q8_eligible(st, size, false);
-    if (hbm_pick[i]) {
-      const bool q8 = hq8;
+    const size_t k = j++;
+    const uint8_t fate = plan.fate[k];
+    if (fate == kFateHbm) {
+      const bool q8 = st.hbm && q8_eligible(st, size, false);
       st.sc.h_req[i] = payload_bytes(size, q8);
       st.sc.h_flags[i] |= kTierHbm | (q8 ? kFlagQ8 : 0);
-      hbm_proj += payload_bytes(size, q8);
       any_hbm = true;
       any_q8 |= q8;
       any_hbm_raw |= !q8;
-      continue;
-    }
-    if (st.dram_tier) {
-      bool q8 = q8_eligible(st, size, true);
-      uint64_t acc = dram_accounted(size, q8);
-      if (dram_proj + acc <= st.dram->capacity()) {
-        uint64_t pay = payload_bytes(size, q8);
-        uint64_t off = st.dram->alloc(pay);
-        if (off != DramArena::kNone) {
-          st.sc.h_off[i] = off;
-          st.sc.h_flags[i] |= kTierDram | (q8 ? kFlagQ8 : 0);
-          dram_proj += acc;
-          if (q8) {
-            any_q8 = true;
-            dram_q8.push_back(i);
-            q8stage_off.push_back(q8stage_bytes);
-            q8stage_bytes += (pay + 255) & ~uint64_t(255);
-          } else {
-            dram_raw.push_back(i);
-          }
-          continue;
-        }
+    } else if (fate == kFateEvicted || fate == kFateDram) {
+      const bool q8 = plan.dq8[k] != 0;
+      st.sc.h_off[i] = plan.off[k];
+      st.sc.h_flags[i] |= kTierDram | (q8 ? kFlagQ8 : 0);
+      st.demoted[i] = fate == kFateEvicted;
+      if (q8) {
+        any_q8 = true;
+        dram_q8.push_back(i);
+        q8stage_off.push_back(q8stage_bytes);
+        q8stage_bytes += (payload_bytes(size, true) + 255) & ~uint64_t(255);
+      } else {
+        dram_raw.push_back(i);
       }
     }
-    // No room anywhere: left with req = none and no offset -> FAILED.
+    // kFateNone: req = none and no offset -> FAILED.
   }
   if (!dram_q8.empty()) {
     if ((rc = ensure_device_buf(st.d_q8stage, st.d_q8stage_cap, q8stage_bytes,
@@ -700,21 +932,17 @@ static int put_placed(Store &st, size_t n, bool use_digests,
     rc = launch_copy(st.sc.ptrs, st.sc.dst, st.sc.eff_raw, (int)n, max_size, s);
   if (rc) return rc;
   // DRAM placements leave the device by DMA into the pinned arena.
+  std::vector<Dma> jobs;
   for (size_t k = 0; k < dram_q8.size(); ++k) {
-    size_t i = dram_q8[k];
-    uint64_t pay = payload_bytes(st.sc.h_sizes[i], true);
-    if (pay)
-      CB_CUDA(cudaMemcpyAsync(st.dram->ptr(st.sc.h_off[i]),
-                              st.d_q8stage + q8stage_off[k], pay,
-                              cudaMemcpyDeviceToHost, s));
+    const size_t i = dram_q8[k];
+    jobs.push_back({st.dram->ptr(st.sc.h_off[i]), st.d_q8stage + q8stage_off[k],
+                    payload_bytes(st.sc.h_sizes[i], true)});
   }
-  for (size_t i : dram_raw) {
-    uint64_t size = st.sc.h_sizes[i];
-    if (size)
-      CB_CUDA(cudaMemcpyAsync(st.dram->ptr(st.sc.h_off[i]),
-                              reinterpret_cast<const void *>(st.sc.h_ptrs[i]),
-                              size, cudaMemcpyDeviceToHost, s));
-  }
+  for (size_t i : dram_raw)
+    jobs.push_back({st.dram->ptr(st.sc.h_off[i]),
+                    reinterpret_cast<const void *>(st.sc.h_ptrs[i]),
+                    st.sc.h_sizes[i]});
+  if ((rc = dma_fanout(st, jobs, 0))) return rc;
   const uint64_t epoch = st.next_epoch;
   st.next_epoch += n;
   rc = launch_index_commit(st.slots, st.sc.slot, st.sc.status, st.sc.off,
@@ -727,6 +955,7 @@ static int put_placed(Store &st, size_t n, bool use_digests,
   CB_CUDA(cudaMemcpyAsync(st.sc.h_off, st.sc.off, n * 8,
                           cudaMemcpyDeviceToHost, s));
   CB_CUDA(cudaStreamSynchronize(s));
+  arena.keep();  // the index (or tally_put, for blocks that failed) owns it
   return CASCADE_OK;
 }
 
@@ -912,6 +1141,7 @@ static int put_uploaded(Store &st, size_t n, bool content_addressed,
                         const uint8_t *h_prefix, uint64_t max_size,
                         bool digests_ready, int mode = -1) {
   int rc;
+  st.demoted.clear();
   if (mode < 0) mode = (content_addressed && can_speculate(st, n)) ? 0 : 1;
   if (mode == 0) {
     if ((rc = put_speculative(st, n, h_prefix, max_size, digests_ready)))
@@ -1057,6 +1287,7 @@ static int deliver_locked(Store &st, size_t n, const uint64_t *out,
     if (rc) return rc;
   }
   uint64_t stage_off = 0;
+  std::vector<Dma> jobs;  // DRAM payloads up to the device
   for (size_t i = 0; i < n; ++i) {
     const LookupInfo &f = st.sc.h_info[i];
     if (!f.found || !deliver[i]) continue;
@@ -1067,16 +1298,12 @@ static int deliver_locked(Store &st, size_t n, const uint64_t *out,
     } else {  // DRAM: bring the payload up first
       uint64_t pay = payload_bytes(f.size, q8);
       if (!q8) {
-        if (f.size)
-          CB_CUDA(cudaMemcpyAsync(reinterpret_cast<void *>(out[i]),
-                                  st.dram->ptr(f.offset), f.size,
-                                  cudaMemcpyHostToDevice, s));
+        jobs.push_back({reinterpret_cast<void *>(out[i]),
+                        st.dram->ptr(f.offset), f.size});
         continue;
       }
       src = (uint64_t)(uintptr_t)(st.d_q8stage + stage_off);
-      if (pay)
-        CB_CUDA(cudaMemcpyAsync(st.d_q8stage + stage_off, st.dram->ptr(f.offset),
-                                pay, cudaMemcpyHostToDevice, s));
+      jobs.push_back({st.d_q8stage + stage_off, st.dram->ptr(f.offset), pay});
       stage_off += (pay + 255) & ~uint64_t(255);
     }
     if (q8) {
@@ -1097,6 +1324,7 @@ static int deliver_locked(Store &st, size_t n, const uint64_t *out,
       ++nc;
     }
   }
+  if (int rc = dma_fanout(st, jobs, 1)) return rc;
   if (nc) {
     CB_CUDA(cudaMemcpyAsync(st.sc.ptrs, st.sc.h_ptrs, nc * 8, cudaMemcpyHostToDevice, s));
     CB_CUDA(cudaMemcpyAsync(st.sc.dst, st.sc.h_dst, nc * 8, cudaMemcpyHostToDevice, s));
@@ -1126,30 +1354,32 @@ static int deliver_locked(Store &st, size_t n, const uint64_t *out,
   // the decoded block, now in out[i], is stored in HBM and its DRAM space
   // released.
   if (!(st.cfg.promotion_enabled && st.hbm)) return CASCADE_OK;
-  std::vector<size_t> promo;
-  {  // room for the promotions: demote older HBM blocks first
-    uint64_t need = 0;
-    for (size_t i = 0; i < n; ++i) {
-      const LookupInfo &f = st.sc.h_info[i];
-      if (!f.found || !deliver[i] || !(f.flags & kTierDram)) continue;
-      const uint64_t size = (f.flags & kFlagQ8) ? 2 * (f.size / 2) : f.size;
-      need += payload_bytes(size, q8_eligible(st, size, false));
-    }
-    need = std::min<uint64_t>(need, st.pool_cap);
-    if (need && st.gpu_used + need > st.pool_cap) {
-      int rc = evict_hbm(st, st.gpu_used + need - st.pool_cap);
-      if (rc) return rc;
-    }
-  }
-  uint64_t proj = st.gpu_used;
+  // The promotions replayed in get order (promote_to_gpu demotes older
+  // blocks when HBM is full): a block that serial gets would promote and
+  // demote again within the batch stays in DRAM and counts both ways.
+  std::vector<size_t> promo, want;
+  std::vector<Arrival> arr;
   for (size_t i = 0; i < n; ++i) {
     const LookupInfo &f = st.sc.h_info[i];
     if (!f.found || !deliver[i] || !(f.flags & kTierDram)) continue;
-    const uint64_t size = (f.flags & kFlagQ8) ? 2 * (f.size / 2) : f.size;
-    const uint64_t need = payload_bytes(size, q8_eligible(st, size, false));
-    if (proj + need > st.pool_cap) continue;  // no eviction on promotion yet
-    proj += need;
-    promo.push_back(i);
+    const bool was_q8 = (f.flags & kFlagQ8) != 0;
+    const uint64_t size = was_q8 ? 2 * (f.size / 2) : f.size;
+    want.push_back(i);
+    arr.push_back({size, payload_bytes(size, q8_eligible(st, size, false)),
+                   victim_class(st, f.flags), false,
+                   dram_accounted(f.size, was_q8)});
+  }
+  if (arr.empty()) return CASCADE_OK;
+  Replay plan;
+  int prc = plan_batch(st, arr, true, plan);
+  if (!prc) prc = demote(st, plan.old);
+  if (prc) return prc;
+  for (size_t k = 0; k < arr.size(); ++k) {
+    if (plan.fate[k] == kFateHbm) promo.push_back(want[k]);
+    if (plan.fate[k] == kFateEvicted) {
+      ++st.promotions_to_gpu;
+      ++st.gpu_evictions;
+    }
   }
   if (promo.empty()) return CASCADE_OK;
   // Build a placement batch over the scratch arrays: one request each.
@@ -1344,6 +1574,13 @@ static int create_store(const cascade_config_t *cfg, Store **out) {
   CB_CUDA(cudaEventCreateWithFlags(&st->ev, cudaEventDisableTiming));
   CB_CUDA(cudaEventCreateWithFlags(&st->ev2, cudaEventDisableTiming));
   CB_CUDA(cudaEventCreateWithFlags(&st->ev3, cudaEventDisableTiming));
+  CB_CUDA(cudaEventCreateWithFlags(&st->dma_start, cudaEventDisableTiming));
+  for (int d = 0; d < 2; ++d)
+    for (int q = 0; q < kDmaStreams; ++q) {
+      CB_CUDA(cudaStreamCreateWithFlags(&st->dma[d][q], cudaStreamNonBlocking));
+      CB_CUDA(cudaEventCreateWithFlags(&st->dma_done[d][q],
+                                       cudaEventDisableTiming));
+    }
   st->hbm = cfg->use_gpu && cfg->gpu_capacity_bytes > 0;
   st->dram_tier = cfg->shm_capacity_bytes > 0;
   if (st->hbm) {
@@ -1408,10 +1645,15 @@ static void destroy_store(Store *st) {
   if (st->d_evstage) cudaFree(st->d_evstage);
   if (st->scan_d) cudaFree(st->scan_d);
   if (st->sha_state) cudaFree(st->sha_state);
-  for (cudaEvent_t e : {st->ev, st->ev2, st->ev3})
+  for (cudaEvent_t e : {st->ev, st->ev2, st->ev3, st->dma_start})
     if (e) cudaEventDestroy(e);
   for (cudaStream_t q : {st->s, st->s2, st->s3})
     if (q) cudaStreamDestroy(q);
+  for (int d = 0; d < 2; ++d)
+    for (int q = 0; q < kDmaStreams; ++q) {
+      if (st->dma_done[d][q]) cudaEventDestroy(st->dma_done[d][q]);
+      if (st->dma[d][q]) cudaStreamDestroy(st->dma[d][q]);
+    }
   delete st;
 }
 

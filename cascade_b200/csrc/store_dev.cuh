@@ -169,6 +169,9 @@ struct PoolDev {
   uint32_t taken[kNumClasses];   // pops claimed by the running alloc batch
 };
 
+// Epoch buckets per class of the demotion-candidate histogram.
+constexpr int kVictimBuckets = 1024;
+
 // One live slot as reported by a scan (victim selection for demotion).
 struct ScanRec {
   uint32_t slot;
@@ -239,10 +242,17 @@ int launch_index_lookup(Slot *slots, uint64_t mask, const uint64_t *keys,
 int launch_index_relocate(Slot *slots, const uint32_t *slot_idx,
                           const uint64_t *offsets, const uint32_t *flags,
                           const uint8_t *headers, int n, cudaStream_t s);
-// Live slots whose flags include `tier_flag`, in slot order of discovery.
-int launch_index_scan(const Slot *slots, uint64_t nslots, uint32_t tier_flag,
-                      uint32_t *count, ScanRec *out, uint32_t max_out,
-                      cudaStream_t s);
+// Demotion candidates (live HBM slots; class 1 = prefix blocks when
+// `semantic`, else class 0), by epoch bucket over [0, span):
+// bytes / count[cls * kVictimBuckets + b] = HBM payload bytes and slots.
+int launch_victim_hist(const Slot *slots, uint64_t nslots, int semantic,
+                       uint64_t span, unsigned long long *bytes,
+                       uint32_t *count, cudaStream_t s);
+// Every candidate of class c in buckets 0..cut_c (cut -1: none), in no
+// particular order; *n_out = how many (at most max_out are written).
+int launch_victim_collect(const Slot *slots, uint64_t nslots, int semantic,
+                          uint64_t span, int cut0, int cut1, uint32_t *n_out,
+                          ScanRec *out, uint32_t max_out, cudaStream_t s);
 
 // Pool: req[i] = payload bytes to allocate, or kNoRequest.  offsets[i] =
 // the allocation, or kInvalidOffset (no request, or the pool is full).

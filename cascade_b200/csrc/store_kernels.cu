@@ -158,25 +158,63 @@ __global__ void relocate_kernel(Slot *slots, const uint32_t *__restrict__ idx,
   sl.hdr_zp = h[4];
 }
 
-__global__ void scan_kernel(const Slot *__restrict__ slots, uint64_t nslots,
-                            uint32_t tier_flag, uint32_t *count,
-                            ScanRec *__restrict__ out, uint32_t max_out) {
+// Demotion candidates.  A live HBM slot belongs to class 1 when it is a
+// prefix block and prefix protection is on, else to class 0; within a class
+// the least recent epoch goes first.  Epochs are bucketed linearly over
+// [0, span) into kVictimBuckets buckets per class; the histogram sums each
+// bucket's HBM payload bytes and slot count, the host picks per class the
+// last bucket it needs, and the collect pass writes out every candidate up
+// to that bucket.  Only those few are sorted on the host.
+__device__ __forceinline__ bool victim_of(const Slot &sl, int semantic,
+                                          uint64_t span, int &cls, int &bucket,
+                                          uint64_t &pay) {
+  if (sl.state != kLive || !(sl.flags & kTierHbm)) return false;
+  cls = (semantic && (sl.flags & kFlagPrefix)) ? 1 : 0;
+  const uint64_t e = sl.epoch < span ? sl.epoch : span - 1;
+  bucket = (int)((e * (uint64_t)kVictimBuckets) / span);
+  pay = (sl.flags & kFlagQ8) ? sl.size / 2 : sl.size;
+  return true;
+}
+
+__global__ void victim_hist_kernel(const Slot *__restrict__ slots,
+                                   uint64_t nslots, int semantic,
+                                   uint64_t span,
+                                   unsigned long long *__restrict__ bytes,
+                                   uint32_t *__restrict__ count) {
   for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x;
        i < nslots; i += (uint64_t)gridDim.x * blockDim.x) {
+    int cls, b;
+    uint64_t pay;
+    if (!victim_of(slots[i], semantic, span, cls, b, pay)) continue;
+    atomicAdd(&bytes[cls * kVictimBuckets + b], (unsigned long long)pay);
+    atomicAdd(&count[cls * kVictimBuckets + b], 1u);
+  }
+}
+
+__global__ void victim_collect_kernel(const Slot *__restrict__ slots,
+                                      uint64_t nslots, int semantic,
+                                      uint64_t span, int cut0, int cut1,
+                                      uint32_t *__restrict__ n_out,
+                                      ScanRec *__restrict__ out,
+                                      uint32_t max_out) {
+  for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x;
+       i < nslots; i += (uint64_t)gridDim.x * blockDim.x) {
+    int cls, b;
+    uint64_t pay;
     const Slot &sl = slots[i];
-    if (sl.state != kLive || !(sl.flags & tier_flag)) continue;
-    const uint32_t k = atomicAdd(count, 1u);
-    if (k < max_out) {
-      ScanRec r;
-      r.slot = (uint32_t)i;
-      r.flags = sl.flags;
-      r.size = sl.size;
-      r.offset = sl.offset;
-      r.epoch = sl.epoch;
-      r.hdr_scale = sl.hdr_scale;
-      r.hdr_zp = sl.hdr_zp;
-      out[k] = r;
-    }
+    if (!victim_of(sl, semantic, span, cls, b, pay)) continue;
+    if (b > (cls ? cut1 : cut0)) continue;
+    const uint32_t k = atomicAdd(n_out, 1u);
+    if (k >= max_out) continue;
+    ScanRec r;
+    r.slot = (uint32_t)i;
+    r.flags = sl.flags;
+    r.size = sl.size;
+    r.offset = sl.offset;
+    r.epoch = sl.epoch;
+    r.hdr_scale = sl.hdr_scale;
+    r.hdr_zp = sl.hdr_zp;
+    out[k] = r;
   }
 }
 
@@ -341,13 +379,26 @@ int launch_index_relocate(Slot *slots, const uint32_t *slot_idx,
   return CASCADE_OK;
 }
 
-int launch_index_scan(const Slot *slots, uint64_t nslots, uint32_t tier_flag,
-                      uint32_t *count, ScanRec *out, uint32_t max_out,
-                      cudaStream_t s) {
-  CB_CUDA(cudaMemsetAsync(count, 0, sizeof(uint32_t), s));
+int launch_victim_hist(const Slot *slots, uint64_t nslots, int semantic,
+                       uint64_t span, unsigned long long *bytes,
+                       uint32_t *count, cudaStream_t s) {
+  CB_CUDA(cudaMemsetAsync(bytes, 0, 2 * kVictimBuckets * sizeof(*bytes), s));
+  CB_CUDA(cudaMemsetAsync(count, 0, 2 * kVictimBuckets * sizeof(*count), s));
   const int grid = grid_for(nslots, 256, 8);
-  scan_kernel<<<grid, 256, 0, s>>>(slots, nslots, tier_flag, count, out,
-                                   max_out);
+  victim_hist_kernel<<<grid, 256, 0, s>>>(slots, nslots, semantic, span,
+                                          bytes, count);
+  count_launches(1);
+  CB_CUDA(cudaGetLastError());
+  return CASCADE_OK;
+}
+
+int launch_victim_collect(const Slot *slots, uint64_t nslots, int semantic,
+                          uint64_t span, int cut0, int cut1, uint32_t *n_out,
+                          ScanRec *out, uint32_t max_out, cudaStream_t s) {
+  CB_CUDA(cudaMemsetAsync(n_out, 0, sizeof(uint32_t), s));
+  const int grid = grid_for(nslots, 256, 8);
+  victim_collect_kernel<<<grid, 256, 0, s>>>(slots, nslots, semantic, span,
+                                             cut0, cut1, n_out, out, max_out);
   count_launches(1);
   CB_CUDA(cudaGetLastError());
   return CASCADE_OK;

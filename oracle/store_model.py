@@ -21,8 +21,15 @@ behaviour the product implements, and says so:
   * a DRAM block stored raw (size < 64, or compression off when it was
     put) is returned raw; the reference "decompresses" any DRAM block when
     kv_compression is on (1149-1156), garbling those.
-Eviction (1001-1018) and the Lustre tier are not modelled: scenarios that
-use the model stay within capacity or expect the put to fail.
+Demotion (evict_gpu_to_shm, 998-1018, from put 1100-1103 and promote_to_gpu
+1039-1056) is modelled with this library's victim order, which differs from
+the reference's: the least recently put or read GPU block first over the
+whole tier (the reference takes the LRU tail of its largest index shard),
+prefix blocks last when semantic_eviction and dedup are on; a demoted block
+goes to the DRAM tier in the DRAM tier's format (KVCompressor output when
+kv_compression applies; the reference demotes raw bytes), and a demotion
+that finds the DRAM tier full ends that put's demotions (the reference
+would push on to its Lustre tier, which is not modelled).
 
 Pinned by tests/test_store_model.py against the compiled reference
 (oracle/_ref) on the configurations the reference can run here
@@ -30,6 +37,7 @@ Pinned by tests/test_store_model.py against the compiled reference
 """
 from __future__ import annotations
 
+from collections import OrderedDict
 from dataclasses import dataclass, field
 
 import numpy as np
@@ -50,8 +58,11 @@ class StoreModel:
     kv_compression: bool = False
     dedup_enabled: bool = True
     promotion_enabled: bool = True
+    semantic_eviction: bool = True
     gpu_q8: bool = False  # B200 extension: HBM keeps the INT8 form too
-    gpu: dict = field(default_factory=dict)     # id -> bytes returned by get
+    # id -> bytes returned by get, least recently used first
+    gpu: OrderedDict = field(default_factory=OrderedDict)
+    gpu_comp: dict = field(default_factory=dict)  # id -> INT8 form (gpu_q8)
     shm: dict = field(default_factory=dict)     # id -> (payload, is_q8, orig)
     known: set = field(default_factory=set)
     prefix: set = field(default_factory=set)
@@ -64,6 +75,55 @@ class StoreModel:
         """GPU-tier bytes of a block: its size (the reference's raw tier), or
         the INT8 payload size/2 in the gpu_q8 extension."""
         return size // 2 if (self.gpu_q8 and self._q8(size)) else size
+
+    def _gpu_store(self, block_id, data, comp):
+        """Puts a block into the GPU tier (most recently used end)."""
+        if self.gpu_q8 and comp is not None:
+            self.gpu[block_id] = kv_decompress(comp, 2 * (data.size // 2))
+            self.gpu_comp[block_id] = comp
+        else:
+            self.gpu[block_id] = data.copy()
+        self.stats["gpu_used"] += self._hbm_bytes(data.size)
+
+    def _victim(self):
+        """The GPU block to demote next: least recently used first, prefix
+        blocks last when prefix protection is on."""
+        protect = self.semantic_eviction and self.dedup_enabled
+        for bid in self.gpu:
+            if not (protect and bid in self.prefix):
+                return bid
+        return next(iter(self.gpu), None)
+
+    def _evict_gpu_to_shm(self, needed: int):
+        """Demotes GPU blocks until `needed` GPU bytes are freed, while the
+        DRAM tier has room (evict_gpu_to_shm, cascade_core.cpp:998-1018)."""
+        if self.shm_capacity <= 0:
+            return
+        s = self.stats
+        freed = 0
+        while freed < needed:
+            bid = self._victim()
+            if bid is None:
+                return
+            data = self.gpu[bid]
+            size = data.size
+            if self._q8(size):
+                payload = self.gpu_comp.get(bid)
+                if payload is None:
+                    payload = kv_compress(data)
+                entry = (payload, True, size)
+            else:
+                entry = (data.copy(), False, size)
+            if s["shm_used"] + entry[0].size > self.shm_capacity:
+                return
+            del self.gpu[bid]
+            self.gpu_comp.pop(bid, None)
+            hbm = self._hbm_bytes(size)
+            s["gpu_used"] -= hbm
+            freed += hbm
+            self.shm[bid] = entry
+            s["shm_used"] += entry[0].size
+            s["gpu_evictions"] += 1
 
     def put(self, block_id: str, data: np.ndarray, is_prefix=False) -> bool:
         data = np.ascontiguousarray(data, dtype=np.uint8)
@@ -79,15 +139,13 @@ class StoreModel:
         stored = False
         if self.use_gpu and self.gpu_capacity > 0:
             hbm = self._hbm_bytes(size)
+            if s["gpu_used"] + hbm > self.gpu_capacity:
+                self._evict_gpu_to_shm(hbm)
             if s["gpu_used"] + hbm <= self.gpu_capacity:
                 if block_id in self.gpu or block_id in self.shm:
                     stored = True
                 else:
-                    if self.gpu_q8 and comp is not None:
-                        self.gpu[block_id] = kv_decompress(comp, 2 * (size // 2))
-                    else:
-                        self.gpu[block_id] = data.copy()
-                    s["gpu_used"] += hbm
+                    self._gpu_store(block_id, data, comp)
                     stored = True
         if not stored and self.shm_capacity > 0:
             acc = comp.size if comp is not None else size
@@ -115,6 +173,7 @@ class StoreModel:
         s = self.stats
         if block_id in self.gpu:
             s["gpu_hits"] += 1
+            self.gpu.move_to_end(block_id)
             return True, self.gpu[block_id]
         if block_id in self.shm:
             s["shm_hits"] += 1
@@ -122,16 +181,14 @@ class StoreModel:
             out = kv_decompress(payload, 2 * (orig // 2)) if q8 else payload
             if self.promotion_enabled and self.use_gpu and self.gpu_capacity > 0:
                 hbm = self._hbm_bytes(out.size)
+                if s["gpu_used"] + hbm > self.gpu_capacity:
+                    self._evict_gpu_to_shm(hbm)
                 if s["gpu_used"] + hbm <= self.gpu_capacity:
-                    if self.gpu_q8 and self._q8(out.size):
-                        self.gpu[block_id] = kv_decompress(
-                            kv_compress(out), 2 * (out.size // 2))
-                    else:
-                        self.gpu[block_id] = out.copy()
-                    s["gpu_used"] += hbm
-                    s["promotions_to_gpu"] += 1
+                    comp = kv_compress(out) if self._q8(out.size) else None
                     del self.shm[block_id]
                     s["shm_used"] -= payload.size
+                    self._gpu_store(block_id, out, comp)
+                    s["promotions_to_gpu"] += 1
             return True, out
         s["misses"] += 1
         return False, None

@@ -21,8 +21,9 @@ pytestmark = pytest.mark.gpu
 
 def make_store(use_gpu=False, gpu_cap=64 << 20, shm_cap=64 << 20,
                kv_compression=False, dedup=True, gpu_q8=False,
-               promotion=True):
+               promotion=True, semantic=True):
     cfg = cc.CascadeConfig()
+    cfg.semantic_eviction = semantic
     cfg.use_gpu = use_gpu
     cfg.gpu_capacity_bytes = gpu_cap
     cfg.shm_capacity_bytes = shm_cap
@@ -376,8 +377,9 @@ def test_overflowing_batch_leaves_serial_end_state():
     """A batch of 12 blocks into an HBM tier that holds 8: the blocks left in
     HBM are the ones serial puts (each demoting the least recently used,
     prefix blocks last) would leave there, i.e. the batch's prefix blocks and
-    its latest blocks.  The batch places them directly, so it counts no
-    demotions where the serial puts count 4."""
+    its latest blocks, and every counter equals the serial puts' (4 GPU
+    evictions: the batch's blocks that serial puts would have stored and
+    demoted go to DRAM directly and count as evictions)."""
     S = 4096
     rng = np.random.default_rng(41)
     blocks = [rng.integers(0, 256, S, dtype=np.uint8) for _ in range(12)]
@@ -407,6 +409,7 @@ def test_overflowing_batch_leaves_serial_end_state():
     assert stored == 12 and (status == 0).all()
     s = _stats(batch)
     assert s["gpu_used"] == 8 * S and s["shm_used"] == 4 * S
+    assert s == _stats(serial)
     want = ["shm" if i in (1, 2, 3, 4) else "gpu" for i in range(12)]
     assert tiers(serial) == want
     assert tiers(batch) == want
@@ -441,3 +444,61 @@ def test_demotion_to_int8_dram_and_promotion(gpu_q8):
     s = _stats(st)
     assert s["promotions_to_gpu"] >= 2
     assert s["gpu_used"] <= 4 * hbm_per_block
+
+
+@pytest.mark.parametrize("semantic", [True, False], ids=["prefix", "lru"])
+@pytest.mark.parametrize("kv_compression,gpu_q8",
+                         [(False, False), (True, False), (True, True)],
+                         ids=["raw", "int8-dram", "int8-hbm"])
+def test_overflowing_batches_match_serial_model(kv_compression, gpu_q8,
+                                                semantic):
+    """Rounds of content-addressed batches (new blocks, repeats of earlier
+    ones, prefix blocks) into an HBM tier of 16 blocks, each followed by
+    single gets (which touch, and promote DRAM hits): after every round the
+    counters, and every block's bytes and tier, equal the serial model's
+    (oracle/store_model.py: each put demotes least recently used blocks,
+    prefix blocks last, until it fits)."""
+    S = 8192
+    rng = np.random.default_rng(97 + 10 * kv_compression + gpu_q8 + 7 * semantic)
+    universe = [rng.integers(0, 256, S, dtype=np.uint8) for _ in range(120)]
+    ids = [oracle.block_id(b) for b in universe]
+    hbm_per_block = S // 2 if gpu_q8 else S
+    st = make_store(use_gpu=True, gpu_cap=16 * hbm_per_block, shm_cap=32 << 20,
+                    kv_compression=kv_compression, gpu_q8=gpu_q8,
+                    semantic=semantic)
+    m = StoreModel(use_gpu=True, gpu_capacity=16 * hbm_per_block,
+                   shm_capacity=32 << 20, kv_compression=kv_compression,
+                   gpu_q8=gpu_q8, semantic_eviction=semantic)
+    is_prefix = rng.random(120) < 0.2
+    seen = []
+    buf = np.zeros(S, np.uint8)
+    for rnd in range(10):
+        k = int(rng.integers(6, 26))
+        fresh = list(range(12 * rnd, 12 * rnd + 12))
+        picks = [int(rng.choice(fresh)) if (not seen or rng.random() < 0.7)
+                 else int(rng.choice(seen)) for _ in range(k)]
+        rows = torch.from_numpy(np.stack([universe[p] for p in picks])).to(DEV)
+        pre = [bool(is_prefix[p]) for p in picks]
+        stored, status, _ = st.put_batch(rows, is_prefix=pre,
+                                         return_status=True)
+        want = [m.put(ids[p], universe[p], is_prefix=q)
+                for p, q in zip(picks, pre)]
+        assert stored == sum(want), rnd
+        seen.extend(picks)
+        assert _stats(st) == m.stats, ("after put", rnd)
+        for p in rng.choice(sorted(set(seen)), 5):
+            got = st.get(ids[p], buf)
+            mf, mdata = m.get(ids[p])
+            assert got == (mf, S), (rnd, p)
+            assert np.array_equal(buf, mdata), (rnd, p)
+        assert _stats(st) == m.stats, ("after get", rnd)
+    # every block: found, its bytes, and which tier answered
+    for p in sorted(set(seen)):
+        before = _stats(st)
+        got = st.get(ids[p], buf)
+        mf, mdata = m.get(ids[p])
+        assert got == (mf, S) and np.array_equal(buf, mdata), p
+        after = _stats(st)
+        assert {f: after[f] - before[f] for f in ("gpu_hits", "shm_hits")} == \
+            {f: m.stats[f] - before[f] for f in ("gpu_hits", "shm_hits")}, p
+    assert _stats(st) == m.stats
