@@ -805,14 +805,23 @@ def run_extra(args):
     torch.cuda.empty_cache()
     bb = rows.shape[1]
     cap = int(args.cap_gib * (1 << 30))
-    cfg = make_cfg(cc, ctx.local, cap, shm=(64 << 30) if ctx.world == 1 else 0)
+    # A pool smaller than a step's INT8 payload overflows to the DRAM tier.
+    capped = n * (bb // 2) > cap
+    cfg = make_cfg(cc, ctx.local, cap,
+                   shm=(64 << 30) if (ctx.world == 1 or capped) else 0)
     if ctx.world > 1:
         from cascade_b200.sharded import ShardedCascadeStore
         store = ShardedCascadeStore(cfg)
+        # A sharded put holds its whole batch in HBM while the keys resolve
+        # (demoting older payloads first), so a capped pool takes the step
+        # in slices that fit; every rank slices the same way.
+        per = max(1, int(0.8 * cap // (bb // 2))) if capped else n
+        cuts = list(range(0, n, per)) + [n]
 
         def put():
             store.clear()
-            return store.put_batch(rows)
+            return sum(store.put_batch(rows[a:b])
+                       for a, b in zip(cuts[:-1], cuts[1:]))
     else:
         store = cc.CascadeStore(cfg)
         ptrs = np.arange(n, dtype=np.uint64) * np.uint64(bb) + np.uint64(rows.data_ptr())
@@ -845,6 +854,8 @@ def run_extra(args):
             "ms_per_step": ms, "steps": args.steps, "warmup": args.warmup,
             "blocks_total": ctx.world * n, "block_bytes": bb,
             "hbm_pool_gib_per_gpu": args.cap_gib,
+            "dram_tier": bool(capped or ctx.world == 1),
+            "put_slices": (len(cuts) - 1) if ctx.world > 1 else 1,
             "dedup_hits_total": hits,
             "expected_hits": ctx.world * n - distinct,
             "gpu_evictions_total": int(ev[:, pool_n + 2].sum()),

@@ -5,7 +5,10 @@
 //
 // Reference: CascadeStore (cascade.hpp:420-502, cascade_core.cpp:960-1303),
 // GPUBackend (gpu_backend.cu:166-528), ShmBackend (cascade_core.cpp:237-569).
+#include <unistd.h>
+
 #include <algorithm>
+#include <cstdio>
 #include <cstring>
 #include <deque>
 #include <memory>
@@ -134,6 +137,7 @@ struct Store {
   uint8_t *shard_aux = nullptr;  // staged records + per-owner counters
   size_t oc_aux_cap = 0;
   int shard_rank = 0;            // this store's rank in the open batch
+  int shard_world = 1;           // and the number of ranks
   size_t shard_open = 0;         // blocks of the open sharded batch
   size_t shard_get_open = 0;     // keys of the open sharded get
   size_t resolve_pending = 0;    // records of a resolve not yet counted
@@ -141,6 +145,14 @@ struct Store {
   // peer_rank is this store's own pool.
   std::vector<uint8_t *> peer_base;
   int peer_rank = -1;
+  // The other ranks' DRAM tiers (shared arenas), by rank; null for this
+  // rank and for ranks without one.
+  std::vector<std::unique_ptr<DramView>> peer_dram;
+  // Relocation records for the next sharded begin: blocks this rank holds
+  // for other owners that it demoted to its DRAM tier.
+  std::vector<ShardRecord> shard_moves;
+  uint8_t *h_moves = nullptr;  // pinned copy of them on the way to d_send
+  size_t h_moves_cap = 0;
   uint8_t *d_stage = nullptr;  // device staging for host buffers
   size_t d_stage_cap = 0;
   uint8_t *h_stage = nullptr;  // pinned staging for host buffers
@@ -549,7 +561,8 @@ struct ArenaGuard {
 
 // Moves `vic` from HBM to their DRAM places: INT8 forms of raw victims on
 // the device, payloads to the arena over the copy streams, slots relocated,
-// pool space returned.  Counts them as gpu_evictions.
+// pool space returned.  Counts them as gpu_evictions.  On return `vic` is
+// reordered and carries each block's DRAM-format header.
 static int demote(Store &st, std::vector<Demotion> &vic) {
   if (vic.empty()) return CASCADE_OK;
   ArenaGuard guard{st.dram.get(), {}};
@@ -606,7 +619,8 @@ static int demote(Store &st, std::vector<Demotion> &vic) {
     const bool hq8 = (v.r.flags & kFlagQ8) != 0;
     oc.h_slot[j] = v.r.slot;
     oc.h_off[j] = v.dram_off;
-    oc.h_flags[j] = (v.r.flags & kFlagPrefix) | kTierDram | (v.dq8 ? kFlagQ8 : 0);
+    oc.h_flags[j] = (v.r.flags & (kFlagPrefix | kFlagHeld | 0xff0000u)) |
+                    kTierDram | (v.dq8 ? kFlagQ8 : 0);
     oc.h_req[j] = payload_bytes(v.r.size, hq8);
     oc.h_seqs[j] = v.r.offset;
     uint8_t *h = oc.h_hdr + 8 * j;
@@ -630,7 +644,13 @@ static int demote(Store &st, std::vector<Demotion> &vic) {
   if (!rc) rc = launch_pool_free_unstored(st.d_pool, oc.req, oc.seqs,
                                           oc.status, (int)k, s);
   if (rc) return rc;
+  if (nq)  // the headers the quantise wrote, for the caller's records
+    CB_CUDA(cudaMemcpyAsync(oc.h_hdr, oc.hdr, nq * 8, cudaMemcpyDeviceToHost, s));
   CB_CUDA(cudaStreamSynchronize(s));
+  for (size_t j = 0; j < nq; ++j) {
+    std::memcpy(&vic[j].r.hdr_scale, oc.h_hdr + 8 * j, 4);
+    vic[j].r.hdr_zp = oc.h_hdr[8 * j + 4];
+  }
   guard.keep();
   st.gpu_used -= freed;
   st.shm_used += acc_total;
@@ -1265,7 +1285,8 @@ static int upload_keys(Store &st, size_t n, const uint8_t *h_keys) {
 // is given (another rank's pool mapped into this process).
 static int deliver_locked(Store &st, size_t n, const uint64_t *out,
                           const uint8_t *deliver,
-                          const uint64_t *bases = nullptr) {
+                          const uint64_t *bases = nullptr,
+                          const uint64_t *dram_src = nullptr) {
   cudaStream_t s = st.s;
   // Copy jobs and dequantise jobs, packed into the scratch arrays:
   //   copies:  ptrs (src) / dst / eff_raw (bytes)
@@ -1297,13 +1318,14 @@ static int deliver_locked(Store &st, size_t n, const uint64_t *out,
       src = (bases ? bases[i] : (uint64_t)(uintptr_t)st.pool) + f.offset;
     } else {  // DRAM: bring the payload up first
       uint64_t pay = payload_bytes(f.size, q8);
+      const void *from = dram_src ? reinterpret_cast<const void *>(dram_src[i])
+                                  : st.dram->ptr(f.offset);
       if (!q8) {
-        jobs.push_back({reinterpret_cast<void *>(out[i]),
-                        st.dram->ptr(f.offset), f.size});
+        jobs.push_back({reinterpret_cast<void *>(out[i]), from, f.size});
         continue;
       }
       src = (uint64_t)(uintptr_t)(st.d_q8stage + stage_off);
-      jobs.push_back({st.d_q8stage + stage_off, st.dram->ptr(f.offset), pay});
+      jobs.push_back({st.d_q8stage + stage_off, from, pay});
       stage_off += (pay + 255) & ~uint64_t(255);
     }
     if (q8) {
@@ -1353,7 +1375,9 @@ static int deliver_locked(Store &st, size_t n, const uint64_t *out,
   // Promotion of DRAM hits (promote_to_gpu, cascade_core.cpp:1039-1056):
   // the decoded block, now in out[i], is stored in HBM and its DRAM space
   // released.
-  if (!(st.cfg.promotion_enabled && st.hbm)) return CASCADE_OK;
+  // A sharded read (bases given) carries no index slot of this rank, so its
+  // DRAM hits are not promoted.
+  if (!(st.cfg.promotion_enabled && st.hbm) || bases) return CASCADE_OK;
   // The promotions replayed in get order (promote_to_gpu demotes older
   // blocks when HBM is full): a block that serial gets would promote and
   // demote again within the batch stays in DRAM and counts both ways.
@@ -1621,6 +1645,7 @@ static void close_peer_pools(Store &st) {
       cudaIpcCloseMemHandle(st.peer_base[r]);
   st.peer_base.clear();
   st.peer_rank = -1;
+  st.peer_dram.clear();
 }
 
 static void destroy_store(Store *st) {
@@ -1639,6 +1664,7 @@ static void destroy_store(Store *st) {
     if (sc->hblob) cudaFreeHost(sc->hblob);
   }
   if (st->shard_aux) cudaFree(st->shard_aux);
+  if (st->h_moves) cudaFreeHost(st->h_moves);
   if (st->d_stage) cudaFree(st->d_stage);
   if (st->h_stage) cudaFreeHost(st->h_stage);
   if (st->d_q8stage) cudaFree(st->d_q8stage);
@@ -1664,6 +1690,7 @@ static int clear_store(Store &st) {
   if (rc) return rc;
   if (st.dram) st.dram->reset();
   st.names.clear();
+  st.shard_moves.clear();
   st.claimed = 0;
   st.gpu_used = st.shm_used = st.gpu_hits = st.shm_hits = st.misses = 0;
   st.dedup_hits = st.gpu_evictions = st.promotions_to_gpu = 0;
@@ -1943,7 +1970,7 @@ __global__ void shard_unpack_kernel(int m, uint32_t rank,
   const int j = blockIdx.x * blockDim.x + threadIdx.x;
   if (j >= m) return;
   const ShardRecord r = in[j];
-  const bool used = r.src_idx != kUnused;
+  const bool used = r.src_idx != kUnused && r.src_idx != kMoveIdx;
   keys[2 * (size_t)j] = r.k0;
   keys[2 * (size_t)j + 1] = r.k1;
   seqs[j] = used ? r.seq : kNoSeq;
@@ -1965,6 +1992,7 @@ __global__ void shard_reply_kernel(int m, const ShardRecord *__restrict__ in,
   if (j >= m) return;
   ShardReply r;
   r.src_idx = in[j].src_idx;
+  if (r.src_idx == kMoveIdx) r.src_idx = kUnused;  // moves get no reply
   r.status = r.src_idx == kUnused ? kUnused : status[j];
   out[j] = r;
 }
@@ -1983,9 +2011,86 @@ __global__ void shard_apply_kernel(int m, int n,
     atomicExch(err, CASCADE_ERR_INVALID);
 }
 
+// Relocation records into their owners' segments, after the batch's own.
+__global__ void shard_moves_kernel(int k, int world, uint32_t cap,
+                                   const ShardRecord *__restrict__ moves,
+                                   uint32_t *__restrict__ cursor,
+                                   ShardRecord *__restrict__ out,
+                                   int *__restrict__ err) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= k) return;
+  const ShardRecord r = moves[i];
+  const int o = owner_of(r.k0, world);
+  const uint32_t c = atomicAdd(&cursor[o], 1u);
+  if (c < cap)
+    out[(size_t)o * cap + c] = r;
+  else
+    atomicExch(err, CASCADE_ERR_INVALID);
+}
+
 inline int nblocks(size_t n) { return (int)((n + 255) / 256); }
 
 }  // namespace
+
+// Makes room in this rank's HBM pool for a batch of n blocks of h_sizes by
+// demoting its least recently used payloads to its DRAM tier (prefix blocks
+// last), and prepares a relocation record for each demoted payload whose
+// key another rank owns, for the next begin to send.  A sharded put keeps
+// its whole batch in HBM until the keys resolve, so the room is made first.
+static int shard_prepare(Store &st, size_t n, const uint64_t *h_sizes,
+                         int world, int rank, uint64_t *n_moves) {
+  *n_moves = 0;
+  st.shard_moves.clear();
+  if (!st.hbm || !st.dram_tier || n == 0) return CASCADE_OK;
+  uint64_t need = 0;
+  for (size_t i = 0; i < n; ++i)
+    need += payload_bytes(h_sizes[i], q8_eligible(st, h_sizes[i], false));
+  if (st.gpu_used + need <= st.pool_cap) return CASCADE_OK;
+  const uint64_t deficit = st.gpu_used + need - st.pool_cap;
+  Candidates cand;
+  int rc = select_candidates(st, deficit, cand);
+  if (rc) return rc;
+  std::vector<Demotion> vic;
+  {
+    ArenaGuard guard{st.dram.get(), {}};
+    uint64_t freed = 0, shm = st.shm_used;
+    for (int c = 0; c < 2 && freed < deficit; ++c)
+      for (const ScanRec &r : cand.c[c]) {
+        if (freed >= deficit) break;
+        const bool hq8 = (r.flags & kFlagQ8) != 0;
+        const bool dq8 = hq8 || q8_eligible(st, r.size, true);
+        const uint64_t acc = dram_accounted(r.size, dq8);
+        if (shm + acc > st.dram->capacity()) break;
+        const uint64_t off = st.dram->alloc(payload_bytes(r.size, dq8));
+        if (off == DramArena::kNone) break;
+        guard.held.emplace_back(off, payload_bytes(r.size, dq8));
+        vic.push_back({r, off, dq8});
+        freed += payload_bytes(r.size, hq8);
+        shm += acc;
+      }
+    guard.keep();  // demote() owns the space now
+  }
+  if ((rc = demote(st, vic))) return rc;
+  for (const Demotion &v : vic) {
+    if (!(v.r.flags & kFlagHeld)) continue;  // this rank's own entry moved
+    ShardRecord m;
+    m.k0 = v.r.k0;
+    m.k1 = v.r.k1;
+    m.seq = kNoSeq;
+    m.offset = v.dram_off;
+    m.size = v.r.size;
+    m.flags = (v.r.flags & kFlagPrefix) | kTierDram | (v.dq8 ? kFlagQ8 : 0) |
+              kFlagRelocate;
+    m.holder = (uint32_t)rank;
+    m.src_idx = kMoveIdx;
+    m.hdr_scale = v.r.hdr_scale;
+    m.hdr_zp = v.r.hdr_zp;
+    m.pad = 0;
+    if (owner_of(m.k0, world) != rank) st.shard_moves.push_back(m);
+  }
+  *n_moves = st.shard_moves.size();
+  return CASCADE_OK;
+}
 
 // Counts the keys the last cascade_shard_resolve stored, once its device
 // work is done (it returns without waiting), and reports an index that ran
@@ -2013,6 +2118,35 @@ static int join_back(Store &st, void *stream) {
   return CASCADE_OK;
 }
 
+// The relocation records shard_prepare made, into the send buffer after
+// the batch's records (cursor: the per-owner fill, on the device).
+static int shard_send_moves(Store &st, int world, size_t cap,
+                            uint32_t *cursor, uint8_t *d_send) {
+  const size_t k = st.shard_moves.size();
+  if (!k) return CASCADE_OK;
+  const size_t bytes = k * sizeof(ShardRecord);
+  if (bytes > st.h_moves_cap) {
+    CB_CUDA(cudaStreamSynchronize(st.s));  // the old buffer may be in flight
+    if (st.h_moves) CB_CUDA(cudaFreeHost(st.h_moves));
+    st.h_moves = nullptr;
+    st.h_moves_cap = 0;
+    CB_CUDA(cudaHostAlloc(&st.h_moves, bytes, cudaHostAllocDefault));
+    st.h_moves_cap = bytes;
+  }
+  std::memcpy(st.h_moves, st.shard_moves.data(), bytes);
+  // shard_aux holds the cursors, then room for the moves (begin sized it)
+  ShardRecord *d_moves = reinterpret_cast<ShardRecord *>(st.shard_aux + 2048);
+  CB_CUDA(cudaMemcpyAsync(d_moves, st.h_moves, bytes, cudaMemcpyHostToDevice,
+                          st.s));
+  shard_moves_kernel<<<nblocks(k), 256, 0, st.s>>>(
+      (int)k, world, (uint32_t)cap, d_moves, cursor,
+      reinterpret_cast<ShardRecord *>(d_send), st.sc.err);
+  count_launches(1);
+  CB_CUDA(cudaGetLastError());
+  st.shard_moves.clear();
+  return CASCADE_OK;
+}
+
 // The batch's descriptors are uploaded (and, with digests_ready, its hash is
 // under way on the hash stream): store it speculatively and write the
 // records.  Does not wait for the device.
@@ -2023,7 +2157,9 @@ static int shard_begin_staged(Store &st, size_t n, uint64_t max_size,
   int rc;
   CB_CHECK(can_speculate(st, n), CASCADE_ERR_NOMEM,
            "sharded put: the HBM pool cannot hold the whole batch");
-  if ((rc = ensure_device_buf(st.shard_aux, st.oc_aux_cap, 2048, st.s)))
+  if ((rc = ensure_device_buf(st.shard_aux, st.oc_aux_cap,
+                              2048 + st.shard_moves.size() * sizeof(ShardRecord),
+                              st.s)))
     return rc;
   uint32_t *cursor = reinterpret_cast<uint32_t *>(st.shard_aux);
   if ((rc = speculate_local(st, n, h_prefix, max_size, digests_ready)))
@@ -2039,11 +2175,13 @@ static int shard_begin_staged(Store &st, size_t n, uint64_t max_size,
       reinterpret_cast<ShardRecord *>(d_send), st.sc.err);
   count_launches(1);
   CB_CUDA(cudaGetLastError());
+  if ((rc = shard_send_moves(st, world, cap, cursor, d_send))) return rc;
   CB_CUDA(cudaMemcpyAsync(st.sc.h_off, st.sc.off, n * 8,
                           cudaMemcpyDeviceToHost, s));
   CB_CUDA(cudaMemcpyAsync(st.sc.h_err, st.sc.err, sizeof(int),
                           cudaMemcpyDeviceToHost, s));
   st.shard_rank = rank;
+  st.shard_world = world;
   st.shard_open = n;
   return CASCADE_OK;
 }
@@ -2134,6 +2272,10 @@ static int shard_resolve(Store &st, const uint8_t *d_recv, size_t m,
       oc.sizes, oc.flags, oc.hdr);
   count_launches(1);
   CB_CUDA(cudaGetLastError());
+  // Entries whose holders demoted the payload follow it first.
+  if ((rc = launch_index_apply_moves(st.slots, st.nslots - 1, d_recv, (int)m,
+                                     (uint32_t)st.shard_rank, s)))
+    return rc;
   CB_CUDA(cudaMemsetAsync(oc.err, 0, sizeof(int), s));
   const uint64_t epoch = st.next_epoch;
   st.next_epoch += m;
@@ -2154,6 +2296,66 @@ static int shard_resolve(Store &st, const uint8_t *d_recv, size_t m,
   CB_CUDA(cudaMemcpyAsync(oc.h_status, oc.status, m, cudaMemcpyDeviceToHost, s));
   CB_CUDA(cudaMemcpyAsync(oc.h_err, oc.err, sizeof(int), cudaMemcpyDeviceToHost, s));
   st.resolve_pending = m;
+  return CASCADE_OK;
+}
+
+// With a DRAM tier, the blocks this rank stored for keys that other ranks
+// own get a held slot in this rank's index (kFlagHeld), so that demotion
+// here sees every payload in this rank's pool, in put order.
+static int shard_hold(Store &st, size_t n) {
+  if (!st.dram_tier) return CASCADE_OK;
+  cudaStream_t s = st.s;
+  CB_CUDA(cudaMemcpyAsync(st.sc.h_digests, st.sc.digests, 32 * n,
+                          cudaMemcpyDeviceToHost, s));
+  CB_CUDA(cudaMemcpyAsync(st.sc.h_hdr, st.sc.hdr, 8 * n,
+                          cudaMemcpyDeviceToHost, s));
+  CB_CUDA(cudaStreamSynchronize(s));
+  std::vector<size_t> held;
+  for (size_t i = 0; i < n; ++i)
+    if (st.sc.h_status[i] == CASCADE_PUT_STORED &&
+        (st.sc.h_flags[i] & kTierHbm) &&
+        owner_of(le64(st.sc.h_digests + 32 * i), st.shard_world) != st.shard_rank)
+      held.push_back(i);
+  if (held.empty()) return CASCADE_OK;
+  const size_t k = held.size();
+  Scratch &oc = st.oc;
+  int rc = ensure_scratch_of(st, oc, k);
+  if (!rc && st.claimed + k > st.nslots / 2) rc = grow_index(st);
+  if (rc) return rc;
+  for (size_t j = 0; j < k; ++j) {
+    const size_t i = held[j];
+    oc.h_keys[2 * j] = le64(st.sc.h_digests + 32 * i);
+    oc.h_keys[2 * j + 1] = le64(st.sc.h_digests + 32 * i + 8);
+    oc.h_seqs[j] = j + 1;
+    oc.h_off[j] = st.sc.h_off[i];
+    oc.h_sizes[j] = st.sc.h_sizes[i];
+    oc.h_flags[j] = (st.sc.h_flags[i] & 0xffffu) | kFlagHeld |
+                    ((uint32_t)st.shard_rank << 16);
+    std::memcpy(oc.h_hdr + 8 * j, st.sc.h_hdr + 8 * i, 8);
+  }
+  CB_CUDA(cudaMemcpyAsync(oc.keys, oc.h_keys, 16 * k, cudaMemcpyHostToDevice, s));
+  CB_CUDA(cudaMemcpyAsync(oc.seqs, oc.h_seqs, 8 * k, cudaMemcpyHostToDevice, s));
+  CB_CUDA(cudaMemcpyAsync(oc.off, oc.h_off, 8 * k, cudaMemcpyHostToDevice, s));
+  CB_CUDA(cudaMemcpyAsync(oc.sizes, oc.h_sizes, 8 * k, cudaMemcpyHostToDevice, s));
+  CB_CUDA(cudaMemcpyAsync(oc.flags, oc.h_flags, 4 * k, cudaMemcpyHostToDevice, s));
+  CB_CUDA(cudaMemcpyAsync(oc.hdr, oc.h_hdr, 8 * k, cudaMemcpyHostToDevice, s));
+  CB_CUDA(cudaMemsetAsync(oc.err, 0, sizeof(int), s));
+  const uint64_t epoch = st.next_epoch;
+  st.next_epoch += k;
+  rc = launch_index_claim(st.slots, st.nslots - 1, oc.keys, 2, oc.seqs, (int)k,
+                          oc.slot, oc.err, s);
+  if (!rc) rc = launch_index_resolve(st.slots, oc.slot, oc.seqs, (int)k,
+                                     oc.status, s);
+  if (!rc) rc = launch_index_commit(st.slots, oc.slot, oc.status, oc.off,
+                                    oc.sizes, oc.flags, oc.hdr, epoch, (int)k, s);
+  if (rc) return rc;
+  CB_CUDA(cudaMemcpyAsync(oc.h_err, oc.err, sizeof(int), cudaMemcpyDeviceToHost, s));
+  CB_CUDA(cudaStreamSynchronize(s));
+  if (*oc.h_err) {
+    set_error("device index is full: raise index_slots");
+    return CASCADE_ERR_FULL;
+  }
+  st.claimed += k;
   return CASCADE_OK;
 }
 
@@ -2200,6 +2402,7 @@ static int shard_end(Store &st, const uint8_t *d_back, size_t m, size_t n,
   const uint64_t claimed = st.claimed;
   tally_put(st, n);
   st.claimed = claimed;
+  if ((rc = shard_hold(st, n))) return rc;
   return finish_put(st, n, true, h_status, h_digests, n_stored);
 }
 
@@ -2244,7 +2447,7 @@ __global__ void shard_locate_kernel(int m, uint32_t rank,
 }  // namespace
 
 static int shard_attach(Store &st, int world, int rank,
-                        const uint8_t *h_handles) {
+                        const uint8_t *h_handles, const uint8_t *h_dram) {
   CB_CHECK(world >= 1 && world <= 256 && rank >= 0 && rank < world,
            CASCADE_ERR_INVALID, "bad world/rank");
   CB_CHECK(st.hbm && st.pool, CASCADE_ERR_UNSUPPORTED,
@@ -2270,6 +2473,39 @@ static int shard_attach(Store &st, int world, int rank,
   }
   st.peer_base = std::move(bases);
   st.peer_rank = rank;
+  st.peer_dram.clear();
+  st.peer_dram.resize(world);
+  for (int r = 0; h_dram && r < world; ++r) {
+    const uint8_t *rec = h_dram + (size_t)CASCADE_SHARD_DRAM_NAME_BYTES * r;
+    if (r == rank || rec[0] == 0) continue;
+    const std::string name(reinterpret_cast<const char *>(rec),
+                           strnlen(reinterpret_cast<const char *>(rec), 55));
+    uint64_t chunk = 0;
+    std::memcpy(&chunk, rec + 56, 8);
+    CB_CHECK(chunk > 0, CASCADE_ERR_INVALID, "bad DRAM tier record");
+    st.peer_dram[r].reset(new DramView(name, chunk));
+  }
+  return CASCADE_OK;
+}
+
+// This store's DRAM tier as a shared arena others can map: its name and
+// chunk size in a 64-byte record (all zero without a DRAM tier).  Shares
+// the arena on the first call, which must come before the tier holds data.
+static int shard_dram_name(Store &st, uint8_t *rec) {
+  std::memset(rec, 0, CASCADE_SHARD_DRAM_NAME_BYTES);
+  if (!st.dram_tier) return CASCADE_OK;
+  if (st.dram->shared_name().empty()) {
+    char name[56];
+    std::snprintf(name, sizeof(name), "/cascade_b200_%d_%llx", (int)getpid(),
+                  (unsigned long long)(uintptr_t)&st);
+    CB_CHECK(st.dram->share(name), CASCADE_ERR_INVALID,
+             "the DRAM tier already holds data; share it before the first put");
+  }
+  const std::string &nm = st.dram->shared_name();
+  CB_CHECK(nm.size() < 56, CASCADE_ERR_INVALID, "DRAM tier name too long");
+  std::memcpy(rec, nm.data(), nm.size());
+  const uint64_t chunk = st.dram->chunk_bytes();
+  std::memcpy(rec + 56, &chunk, 8);
   return CASCADE_OK;
 }
 
@@ -2351,7 +2587,7 @@ static int shard_get_end(Store &st, const uint8_t *d_back, size_t m, size_t n,
   const ShardLocation *loc = reinterpret_cast<const ShardLocation *>(st.h_stage);
   const int world = (int)st.peer_base.size();
   std::vector<uint8_t> seen(n, 0), deliver(n, 0);
-  std::vector<uint64_t> bases(n, 0);
+  std::vector<uint64_t> bases(n, 0), dram_src(n, 0);
   uint64_t found = 0;
   size_t named = 0;
   for (size_t j = 0; j < m; ++j) {
@@ -2373,13 +2609,22 @@ static int shard_get_end(Store &st, const uint8_t *d_back, size_t m, size_t n,
     if (!r.found) continue;
     CB_CHECK((int)r.holder < world, CASCADE_ERR_INVALID,
              "shard_get_end: holder rank out of range");
-    // A location carries no index slot of this rank, so a DRAM block could
-    // not be promoted (relocated) here; a sharded store keeps its blocks
-    // in HBM.
-    CB_CHECK((r.flags & kTierHbm) && !(r.flags & kTierDram),
-             CASCADE_ERR_UNSUPPORTED,
-             "sharded get: the block is in a DRAM tier, not in HBM");
-    bases[r.src_idx] = (uint64_t)(uintptr_t)st.peer_base[r.holder];
+    if (r.flags & kTierHbm) {
+      bases[r.src_idx] = (uint64_t)(uintptr_t)st.peer_base[r.holder];
+      continue;
+    }
+    // In the holder's DRAM tier: this rank's own arena, or the holder's
+    // shared arena mapped here.  (Not promoted: a location carries no index
+    // slot of this rank.)
+    const uint64_t pay = payload_bytes(r.size, (r.flags & kFlagQ8) != 0);
+    const uint8_t *p = nullptr;
+    if ((int)r.holder == st.peer_rank)
+      p = st.dram ? st.dram->ptr(r.offset) : nullptr;
+    else if (r.holder < st.peer_dram.size() && st.peer_dram[r.holder])
+      p = st.peer_dram[r.holder]->ptr(r.offset, pay);
+    CB_CHECK(p != nullptr, CASCADE_ERR_UNSUPPORTED,
+             "sharded get: the holder's DRAM tier is not mapped here");
+    dram_src[r.src_idx] = (uint64_t)(uintptr_t)p;
   }
   CB_CHECK(named == n, CASCADE_ERR_INVALID,
            "shard_get_end: the locations do not name each key once");
@@ -2393,7 +2638,8 @@ static int shard_get_end(Store &st, const uint8_t *d_back, size_t m, size_t n,
     deliver[i] = (!f.found || size <= h_caps[i]) ? 1 : 0;
   }
   if (n_found) *n_found = found;
-  return deliver_locked(st, n, h_out, deliver.data(), bases.data());
+  return deliver_locked(st, n, h_out, deliver.data(), bases.data(),
+                        dram_src.data());
 }
 
 }  // namespace cb
@@ -2691,10 +2937,28 @@ extern "C" int cascade_shard_pool_handle(cascade_store_t *s,
 }
 
 extern "C" int cascade_shard_attach_pools(cascade_store_t *s, int world,
-                                          int rank, const uint8_t *h_handles) {
+                                          int rank, const uint8_t *h_handles,
+                                          const uint8_t *h_dram_names) {
   STORE_ENTRY(s);
   CB_CHECK(h_handles, CASCADE_ERR_INVALID, "null argument");
-  return cb::shard_attach(st, world, rank, h_handles);
+  return cb::shard_attach(st, world, rank, h_handles, h_dram_names);
+}
+
+extern "C" int cascade_shard_dram_name(cascade_store_t *s, uint8_t *h_record) {
+  STORE_ENTRY(s);
+  CB_CHECK(h_record, CASCADE_ERR_INVALID, "null argument");
+  return cb::shard_dram_name(st, h_record);
+}
+
+extern "C" int cascade_shard_put_prepare(cascade_store_t *s, size_t n,
+                                         const uint64_t *h_sizes, int world,
+                                         int rank, uint64_t *n_moves) {
+  STORE_ENTRY(s);
+  CB_CHECK(n_moves && (n == 0 || h_sizes), CASCADE_ERR_INVALID,
+           "null argument");
+  CB_CHECK(world >= 1 && world <= 256 && rank >= 0 && rank < world,
+           CASCADE_ERR_INVALID, "bad world/rank");
+  return cb::shard_prepare(st, n, h_sizes, world, rank, n_moves);
 }
 
 extern "C" int cascade_shard_detach_pools(cascade_store_t *s) {

@@ -36,6 +36,13 @@ enum SlotFlags : uint32_t {
   kTierHbm = 1u << 2,     // payload in the HBM pool
   kTierDram = 1u << 3,    // payload in the pinned DRAM arena
   kFlagRemote = 1u << 4,  // payload held by another rank (bits 16..23)
+  // Sharded store: this rank holds the payload of a key another rank owns
+  // (the slot tracks the payload for demotion; the owner's slot answers
+  // lookups).
+  kFlagHeld = 1u << 5,
+  // Sharded exchange: the record moves an owner's entry (its holder demoted
+  // the payload) instead of claiming the key.
+  kFlagRelocate = 1u << 6,
 };
 
 // Sharded dedup exchange (one box, one rank per GPU).  A rank sends one
@@ -44,6 +51,8 @@ enum SlotFlags : uint32_t {
 // padded to a fixed number of entries per rank; an entry whose src_idx is
 // kUnused (all bytes 0xff) carries nothing.
 constexpr uint32_t kUnused = 0xffffffffu;
+// src_idx of a record that relocates an owner's entry (kFlagRelocate).
+constexpr uint32_t kMoveIdx = 0xfffffffeu;
 // Sequence number of a request that takes part in no claim.
 constexpr uint64_t kNoSeq = ~0ull;
 struct ShardRecord {
@@ -181,8 +190,9 @@ struct ScanRec {
   uint64_t epoch;
   uint32_t hdr_scale;
   uint32_t hdr_zp;
+  uint64_t k0, k1;  // the key (unmasked)
 };
-static_assert(sizeof(ScanRec) == 40, "scan record layout");
+static_assert(sizeof(ScanRec) == 56, "scan record layout");
 
 constexpr uint64_t kNoRequest = ~0ull;  // pool request: allocate nothing
 
@@ -242,7 +252,12 @@ int launch_index_lookup(Slot *slots, uint64_t mask, const uint64_t *keys,
 int launch_index_relocate(Slot *slots, const uint32_t *slot_idx,
                           const uint64_t *offsets, const uint32_t *flags,
                           const uint8_t *headers, int n, cudaStream_t s);
-// Demotion candidates (live HBM slots; class 1 = prefix blocks when
+// Applies the relocation records (src_idx == kMoveIdx) among `m` received
+// shard records to this rank's live entries of their keys.
+int launch_index_apply_moves(Slot *slots, uint64_t mask, const void *records,
+                             int m, uint32_t rank, cudaStream_t s);
+// Demotion candidates (live HBM slots whose payload this rank holds; class
+// 1 = prefix blocks when
 // `semantic`, else class 0), by epoch bucket over [0, span):
 // bytes / count[cls * kVictimBuckets + b] = HBM payload bytes and slots.
 int launch_victim_hist(const Slot *slots, uint64_t nslots, int semantic,

@@ -168,7 +168,9 @@ __global__ void relocate_kernel(Slot *slots, const uint32_t *__restrict__ idx,
 __device__ __forceinline__ bool victim_of(const Slot &sl, int semantic,
                                           uint64_t span, int &cls, int &bucket,
                                           uint64_t &pay) {
-  if (sl.state != kLive || !(sl.flags & kTierHbm)) return false;
+  if (sl.state != kLive || !(sl.flags & kTierHbm) ||
+      (sl.flags & kFlagRemote))
+    return false;
   cls = (semantic && (sl.flags & kFlagPrefix)) ? 1 : 0;
   const uint64_t e = sl.epoch < span ? sl.epoch : span - 1;
   bucket = (int)((e * (uint64_t)kVictimBuckets) / span);
@@ -214,7 +216,36 @@ __global__ void victim_collect_kernel(const Slot *__restrict__ slots,
     r.epoch = sl.epoch;
     r.hdr_scale = sl.hdr_scale;
     r.hdr_zp = sl.hdr_zp;
+    r.k0 = sl.k0 ^ kKeyMask0;
+    r.k1 = sl.k1 ^ kKeyMask1;
     out[k] = r;
+  }
+}
+
+// An owner's entry follows its payload to the holder's DRAM tier.
+__global__ void apply_moves_kernel(Slot *slots, uint64_t mask,
+                                   const ShardRecord *__restrict__ in, int m,
+                                   uint32_t rank) {
+  const int j = blockIdx.x * blockDim.x + threadIdx.x;
+  if (j >= m) return;
+  const ShardRecord r = in[j];
+  if (r.src_idx != kMoveIdx) return;
+  const uint64_t s0 = r.k0 ^ kKeyMask0, s1 = r.k1 ^ kKeyMask1;
+  const uint64_t h = slot_hash(s0, s1);
+  for (int p = 0; p < kMaxProbe; ++p) {
+    Slot *sl = slots + ((h + (uint64_t)p) & mask);
+    uint64_t a, b;
+    ld_key(sl, a, b);
+    if ((a | b) == 0) return;
+    if (a != s0 || b != s1) continue;
+    if (sl->state != kLive) return;
+    sl->offset = r.offset;
+    sl->flags = (r.flags & 0xffffu & ~(uint32_t)kFlagRelocate) |
+                ((r.holder & 0xffu) << 16) |
+                (r.holder != rank ? (uint32_t)kFlagRemote : 0u);
+    sl->hdr_scale = r.hdr_scale;
+    sl->hdr_zp = r.hdr_zp;
+    return;
   }
 }
 
@@ -374,6 +405,16 @@ int launch_index_relocate(Slot *slots, const uint32_t *slot_idx,
   if (n <= 0) return CASCADE_OK;
   relocate_kernel<<<blocks_for(n), 256, 0, s>>>(slots, slot_idx, offsets,
                                                 flags, headers, n);
+  count_launches(1);
+  CB_CUDA(cudaGetLastError());
+  return CASCADE_OK;
+}
+
+int launch_index_apply_moves(Slot *slots, uint64_t mask, const void *records,
+                             int m, uint32_t rank, cudaStream_t s) {
+  if (m <= 0) return CASCADE_OK;
+  apply_moves_kernel<<<blocks_for(m), 256, 0, s>>>(
+      slots, mask, static_cast<const ShardRecord *>(records), m, rank);
   count_launches(1);
   CB_CUDA(cudaGetLastError());
   return CASCADE_OK;

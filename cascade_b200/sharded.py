@@ -49,6 +49,7 @@ REPLY_BYTES = 8
 QUERY_BYTES = 32
 LOCATION_BYTES = 48
 IPC_HANDLE_BYTES = 64
+DRAM_NAME_BYTES = 64
 
 _vp = ctypes.c_void_p
 _sz = ctypes.c_size_t
@@ -62,7 +63,11 @@ _lib.register("cascade_shard_resolve", _int, [_vp, _vp, _sz, _vp, _vp])
 _lib.register("cascade_shard_put_end", _int,
               [_vp, _vp, _sz, _sz, _vp, _vp, ctypes.POINTER(_u64), _vp])
 _lib.register("cascade_shard_pool_handle", _int, [_vp, _vp])
-_lib.register("cascade_shard_attach_pools", _int, [_vp, _int, _int, _vp])
+_lib.register("cascade_shard_attach_pools", _int,
+              [_vp, _int, _int, _vp, _vp])
+_lib.register("cascade_shard_dram_name", _int, [_vp, _vp])
+_lib.register("cascade_shard_put_prepare", _int,
+              [_vp, _sz, _vp, _int, _int, ctypes.POINTER(_u64)])
 _lib.register("cascade_shard_detach_pools", _int, [_vp])
 _lib.register("cascade_shard_get_begin", _int, [_vp, _sz, _vp, _sz, _vp, _vp])
 _lib.register("cascade_shard_lookup", _int, [_vp, _vp, _sz, _vp, _vp])
@@ -109,69 +114,80 @@ class CudaShardOps:
         import torch
         return torch.cuda.current_stream(self.device).cuda_stream
 
-    def begin(self, blocks, is_prefix, world, rank, seq_base, cap):
-        """Records for `world` segments of `cap` entries (device tensor)."""
+    @staticmethod
+    def _describe(blocks):
+        """Device blocks -> (addresses, sizes, what to keep alive)."""
         import torch
         if isinstance(blocks, tuple):    # (device addresses, sizes)
             ptrs = np.ascontiguousarray(blocks[0], dtype=np.uint64)
             sizes = np.ascontiguousarray(blocks[1], dtype=np.uint64)
-            n = len(ptrs)
-            self._keep = None            # the caller keeps the blocks alive
-        elif isinstance(blocks, torch.Tensor) and blocks.dim() == 2:
+            return ptrs, sizes, None     # the caller keeps the blocks alive
+        if isinstance(blocks, torch.Tensor) and blocks.dim() == 2:
             rows = blocks.contiguous()   # one block per row
             n = rows.shape[0]
             stride = rows.stride(0) * rows.element_size()
             ptrs = (np.arange(n, dtype=np.uint64) * np.uint64(stride)
                     + np.uint64(rows.data_ptr()))
             sizes = np.full(n, rows.shape[1] * rows.element_size(), np.uint64)
-            self._keep = rows
-        else:
-            blocks = [_cuda_u8(b) for b in blocks]
-            n = len(blocks)
-            self._keep = blocks
-            ptrs = np.array([b.data_ptr() for b in blocks], dtype=np.uint64)
-            sizes = np.array([b.numel() for b in blocks], dtype=np.uint64)
+            return ptrs, sizes, rows
+        blocks = [_cuda_u8(b) for b in blocks]
+        ptrs = np.array([b.data_ptr() for b in blocks], dtype=np.uint64)
+        sizes = np.array([b.numel() for b in blocks], dtype=np.uint64)
+        return ptrs, sizes, blocks
+
+    @staticmethod
+    def _describe_host(blocks):
+        """Host blocks -> (addresses, sizes, what to keep alive)."""
+        if isinstance(blocks, np.ndarray) and blocks.ndim == 2:
+            n = blocks.shape[0]
+            ptrs = (np.arange(n, dtype=np.uint64) * np.uint64(blocks.strides[0])
+                    + np.uint64(blocks.ctypes.data))
+            return ptrs, np.full(n, blocks.shape[1], np.uint64), blocks
+        arrs = [np.ascontiguousarray(b, dtype=np.uint8).reshape(-1)
+                for b in blocks]
+        ptrs = np.array([a.ctypes.data for a in arrs], dtype=np.uint64)
+        sizes = np.array([a.size for a in arrs], dtype=np.uint64)
+        return ptrs, sizes, arrs
+
+    def prepare(self, blocks, host, world, rank):
+        """Room in this rank's pool for the batch (demoting to the DRAM
+        tier); returns the relocation records the next begin sends."""
+        _, sizes, _ = (self._describe_host if host else self._describe)(blocks)
+        n = len(sizes)
+        moves = _u64(0)
+        check(_lib.load().cascade_shard_put_prepare(
+            self.store._h, n, sizes.ctypes.data if n else None, world, rank,
+            ctypes.byref(moves)))
+        return int(moves.value)
+
+    def _begin(self, fn, desc, is_prefix, world, rank, seq_base, cap):
+        import torch
+        ptrs, sizes, keep = desc
+        n = len(ptrs)
         pf = (np.array([1 if p else 0 for p in is_prefix], dtype=np.uint8)
               if is_prefix is not None else None)
         send = torch.empty((world * cap, RECORD_BYTES), dtype=torch.uint8,
                            device=self.device)
-        check(_lib.load().cascade_shard_put_begin(
-            self.store._h, n, ptrs.ctypes.data if n else None,
-            sizes.ctypes.data if n else None,
-            pf.ctypes.data if pf is not None else None, world, rank, seq_base,
-            cap, send.data_ptr(), self._stream()))
+        self._keep = keep
+        check(fn(self.store._h, n, ptrs.ctypes.data if n else None,
+                 sizes.ctypes.data if n else None,
+                 pf.ctypes.data if pf is not None else None, world, rank,
+                 seq_base, cap, send.data_ptr(), self._stream()))
         self._n = n
         return send
+
+    def begin(self, blocks, is_prefix, world, rank, seq_base, cap):
+        """Records for `world` segments of `cap` entries (device tensor)."""
+        return self._begin(_lib.load().cascade_shard_put_begin,
+                           self._describe(blocks), is_prefix, world, rank,
+                           seq_base, cap)
 
     def begin_host(self, blocks, is_prefix, world, rank, seq_base, cap):
         """begin for host blocks: a list of uint8 numpy arrays, or one 2-D
         uint8 array (pinned rows are staged fastest)."""
-        import torch
-        if isinstance(blocks, np.ndarray) and blocks.ndim == 2:
-            rows = blocks
-            n = rows.shape[0]
-            ptrs = (np.arange(n, dtype=np.uint64) * np.uint64(rows.strides[0])
-                    + np.uint64(rows.ctypes.data))
-            sizes = np.full(n, rows.shape[1], np.uint64)
-            self._keep = rows
-        else:
-            arrs = [np.ascontiguousarray(b, dtype=np.uint8).reshape(-1)
-                    for b in blocks]
-            n = len(arrs)
-            ptrs = np.array([a.ctypes.data for a in arrs], dtype=np.uint64)
-            sizes = np.array([a.size for a in arrs], dtype=np.uint64)
-            self._keep = arrs
-        pf = (np.array([1 if p else 0 for p in is_prefix], dtype=np.uint8)
-              if is_prefix is not None else None)
-        send = torch.empty((world * cap, RECORD_BYTES), dtype=torch.uint8,
-                           device=self.device)
-        check(_lib.load().cascade_shard_put_begin_host(
-            self.store._h, n, ptrs.ctypes.data if n else None,
-            sizes.ctypes.data if n else None,
-            pf.ctypes.data if pf is not None else None, world, rank, seq_base,
-            cap, send.data_ptr(), self._stream()))
-        self._n = n
-        return send
+        return self._begin(_lib.load().cascade_shard_put_begin_host,
+                           self._describe_host(blocks), is_prefix, world,
+                           rank, seq_base, cap)
 
     def resolve(self, recv):
         import torch
@@ -208,9 +224,14 @@ class CudaShardOps:
         check(_lib.load().cascade_shard_pool_handle(self.store._h, buf))
         return bytes(buf)
 
-    def attach(self, world, rank, handles: bytes):
+    def dram_name(self) -> bytes:
+        buf = (ctypes.c_uint8 * DRAM_NAME_BYTES)()
+        check(_lib.load().cascade_shard_dram_name(self.store._h, buf))
+        return bytes(buf)
+
+    def attach(self, world, rank, handles: bytes, dram_names: bytes = None):
         check(_lib.load().cascade_shard_attach_pools(
-            self.store._h, world, rank, handles))
+            self.store._h, world, rank, handles, dram_names))
 
     def detach(self):
         check(_lib.load().cascade_shard_detach_pools(self.store._h))
@@ -283,17 +304,21 @@ class ShardedCascadeStore:
         self._attach()
 
     def _attach(self):
-        """Collective: every rank maps the other ranks' pools."""
+        """Collective: every rank maps the other ranks' pools and DRAM
+        tiers."""
         import torch
         import torch.distributed as dist
         if not hasattr(self.ops, "attach"):
             return
-        mine = torch.frombuffer(bytearray(self.ops.pool_handle()),
+        rec = self.ops.pool_handle() + self.ops.dram_name()
+        mine = torch.frombuffer(bytearray(rec),
                                 dtype=torch.uint8).to(self.ops.device)
         every = [torch.empty_like(mine) for _ in range(self.world)]
         dist.all_gather(every, mine, group=self.group)
-        handles = b"".join(bytes(t.cpu().numpy().tobytes()) for t in every)
-        self.ops.attach(self.world, self.rank, handles)
+        recs = [bytes(t.cpu().numpy().tobytes()) for t in every]
+        handles = b"".join(r[:IPC_HANDLE_BYTES] for r in recs)
+        names = b"".join(r[IPC_HANDLE_BYTES:] for r in recs)
+        self.ops.attach(self.world, self.rank, handles, names)
         self._attached = True
 
     def put_batch(self, blocks: Sequence, is_prefix=None,
@@ -305,27 +330,29 @@ class ShardedCascadeStore:
         the number of this rank's blocks stored or deduplicated (and, with
         ``return_status``, per-block status codes and 32-byte digests)."""
         n = len(blocks[0]) if isinstance(blocks, tuple) else len(blocks)
-        return self._put(self.ops.begin, blocks, n, is_prefix, return_status)
+        return self._put(False, blocks, n, is_prefix, return_status)
 
     def put_batch_host(self, blocks, is_prefix=None,
                        return_status: bool = False):
         """put_batch for blocks in host memory (a list of uint8 numpy arrays,
         or one 2-D uint8 array with a block per row).  Pinned rows of one
         size are copied to the GPU in stripes and hashed as they land."""
-        return self._put(self.ops.begin_host, blocks, len(blocks), is_prefix,
-                         return_status)
+        return self._put(True, blocks, len(blocks), is_prefix, return_status)
 
-    def _sizes(self, n):
-        """Collective: every rank's batch size (one small all-gather)."""
+    def _sizes(self, n, extra=0):
+        """Collective: every rank's (batch size, extra records), in one
+        small all-gather."""
         import torch
         import torch.distributed as dist
-        mine = torch.tensor([n], dtype=torch.int64, device=self.ops.device)
-        every = torch.zeros(self.world, dtype=torch.int64,
+        mine = torch.tensor([n, extra], dtype=torch.int64,
+                            device=self.ops.device)
+        every = torch.zeros(2 * self.world, dtype=torch.int64,
                             device=self.ops.device)
         dist.all_gather_into_tensor(every, mine, group=self.group)
-        return [int(x) for x in every.tolist()]
+        v = [int(x) for x in every.tolist()]
+        return list(zip(v[0::2], v[1::2]))
 
-    def _put(self, begin, blocks, n, is_prefix, return_status):
+    def _put(self, host, blocks, n, is_prefix, return_status):
         """The put exchange.  A rank whose own step fails still takes part
         in both all-to-alls (sending entries that carry nothing, or failed
         replies for the records it received) and raises afterwards, so its
@@ -335,19 +362,30 @@ class ShardedCascadeStore:
         import torch.distributed as dist
         with self._lock:
             dev = self.ops.device
-            counts = self._sizes(n)
-            seq_base = self._next_seq + sum(counts[:self.rank])
-            self._next_seq += sum(counts)
-            cap = max(counts)
-            if cap == 0:
-                empty = (0, np.zeros(0, np.uint8), np.zeros((0, 32), np.uint8))
-                return empty if return_status else 0
-            error = None
-            try:
-                send = begin(blocks, is_prefix, self.world, self.rank,
-                             seq_base, cap)
+            error, moves = None, 0
+            try:    # room in this rank's pool; relocation records to send
+                moves = self.ops.prepare(blocks, host, self.world, self.rank)
             except Exception as e:       # noqa: BLE001 (re-raised below)
                 error = e
+            sizes = self._sizes(n, moves)
+            counts = [c for c, _ in sizes]
+            seq_base = self._next_seq + sum(counts[:self.rank])
+            self._next_seq += sum(counts)
+            cap = max(c + m for c, m in sizes)
+            if cap == 0:
+                if error is not None:
+                    raise error
+                empty = (0, np.zeros(0, np.uint8), np.zeros((0, 32), np.uint8))
+                return empty if return_status else 0
+            send = None
+            if error is None:
+                try:
+                    begin = self.ops.begin_host if host else self.ops.begin
+                    send = begin(blocks, is_prefix, self.world, self.rank,
+                                 seq_base, cap)
+                except Exception as e:   # noqa: BLE001
+                    error = e
+            if send is None:
                 send = unused(self.world * cap, RECORD_BYTES, dev)
             recv = torch.empty_like(send)
             dist.all_to_all_single(recv, send, group=self.group)
@@ -387,7 +425,7 @@ class ShardedCascadeStore:
             raise ValueError("one output per id")
         with self._lock:
             dev = self.ops.device
-            cap = max(self._sizes(n_out))
+            cap = max(c for c, _ in self._sizes(n_out))
             if cap == 0:
                 return np.zeros(0, np.uint8), np.zeros(0, np.uint64)
             error = None

@@ -277,10 +277,23 @@ int cascade_store_get_batch(cascade_store_t *s, size_t n,
 /* caller's exchange must be ordered after `stream`).  end is           */
 /* synchronous.  A rank must not run other operations on the store      */
 /* between begin and end.  Blocks are content-addressed; HBM must hold  */
-/* the whole batch. */
+/* the whole batch (cascade_shard_put_prepare makes room with a DRAM    */
+/* tier). */
 #define CASCADE_SHARD_RECORD_BYTES 64
 #define CASCADE_SHARD_REPLY_BYTES 8
 
+/* Before a put with a DRAM tier: makes room in this rank's HBM pool for a
+ * batch of n blocks of h_sizes bytes by demoting its least recently used
+ * payloads to its DRAM tier (prefix blocks last; GPUBackend::evict_for_space,
+ * gpu_backend.cu:467-487, as called from CascadeStore::put,
+ * cascade_core.cpp:1100-1103), and sets *n_moves to the relocation records
+ * the next begin adds to d_send: one per demoted payload whose key another
+ * rank owns, so that the owner's entry follows it.  cap must then cover
+ * every rank's batch plus its moves.  Without a DRAM tier it does nothing
+ * (*n_moves = 0). */
+int cascade_shard_put_prepare(cascade_store_t *s, size_t n,
+                              const uint64_t *h_sizes, int world, int rank,
+                              uint64_t *n_moves);
 /* d_send: world * cap records (16-byte aligned). */
 int cascade_shard_put_begin(cascade_store_t *s, size_t n,
                             const uint64_t *h_ptrs, const uint64_t *h_sizes,
@@ -327,22 +340,30 @@ int cascade_shard_put_end(cascade_store_t *s, const uint8_t *d_back,
  * get_begin and lookup do not wait for the device; get_end is synchronous.
  * cascade_shard_attach_pools must have run on every rank first.  As for a
  * put, a rank must not run other operations on the store between get_begin
- * and get_end.  Blocks of a sharded store live in HBM (a sharded put needs
- * the whole batch to fit there); a block found in a DRAM tier is an error
- * (CASCADE_ERR_UNSUPPORTED). */
+ * and get_end.  A block its holder demoted is read from the holder's DRAM
+ * tier (a shared-memory arena every rank maps; the reference reads the
+ * holder's DRAM shadow, distributed_backend.cpp:720-767); sharded reads do
+ * not promote. */
 #define CASCADE_SHARD_QUERY_BYTES 32
 #define CASCADE_SHARD_LOCATION_BYTES 48
 #define CASCADE_IPC_HANDLE_BYTES 64
+#define CASCADE_SHARD_DRAM_NAME_BYTES 64
 
 /* This store's HBM pool as a CUDA IPC handle (64 bytes). */
 int cascade_shard_pool_handle(cascade_store_t *s, uint8_t *h_handle);
+/* This store's DRAM tier as a named shared-memory arena: a 64-byte record
+ * (name, and chunk size in bytes 56..63; all zero without a DRAM tier).
+ * The first call shares the arena, so it must come before the first put. */
+int cascade_shard_dram_name(cascade_store_t *s, uint8_t *h_record);
 /* Maps the pools of the other ranks: h_handles holds world handles, one per
- * rank in rank order (this rank's own is not opened).  Mappings are closed
- * by cascade_shard_detach_pools or when the store is destroyed.  A rank
- * must not free its store while another rank can still read its pool: have
- * every rank detach, then synchronise the ranks, then destroy. */
+ * rank in rank order (this rank's own is not opened), and h_dram_names
+ * (or NULL) the world records of cascade_shard_dram_name.  Mappings are
+ * closed by cascade_shard_detach_pools or when the store is destroyed.  A
+ * rank must not free its store while another rank can still read its pool:
+ * have every rank detach, then synchronise the ranks, then destroy. */
 int cascade_shard_attach_pools(cascade_store_t *s, int world, int rank,
-                               const uint8_t *h_handles);
+                               const uint8_t *h_handles,
+                               const uint8_t *h_dram_names);
 int cascade_shard_detach_pools(cascade_store_t *s);
 /* d_send: world * cap queries. */
 int cascade_shard_get_begin(cascade_store_t *s, size_t n,

@@ -142,7 +142,13 @@ class CpuShardOps:
         import torch.distributed as dist
         return bytes([dist.get_rank()]) * 64
 
-    def attach(self, world, rank, handles: bytes):
+    def prepare(self, blocks, host, world, rank):
+        return 0              # no DRAM tier: nothing to demote, no moves
+
+    def dram_name(self) -> bytes:
+        return bytes(64)
+
+    def attach(self, world, rank, handles: bytes, dram_names: bytes = None):
         assert handles == b"".join(bytes([r]) * 64 for r in range(world))
         self._world, self._rank = world, rank
 

@@ -151,3 +151,115 @@ def test_sharded_put_get_two_gpus(tmp_path, q8):
         hits = res[rank][5]      # the block that did not fit is no hit
         assert hits["gpu_hits"] == 2 * (len(ids) - 1) - 1
         assert hits["misses"] == 2
+
+
+def _demote_blocks(rank, rnd):
+    rng = np.random.default_rng(5000 + 10 * rnd + rank)
+    shared = np.random.default_rng(77).integers(0, 256, (16, 65536),
+                                                dtype=np.uint8)
+    own = rng.integers(0, 256, (12, 65536), dtype=np.uint8)
+    picks = [shared[int(p)] for p in rng.integers(0, 16, 4)]
+    return list(own) + picks
+
+
+def _demote_main(rank, world, port, out_dir, q8):
+    import datetime
+
+    import torch.distributed as dist
+
+    from cascade_b200 import cascade_cpp as cc
+    from cascade_b200.sharded import ShardedCascadeStore
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                            timeout=datetime.timedelta(seconds=60))
+    try:
+        cfg = cc.CascadeConfig()
+        cfg.gpu_device_id = rank
+        hbm = 32768 if q8 else 65536
+        cfg.gpu_capacity_bytes = 20 * hbm          # 20 blocks per GPU
+        cfg.shm_capacity_bytes = 64 << 20
+        cfg.dram_chunk_bytes = 4 << 20
+        cfg.kv_compression = True
+        cfg.gpu_q8 = q8
+        store = ShardedCascadeStore(cfg)
+        res = []
+        for rnd in range(4):
+            blocks = torch.from_numpy(np.stack(_demote_blocks(rank, rnd))).to(dev)
+            stored, status, _ = store.put_batch(blocks, return_status=True)
+            res.append({"stored": stored, "status": status.tolist()})
+        s = store.get_stats()
+        res.append({"gpu_used": s.gpu_used, "gpu_evictions": s.gpu_evictions,
+                    "shm_used": s.shm_used})
+        ids = []
+        for r in range(world):
+            for rnd in range(4):
+                for b in _demote_blocks(r, rnd):
+                    ids.append(hashlib.sha256(b.tobytes()).hexdigest()[:32])
+        outs = torch.zeros((len(ids), 65536), dtype=torch.uint8, device=dev)
+        found, sizes = store.get_batch(ids, outs)
+        res.append({"found": found.tolist(), "sizes": sizes.tolist(),
+                    "sha": [hashlib.sha256(o.cpu().numpy().tobytes())
+                            .hexdigest() for o in outs]})
+        store.close()
+        with open(os.path.join(out_dir, f"d{rank}.json"), "w") as f:
+            json.dump(res, f)
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < WORLD, reason="needs 2 GPUs")
+@pytest.mark.parametrize("q8", [False, True], ids=["raw-hbm", "int8-hbm"])
+def test_sharded_demotion_two_gpus(tmp_path, q8):
+    """Pools of 20 blocks per GPU take 4 rounds of 16 blocks per rank: each
+    rank demotes its least recently put payloads to its DRAM tier before a
+    round (cascade_shard_put_prepare), the owners' entries follow them, and
+    every rank then reads every block, from HBM or from the holder's DRAM
+    tier (its own, or the other rank's shared arena), as the oracle's
+    compress -> decompress of the stored bytes; the statuses still equal
+    serial puts in (round, rank, block) order."""
+    import torch.multiprocessing as mp
+
+    import oracle
+    mp.spawn(_demote_main, args=(WORLD, _free_port(), str(tmp_path), q8),
+             nprocs=WORLD, join=True)
+    res = [json.load(open(tmp_path / f"d{r}.json")) for r in range(WORLD)]
+    known = set()
+    for rnd in range(4):
+        for r in range(WORLD):
+            got = res[r][rnd]
+            assert got["stored"] == 16
+            for b, s in zip(_demote_blocks(r, rnd), got["status"]):
+                d = hashlib.sha256(b.tobytes()).digest()[:16]
+                assert (s != 0) == (d in known)
+                known.add(d)
+    assert sum(r[4]["gpu_evictions"] for r in res) > 0
+    hbm = 32768 if q8 else 65536
+    for r in res:
+        assert r[4]["gpu_used"] <= 20 * hbm
+    # INT8 in HBM, or demoted to the INT8 DRAM tier: the lossy form; a raw
+    # HBM block that stayed in HBM: its own bytes
+    want = {}
+    for r in range(WORLD):
+        for rnd in range(4):
+            for b in _demote_blocks(r, rnd):
+                k = hashlib.sha256(b.tobytes()).hexdigest()[:32]
+                want[k] = {hashlib.sha256(np.ascontiguousarray(
+                    oracle.kv_decompress(oracle.kv_compress(b), b.size))
+                    .tobytes()).hexdigest()}
+                if not q8:
+                    want[k].add(hashlib.sha256(b.tobytes()).hexdigest())
+    ids = [hashlib.sha256(b.tobytes()).hexdigest()[:32]
+           for r in range(WORLD) for rnd in range(4)
+           for b in _demote_blocks(r, rnd)]
+    for rank in range(WORLD):
+        got = res[rank][5]
+        assert got["found"] == [1] * len(ids)
+        assert got["sizes"] == [65536] * len(ids)
+        for i, k in enumerate(ids):
+            assert got["sha"][i] in want[k], (rank, i)
+    # both ranks read the same bytes for every block
+    assert res[0][5]["sha"] == res[1][5]["sha"]
