@@ -48,6 +48,9 @@ def parse():
                     help="layers per KV block (32 = 2 MiB; smaller for "
                          "profiling captures)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--headline-only", action="store_true",
+                    help="skip the 1 MiB round trip, the block-size sweep "
+                         "and the prefix-dedup mix (for profiling captures)")
     ap.add_argument("--workload", default="llama3-8b",
                     choices=["llama3-8b", "llama3-70b-zipf"],
                     help="llama3-8b: the headline line (it also carries the "
@@ -679,10 +682,11 @@ def main_ours(args):
     del host, host_np, rows
     torch.cuda.empty_cache()
     extra = {}
-    if world == 1:
+    if world == 1 and not args.headline_only:
         extra["cfg1"] = section_cfg1(ctx, args)
         extra["sweep"] = section_sweep(ctx, args, peak_gbps.value)
-    extra["dedup"] = section_dedup(ctx, args)
+    if not args.headline_only:
+        extra["dedup"] = section_dedup(ctx, args)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

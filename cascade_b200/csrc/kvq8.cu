@@ -672,13 +672,13 @@ cudaLaunchConfig_t fused_config(int csize, cudaStream_t s,
 template <int T, int U, int LA, bool HINT>
 int fused_active_clusters(int csize, int *active_out) {
   auto kernel = compress_fused_kernel<T, U, LA, HINT>;
-  constexpr int kMaxDev = 64, kMaxLog = 5;
-  static std::atomic<int> cache[kMaxDev][kMaxLog];
+  constexpr int kMaxDev = 64, kMaxCluster = 16;
+  static std::atomic<int> cache[kMaxDev][kMaxCluster + 1];
   int dev = 0;
   CB_CUDA(cudaGetDevice(&dev));
-  int lg = 0;
-  while ((1 << lg) < csize) ++lg;
-  int active = dev < kMaxDev && lg < kMaxLog ? cache[dev][lg].load() : 0;
+  CB_CHECK(csize >= 1 && csize <= kMaxCluster, CASCADE_ERR_INVALID,
+           "cluster size out of range");
+  int active = dev < kMaxDev ? cache[dev][csize].load() : 0;
   if (active <= 0) {
     if (csize > 8)
       CB_CUDA(cudaFuncSetAttribute(
@@ -689,7 +689,7 @@ int fused_active_clusters(int csize, int *active_out) {
     CB_CUDA(cudaOccupancyMaxActiveClusters(&active, kernel, &cfg));
     CB_CHECK(active > 0, CASCADE_ERR_UNSUPPORTED,
              "no cluster of this size fits on the device");
-    if (dev < kMaxDev && lg < kMaxLog) cache[dev][lg].store(active);
+    if (dev < kMaxDev) cache[dev][csize].store(active);
   }
   *active_out = active;
   return CASCADE_OK;

@@ -50,24 +50,26 @@ __device__ __forceinline__ Params params_from_minmax(int mn, int mx,
   return p;
 }
 
-// The code of one value, from d = v - min (0 <= d <= 65535, v from the
-// block the min was taken over), without integer/float conversion
-// instructions (a quarter-rate pipe on this GPU):
+// The code of one value, given md = bits(2^23) | d with d = v - min
+// (0 <= d <= 65535, v from the block the min was taken over), without
+// integer/float conversion instructions (a quarter-rate pipe on this GPU):
 //   x = 2^23 + d - 2^23           == (float)v - (float)min, exactly
 //   r = fma(x, inv, 0.5)          the reference's rounding, one FMA
-//   floor(r) = bits(RD(r + 2^23)) - bits(2^23), exact for 0 <= r < 2^23
-// and r = d * inv + 0.5 stays below 256 (d <= max - min, inv ~ 255 / range),
-// so the clamp to [0, 255] reduces to min(q, 255).  Returns the 32-bit
-// pattern of RD(r + 2^23) clamped, whose low byte is q (0..255).
-__device__ __forceinline__ uint32_t code_bits(uint32_t d, const Params &p) {
-  const float x = __fsub_rn(__uint_as_float(kMagicBits | d), kMagic);
+//   floor(r) = bits(RD(r + 2^23)) - bits(2^23), exact for 0 <= r < 2^23.
+// The reference's clamp to [0, 255] never binds: r >= 0.5, and for every
+// int16 range (checked for all 65 535) range * RN(1 / RN(range / 255)) + 0.5
+// rounds below 256, which bounds r for every d <= range.  Returns the bits
+// of RD(r + 2^23), whose low byte is q (0..255).
+__device__ __forceinline__ uint32_t code_of_magic(uint32_t md,
+                                                  const Params &p) {
+  const float x = __fsub_rn(__uint_as_float(md), kMagic);
   const float r = __fmaf_rn(x, p.inv, 0.5f);
-  return min(__float_as_uint(__fadd_rd(r, kMagic)), kMagicBits | 255u);
+  return __float_as_uint(__fadd_rd(r, kMagic));
 }
 
 __device__ __forceinline__ uint32_t code(int v, const Params &p) {
   const uint32_t d = ((uint32_t)v - p.mn_u) & 0xffffu;
-  return (code_bits(d, p) & 0xffu) ^ 0x80u;  // (q - 128) as a byte
+  return (code_of_magic(kMagicBits | d, p) & 0xffu) ^ 0x80u;  // q - 128
 }
 
 // Eight int16 values packed in a uint4 -> eight code bytes in a uint2.
@@ -77,8 +79,8 @@ __device__ __forceinline__ uint2 codes8(uint4 v, const Params &p) {
   uint32_t c[8];
 #pragma unroll
   for (int k = 0; k < 4; ++k) {
-    c[2 * k] = code_bits((w[k] - p.mn_u) & 0xffffu, p);
-    c[2 * k + 1] = code_bits((w[k] - mhi) >> 16, p);
+    c[2 * k] = code_of_magic(kMagicBits | ((w[k] - p.mn_u) & 0xffffu), p);
+    c[2 * k + 1] = code_of_magic(kMagicBits | ((w[k] - mhi) >> 16), p);
   }
   // Low bytes of c[0..3] and c[4..7], then q - 128 on all four bytes.
   uint2 r;

@@ -77,6 +77,26 @@ def test_decompress_fma_discriminating(kvq8_cases):
         assert np.array_equal(got[i], want)
 
 
+@pytest.mark.parametrize("scale", [0.003, 1.0, -3.7, 257.0, 8191.75, 8192.0,
+                                   8192.5, -8192.0, -9000.25, 20000.125,
+                                   1.0e5])
+def test_decompress_headers_either_side_of_the_fast_path(scale):
+    """Headers of any scale (including ones the compressor never writes:
+    negative, or large enough to wrap the 16-bit result) decode like the
+    oracle for every code, every zero point sign and values on both sides
+    of zero."""
+    codes = np.arange(256, dtype=np.uint8)
+    comps = []
+    for zp in (-128, -77, -1, 0, 1, 64, 127):
+        hdr = np.zeros(8, np.uint8)
+        hdr[:4] = np.frombuffer(np.float32(scale).tobytes(), np.uint8)
+        hdr[4] = np.uint8(zp & 0xff)
+        comps.append(np.concatenate([hdr, codes, codes[::-1]]))
+    got = _decompress(comps, [1024] * len(comps))
+    for c, g in zip(comps, got):
+        assert np.array_equal(g, oracle.kv_decompress(c, 1024))
+
+
 def test_llama_kv_blocks_roundtrip_vs_oracle():
     blocks = workloads.kv_blocks_np(6, 21)          # 6 x 2 MiB, outliers
     got = _compress(list(blocks))

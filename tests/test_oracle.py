@@ -78,3 +78,16 @@ def test_oracle_matches_compiled_reference_random():
         assert np.array_equal(oracle.kv_decompress(c, x.size),
                               oracle.ref_kv_decompress(c, x.size))
         assert oracle.block_id(x) == oracle.ref_block_id(x)
+
+
+def test_quantise_clamp_never_binds():
+    """The device quantiser drops the reference's clamp to [0, 255]
+    (cascade_core.cpp:842-846): for every int16 range, d = range (the
+    largest difference) gives fma(d, RN(1 / RN(range / 255)), 0.5) below
+    256, and the code grows with d, so no code exceeds 255."""
+    rng = np.arange(1, 65536, dtype=np.float64)
+    scale = (rng.astype(np.float32) / np.float32(255.0)).astype(np.float32)
+    inv = (np.float32(1.0) / scale).astype(np.float32)
+    r = (rng * inv.astype(np.float64) + 0.5).astype(np.float32)  # one rounding
+    assert float(r.max()) < 256.0
+    assert float(np.floor(r).max()) == 255.0
