@@ -750,7 +750,8 @@ def main_ours(args):
                     "bounds 2 MiB blocks",
             "chain_floor": chain_floor},
         "roofline_quantise": {
-            "kernel": "compress_fused_kernel (single pass: one HBM read, "
+            "kernel": "compress_fused_kernel (single pass: one HBM read; "
+                      "reducer and quantiser warps decoupled by mbarriers, "
                       "clusters of 8 exchanging min/max through DSMEM)",
             "bound": "hbm",
             "achieved": q_gbps, "peak": hbm, "unit": "GB/s",

@@ -211,18 +211,17 @@ __global__ void __launch_bounds__(kThreads, 8)
 // ------------------------------------------------ single-pass compression
 //
 // One HBM read of each block and one write of its codes.  A cluster of C
-// CTAs owns one block at a time and each CTA one C-th of it (its slice).
-// The clusters walk the batch persistently: block j + 1 of a cluster is
-// reduced (int16 min/max, HBM read, lines kept in L2) in the same loop
-// that quantises block j from the same slice, which the reduction read one
-// step earlier and which is still in L2, so the HBM reads, the L2 reads
-// and the code stores are in flight together.  Between the two the
-// cluster exchanges its per-CTA (min, max) pairs through distributed
-// shared memory, as remote stores that complete an mbarrier in the
-// receiving CTA (no cluster-wide barrier and no memory fence per block, so
-// a block's outstanding code stores never hold up the exchange).  The L2
-// holds two blocks per active cluster, which bounds the block sizes and
-// cluster sizes this form takes (the launcher checks it).
+// CTAs owns one block at a time and each CTA one C-th of it (its slice);
+// the clusters walk the batch persistently.  Within a CTA, reducer warps
+// read the slice of block j from HBM (lines kept in L2) and reduce its
+// int16 min/max, while quantiser warps code the slice of an earlier block
+// from L2 once that block's cluster-wide (min, max) has arrived.  The two
+// halves meet only at mbarriers, so HBM reads, L2 reads and code stores stay
+// in flight across block boundaries.  The per-CTA pairs cross the cluster
+// as st.async remote stores that complete an mbarrier in each receiving
+// CTA (no cluster barrier and no memory fence per block).  The L2 holds up
+// to S + 1 blocks per active cluster, which bounds the block and cluster
+// sizes the launcher takes.
 
 __device__ __forceinline__ uint32_t cluster_rank() {
   uint32_t r;
@@ -353,26 +352,20 @@ struct FusedArgs {
   int header_inline;
 };
 
-template <int T>
-struct FusedSmem {
-  uint64_t pmbar[2];   // the peers' pairs have landed, by block parity
-  int2 pairs[2][16];   // exchange arrays, by block parity; [rank]
-  int wmin[T / 32], wmax[T / 32];
-};
-
 // Thread-local int16 min/max of elements [e0, e1) of src (HBM read; the
 // lines are kept in L2 for the second read when HINT).  U loads per thread
 // are in flight at a time.
 template <int T, bool HINT, int U = 1>
 __device__ __forceinline__ void minmax_range(const uint8_t *src, uint64_t e0,
-                                             uint64_t e1, int &lo, int &hi) {
+                                             uint64_t e1, int &lo, int &hi,
+                                             uint32_t tid = threadIdx.x) {
   uint64_t tail = e0;
   if (((uintptr_t)src & 15u) == 0 && e1 > e0) {
     const uint4 *q = reinterpret_cast<const uint4 *>(src);
     uint32_t pmin = 0x7fff7fffu, pmax = 0x80008000u;
     const uint64_t pol = HINT ? l2_policy_keep() : 0;
     const uint64_t v1 = e1 >> 3;
-    uint64_t v = (e0 >> 3) + threadIdx.x;
+    uint64_t v = (e0 >> 3) + tid;
 #pragma unroll 1
     for (; v + (U - 1) * T < v1; v += U * T) {
       const uint4 *qv = q + v;
@@ -389,7 +382,7 @@ __device__ __forceinline__ void minmax_range(const uint8_t *src, uint64_t e0,
     hi = max(hi, max((int)(int16_t)(pmax & 0xffffu), (int)(int16_t)(pmax >> 16)));
     tail = v1 << 3;
   }
-  for (uint64_t e = tail + threadIdx.x; e < e1; e += T) {
+  for (uint64_t e = tail + tid; e < e1; e += T) {
     const int x = ld_i16_bytes(src + 2 * e);
     lo = min(lo, x);
     hi = max(hi, x);
@@ -402,14 +395,15 @@ template <int T, bool HINT, int U = 1>
 __device__ __forceinline__ void quantize_range(const uint8_t *src,
                                                uint8_t *codes, uint64_t e0,
                                                uint64_t e1,
-                                               const q8::Params &p) {
+                                               const q8::Params &p,
+                                               uint32_t tid = threadIdx.x) {
   uint64_t tail = e0;
   if (((uintptr_t)src & 15u) == 0 && ((uintptr_t)codes & 7u) == 0 && e1 > e0) {
     const uint4 *q = reinterpret_cast<const uint4 *>(src);
     uint2 *o = reinterpret_cast<uint2 *>(codes);
     const uint64_t pol = HINT ? l2_policy_drop() : 0;
     const uint64_t v1 = e1 >> 3;
-    uint64_t v = (e0 >> 3) + threadIdx.x;
+    uint64_t v = (e0 >> 3) + tid;
 #pragma unroll 1
     for (; v + (U - 1) * T < v1; v += U * T) {
       const uint4 *qv = q + v;
@@ -430,152 +424,162 @@ __device__ __forceinline__ void quantize_range(const uint8_t *src,
     }
     tail = v1 << 3;
   }
-  for (uint64_t e = tail + threadIdx.x; e < e1; e += T)
+  for (uint64_t e = tail + tid; e < e1; e += T)
     codes[e] = (uint8_t)q8::code(ld_i16_bytes(src + 2 * e), p);
 }
 
-template <int T>
-__device__ __forceinline__ int2 cta_reduce_pair(int lo, int hi,
-                                                FusedSmem<T> &sm) {
-  lo = __reduce_min_sync(0xffffffffu, lo);
-  hi = __reduce_max_sync(0xffffffffu, hi);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if (lane == 0) { sm.wmin[warp] = lo; sm.wmax[warp] = hi; }
-  __syncthreads();
-  lo = lane < T / 32 ? sm.wmin[lane] : INT_MAX;
-  hi = lane < T / 32 ? sm.wmax[lane] : INT_MIN;
-  lo = __reduce_min_sync(0xffffffffu, lo);
-  hi = __reduce_max_sync(0xffffffffu, hi);
-  __syncthreads();  // wmin/wmax are reused by the next reduction
-  return make_int2(lo, hi);
+// The single pass with the two halves of each CTA decoupled.  Reducer
+// warps (NR) read the CTA's slice of block j from HBM (lines kept in L2),
+// reduce it, and move on to block j + 1 as soon as the quantiser warps (NQ)
+// have finished block j + 1 - S; quantiser warps wait for block j's
+// cluster-wide (min, max), then code their slice from L2 (U loads in flight
+// per thread in both halves).  Neither half waits for the other's loads to
+// drain, so HBM reads, L2 reads and code stores stay in flight across
+// block boundaries.  Synchronisation, all bounded waits:
+//   part_bar[j % S]  (CTA) the reducer warps' partial pairs of block j;
+//                    reducer warp 0 then sends the CTA's pair to every CTA
+//                    of the cluster (st.async completing pmbar);
+//   pmbar[j % 2S]    (cluster) the csize pairs of block j have landed;
+//   free_bar[j % S]  (CTA) the quantiser warps are done with block j, so
+//                    the reducers may start block j + S.
+// A peer sends its pair of block k only after this CTA's quantisers have
+// finished block k - 2S (k - S gates the peer's reducers, whose quantisers
+// needed this CTA's pair of k - S, whose reducers waited for block k - 2S),
+// so 2S pair slots never overlap, and each slot is re-armed (by quantiser
+// thread 0, before its warp arrives on free_bar) before it is needed.  The
+// L2 holds up to S + 1 blocks per cluster.
+template <int NR, int NQ, int S>
+struct FusedSmem {
+  uint64_t pmbar[2 * S];
+  uint64_t part_bar[S];
+  uint64_t free_bar[S];
+  int2 pairs[2 * S][16];
+  int2 part[S][NR];
+};
+
+__device__ __forceinline__ void mbar_init_count(uint64_t *m, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;"
+               :: "r"(smem_addr(m)), "r"(count));
 }
 
-// One step of a cluster: quantise this CTA's slice of block bq (params p;
-// bq < 0: none) while reducing its slice of block br (br < 0: none), in one
-// loop when both are aligned, so the HBM reads of br, the L2 reads of bq
-// and the code stores are in flight together.  Returns the CTA's (min, max)
-// of br's slice.
-template <int T, int U, bool HINT>
-__device__ __forceinline__ int2 fused_step(const FusedArgs &a, int bq,
-                                           const q8::Params &p, int br,
-                                           uint32_t rank, uint32_t csize,
-                                           FusedSmem<T> &sm) {
-  int lo = INT_MAX, hi = INT_MIN;
-  uint64_t qe0 = 0, qe1 = 0, re0 = 0, re1 = 0;
-  const uint8_t *qs = nullptr, *rs = nullptr;
-  uint8_t *qc = nullptr;
-  if (bq >= 0) {
-    slice_of(a.sizes[bq] >> 1, rank, csize, &qe0, &qe1);
-    qs = reinterpret_cast<const uint8_t *>(a.ptrs[bq]);
-    uint8_t *dst = reinterpret_cast<uint8_t *>(a.dsts[bq]);
-    qc = a.header_inline ? dst + 8 : dst;
-  }
-  if (br >= 0) {
-    slice_of(a.sizes[br] >> 1, rank, csize, &re0, &re1);
-    rs = reinterpret_cast<const uint8_t *>(a.ptrs[br]);
-  }
-  if (bq >= 0 && br >= 0 && ((uintptr_t)qs & 15u) == 0 &&
-      ((uintptr_t)qc & 7u) == 0 && ((uintptr_t)rs & 15u) == 0) {
-    const uint4 *qq = reinterpret_cast<const uint4 *>(qs);
-    const uint4 *rq = reinterpret_cast<const uint4 *>(rs);
-    uint2 *o = reinterpret_cast<uint2 *>(qc);
-    const uint64_t qv1 = qe1 >> 3, rv1 = re1 >> 3;
-    uint64_t qv = (qe0 >> 3) + threadIdx.x, rv = (re0 >> 3) + threadIdx.x;
-    uint32_t pmin = 0x7fff7fffu, pmax = 0x80008000u;
-    const uint64_t keep = HINT ? l2_policy_keep() : 0;
-    const uint64_t drop = HINT ? l2_policy_drop() : 0;
-#pragma unroll 1
-    for (; qv + (U - 1) * T < qv1 && rv + (U - 1) * T < rv1;
-         qv += U * T, rv += U * T) {
-      uint4 x[U], y[U];
-#pragma unroll
-      for (int k = 0; k < U; ++k) {
-        x[k] = HINT ? ld_hint(rq + rv + k * T, keep) : ld_stream(rq + rv + k * T);
-        y[k] = HINT ? ld_hint(qq + qv + k * T, drop) : ld_stream(qq + qv + k * T);
-      }
-#pragma unroll
-      for (int k = 0; k < U; ++k) {
-        minmax16(x[k], pmin, pmax);
-        const uint2 c = q8::codes8(y[k], p);
-        if (HINT) st_hint(o + qv + k * T, c, drop); else o[qv + k * T] = c;
-      }
-    }
-    for (; rv < rv1; rv += T)
-      minmax16(HINT ? ld_hint(rq + rv, keep) : ld_stream(rq + rv), pmin, pmax);
-    for (; qv < qv1; qv += T) {
-      const uint2 c = q8::codes8(HINT ? ld_hint(qq + qv, drop) : ld_stream(qq + qv), p);
-      if (HINT) st_hint(o + qv, c, drop); else o[qv] = c;
-    }
-    lo = min((int)(int16_t)(pmin & 0xffffu), (int)(int16_t)(pmin >> 16));
-    hi = max((int)(int16_t)(pmax & 0xffffu), (int)(int16_t)(pmax >> 16));
-    minmax_range<T, false>(rs, re1 & ~7ull, re1, lo, hi);   // ragged ends
-    quantize_range<T, false>(qs, qc, qe1 & ~7ull, qe1, p);
-  } else {
-    if (br >= 0) minmax_range<T, HINT>(rs, re0, re1, lo, hi);
-    if (bq >= 0) quantize_range<T, HINT>(qs, qc, qe0, qe1, p);
-  }
-  return cta_reduce_pair<T>(lo, hi, sm);
+__device__ __forceinline__ void mbar_arrive(uint64_t *m) {
+  asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];"
+               :: "r"(smem_addr(m)) : "memory");
 }
 
-// Blocks cid, cid + ncl, ... of the batch, LA = 1 or 2 blocks of
-// look-ahead: in step j the CTA quantises block j and reduces block j + LA.
-// The pairs of block j travel as remote stores that complete the
-// receiver's pmbar[j & 1] (armed for C x 8 bytes before they can arrive),
-// as in compress_staged_kernel; with LA = 2 the pair of block j + 1 is sent
-// before step j, so its exchange completes under a whole step.
-template <int T, int U, int LA, bool HINT>
-__global__ void __launch_bounds__(T, 1) compress_fused_kernel(FusedArgs a) {
-  static_assert(LA == 1 || LA == 2, "look-ahead of one or two blocks");
-  __shared__ FusedSmem<T> sm;
+// Bounded wait for a CTA-local barrier phase (acquire at CTA scope).
+__device__ __forceinline__ void mbar_wait_cta(uint64_t *m, uint32_t ph) {
+  uint32_t done = 0;
+  for (uint32_t i = 0; i < kWaitLimit && !done; ++i) {
+    asm volatile(
+        "{\n .reg .pred p;\n"
+        " mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n"
+        " selp.u32 %0, 1, 0, p;\n}"
+        : "=r"(done) : "r"(smem_addr(m)), "r"(ph) : "memory");
+  }
+  if (!done && (threadIdx.x & 31) == 0) atomicAdd(&g_pair_wait_timeouts, 1u);
+}
+
+template <int NR, int NQ, int U, int S>
+__global__ void __launch_bounds__(32 * (NR + NQ), 1)
+    compress_fused_kernel(FusedArgs a) {
+  constexpr int TR = 32 * NR, TQ = 32 * NQ;
+  __shared__ FusedSmem<NR, NQ, S> sm;
   const uint32_t rank = cluster_rank(), csize = cluster_size();
   const int cid = (int)cluster_id(), ncl = (int)cluster_count();
   const int J = a.n > cid ? (a.n - cid + ncl - 1) / ncl : 0;
-  auto block = [&](int j) { return j < J ? cid + j * ncl : -1; };
+  const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
-    mbar_init(&sm.pmbar[0]);
-    mbar_init(&sm.pmbar[1]);
+    for (int k = 0; k < 2 * S; ++k) mbar_init(&sm.pmbar[k]);
+    for (int k = 0; k < S; ++k) {
+      mbar_init_count(&sm.part_bar[k], NR);
+      mbar_init_count(&sm.free_bar[k], NQ);
+    }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    if (J > 0) mbar_expect(&sm.pmbar[0], csize * 8);
-    if (J > 1) mbar_expect(&sm.pmbar[1], csize * 8);
+    for (int k = 0; k < 2 * S && k < J; ++k)
+      mbar_expect(&sm.pmbar[k], csize * 8);
   }
   __syncthreads();
   cluster_arrive();  // every CTA's barriers exist before any remote store
   cluster_wait();
-  if (J == 0) return;
-  auto send = [&](int j, int2 m) {
-    if (threadIdx.x < csize)
-      st_async_pair(&sm.pairs[j & 1][rank], &sm.pmbar[j & 1], threadIdx.x,
-                    m.x, m.y);
-  };
-  const q8::Params none{};
-  int2 held = fused_step<T, U, HINT>(a, -1, none, block(0), rank, csize, sm);
-  send(0, held);
-  if (LA == 2)
-    held = fused_step<T, U, HINT>(a, -1, none, block(1), rank, csize, sm);
-#pragma unroll 1
-  for (int j = 0; j < J; ++j) {
-    mbar_wait_cluster(&sm.pmbar[j & 1], (j >> 1) & 1);
-    int lo = INT_MAX, hi = INT_MIN;
-    for (uint32_t q = 0; q < csize; ++q) {
-      const int2 v = sm.pairs[j & 1][q];
-      lo = min(lo, v.x);
-      hi = max(hi, v.y);
+  if (warp < NR) {
+    // ------------------------------------------------------ reducers
+    const uint32_t tid = threadIdx.x;
+    for (int j = 0; j < J; ++j) {
+      if (j >= S) mbar_wait_cta(&sm.free_bar[j % S], ((j - S) / S) & 1);
+      const int b = cid + j * ncl;
+      uint64_t e0, e1;
+      slice_of(a.sizes[b] >> 1, rank, csize, &e0, &e1);
+      int lo = INT_MAX, hi = INT_MIN;
+      minmax_range<TR, true, U>(reinterpret_cast<const uint8_t *>(a.ptrs[b]),
+                                e0, e1, lo, hi, tid);
+      lo = __reduce_min_sync(0xffffffffu, lo);
+      hi = __reduce_max_sync(0xffffffffu, hi);
+      if (lane == 0) {
+        sm.part[j % S][warp] = make_int2(lo, hi);
+        mbar_arrive(&sm.part_bar[j % S]);
+      }
+      if (warp == 0) {  // the CTA's pair to every CTA of the cluster
+        mbar_wait_cta(&sm.part_bar[j % S], (j / S) & 1);
+        lo = INT_MAX;
+        hi = INT_MIN;
+        for (int w = 0; w < NR; ++w) {
+          const int2 v = sm.part[j % S][w];
+          lo = min(lo, v.x);
+          hi = max(hi, v.y);
+        }
+        const int k = j % (2 * S);
+        if (lane < csize)
+          st_async_pair(&sm.pairs[k][rank], &sm.pmbar[k], lane, lo, hi);
+      }
     }
-    if (threadIdx.x == 0 && j + 2 < J) mbar_expect(&sm.pmbar[j & 1], csize * 8);
-    __syncthreads();  // pairs read and the barrier re-armed before any send
-    const int b = block(j);
-    const q8::Params p = q8::params_from_minmax(lo, hi, (a.sizes[b] >> 1) == 0);
-    if (rank == 0 && threadIdx.x == 0) {
+  } else {
+    // ----------------------------------------------------- quantisers
+    const uint32_t tid = threadIdx.x - TR;
+    for (int j = 0; j < J; ++j) {
+      const int k = j % (2 * S);
+      mbar_wait_cluster(&sm.pmbar[k], (j / (2 * S)) & 1);
+      int lo = INT_MAX, hi = INT_MIN;
+      for (uint32_t q = 0; q < csize; ++q) {
+        const int2 v = sm.pairs[k][q];
+        lo = min(lo, v.x);
+        hi = max(hi, v.y);
+      }
+      const int b = cid + j * ncl;
+      uint64_t e0, e1;
+      const uint64_t nelem = a.sizes[b] >> 1;
+      slice_of(nelem, rank, csize, &e0, &e1);
+      const q8::Params p = q8::params_from_minmax(lo, hi, nelem == 0);
       uint8_t *dst = reinterpret_cast<uint8_t *>(a.dsts[b]);
-      write_header(a.header_inline ? dst : a.headers + 8 * (size_t)b, p);
+      if (rank == 0 && tid == 0)
+        write_header(a.header_inline ? dst : a.headers + 8 * (size_t)b, p);
+      quantize_range<TQ, true, U>(reinterpret_cast<const uint8_t *>(a.ptrs[b]),
+                                  a.header_inline ? dst + 8 : dst, e0, e1, p,
+                                  tid);
+      if (tid == 0 && j + 2 * S < J) mbar_expect(&sm.pmbar[k], csize * 8);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.free_bar[j % S]);
     }
-    if (LA == 2 && j + 1 < J) send(j + 1, held);
-    held = fused_step<T, U, HINT>(a, b, p, block(j + LA), rank, csize, sm);
-    if (LA == 1 && j + 1 < J) send(j + 1, held);
   }
   // No CTA leaves while a peer may still address its shared memory.
   cluster_arrive();
   cluster_wait();
+}
+
+// Launch configuration with csize CTAs per cluster.
+cudaLaunchConfig_t fused_config(int csize, int threads, cudaStream_t s,
+                                cudaLaunchAttribute *attr) {
+  cudaLaunchConfig_t cfg = {};
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = csize;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(threads);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = s;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cfg;
 }
 
 constexpr uint64_t kCopyTile = kThreads * kVec * 16;  // 32 KiB
@@ -649,42 +653,24 @@ int launch_quantize(const uint64_t *d_ptrs, const uint64_t *d_sizes, int n,
   return CASCADE_OK;
 }
 
-// Launch configuration of the single-pass kernel with csize CTAs per
-// cluster.
-template <int T, int U, int LA, bool HINT>
-cudaLaunchConfig_t fused_config(int csize, cudaStream_t s,
-                                cudaLaunchAttribute *attr) {
-  cudaLaunchConfig_t cfg = {};
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = csize;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.blockDim = dim3(T);
-  cfg.dynamicSmemBytes = 0;
-  cfg.stream = s;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return cfg;
-}
-
-// Clusters of csize CTAs the device keeps resident (cached per device and
-// cluster size).
-template <int T, int U, int LA, bool HINT>
+// Clusters of csize CTAs of the single-pass kernel that the device keeps
+// resident (cached per device and cluster size).
+template <int NR, int NQ, int U, int S>
 int fused_active_clusters(int csize, int *active_out) {
-  auto kernel = compress_fused_kernel<T, U, LA, HINT>;
+  auto kernel = compress_fused_kernel<NR, NQ, U, S>;
   constexpr int kMaxDev = 64, kMaxCluster = 16;
   static std::atomic<int> cache[kMaxDev][kMaxCluster + 1];
-  int dev = 0;
-  CB_CUDA(cudaGetDevice(&dev));
   CB_CHECK(csize >= 1 && csize <= kMaxCluster, CASCADE_ERR_INVALID,
            "cluster size out of range");
+  int dev = 0;
+  CB_CUDA(cudaGetDevice(&dev));
   int active = dev < kMaxDev ? cache[dev][csize].load() : 0;
   if (active <= 0) {
     if (csize > 8)
       CB_CUDA(cudaFuncSetAttribute(
           kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
     cudaLaunchAttribute attr[1];
-    cudaLaunchConfig_t cfg = fused_config<T, U, LA, HINT>(csize, nullptr, attr);
+    cudaLaunchConfig_t cfg = fused_config(csize, 32 * (NR + NQ), nullptr, attr);
     cfg.gridDim = dim3(csize * sm_count());
     CB_CUDA(cudaOccupancyMaxActiveClusters(&active, kernel, &cfg));
     CB_CHECK(active > 0, CASCADE_ERR_UNSUPPORTED,
@@ -695,53 +681,46 @@ int fused_active_clusters(int csize, int *active_out) {
   return CASCADE_OK;
 }
 
-template <int T, int U, int LA, bool HINT>
-int launch_fused_form(const FusedArgs &a, int csize, cudaStream_t s,
-                      int *active_out) {
-  int active = 0;
-  int rc = fused_active_clusters<T, U, LA, HINT>(csize, &active);
-  if (rc) return rc;
-  if (active_out) *active_out = active;
+template <int NR, int NQ, int U, int S>
+int launch_fused_form(const FusedArgs &a, int csize, int active,
+                      cudaStream_t s) {
   cudaLaunchAttribute attr[1];
-  cudaLaunchConfig_t cfg = fused_config<T, U, LA, HINT>(csize, s, attr);
+  cudaLaunchConfig_t cfg = fused_config(csize, 32 * (NR + NQ), s, attr);
   cfg.gridDim = dim3(std::min(active, a.n) * csize);
-  CB_CUDA(cudaLaunchKernelEx(&cfg, compress_fused_kernel<T, U, LA, HINT>, a));
+  CB_CUDA(cudaLaunchKernelEx(&cfg, compress_fused_kernel<NR, NQ, U, S>, a));
   count_launches(1);
   return CASCADE_OK;
 }
 
-// The single-pass form that the batch sizes call for.  The L2 holds two
-// blocks per active cluster (the one being quantised and the one being
-// reduced); the cluster is the smallest whose blocks in flight fit 72 MiB.
-// Measured on 4096 x 2 MiB and 1024 x 1 MiB: 8 and 4 CTAs per cluster, 3.03
-// and 0.37 ms against 3.50 and 0.43 ms for min/max + quantise.  Smaller
-// blocks gain nothing over the two kernels (and larger ones need clusters
-// of 16, which only 7 of fit on the device, and lose), so they get
-// CASCADE_ERR_UNSUPPORTED.
-constexpr uint64_t kFusedL2Budget = 72ull << 20;
-constexpr int kFusedThreads = 1024;
-constexpr int kFusedUnroll = 4;
-constexpr int kFusedLookahead = 1;
+// The single-pass form: 16 reducer and 16 quantiser warps per CTA, 8
+// 16-byte loads in flight per thread, two blocks between the halves, and
+// the smallest cluster (most SMs busy) whose blocks in flight, (S + 1) per
+// active cluster, fit 112 MiB of L2.  Measured on 512 KiB ... 4 MiB blocks
+// (4-8 GiB per batch) against every cluster size, 1-3 blocks in flight,
+// 2-8 loads and other warp splits: 0.88, 0.86, 0.82 and 0.77 of the HBM
+// copy peak at 512 KiB, 1, 2 and 4 MiB, with clusters of 2, 4, 8 and 16.
+// Outside 512 KiB ... 6 MiB the two kernels are used
+// (CASCADE_ERR_UNSUPPORTED here).
+constexpr uint64_t kFusedL2Budget = 112ull << 20;
+constexpr int kFusedReducers = 16, kFusedQuantisers = 16, kFusedUnroll = 8,
+              kFusedDepth = 2;
 
 int launch_compress_fused(const uint64_t *d_ptrs, const uint64_t *d_sizes,
                           int n, uint64_t max_size, const uint64_t *d_dsts,
                           uint8_t *d_headers, int header_inline,
                           cudaStream_t s) {
   if (n <= 0) return CASCADE_OK;
-  if (max_size < (1ull << 20) || max_size > (2ull << 20) + 4096)
+  if (max_size < (512ull << 10) || max_size > (6ull << 20))
     return CASCADE_ERR_UNSUPPORTED;
   FusedArgs a{d_ptrs, d_sizes, d_dsts, d_headers, n, header_inline};
-  auto launch = [&](int cs, int *active) {
-    return launch_fused_form<kFusedThreads, kFusedUnroll, kFusedLookahead,
-                             true>(a, cs, s, active);
-  };
-  for (int cs = 1; cs <= 8; cs *= 2) {
+  for (int cs = 1; cs <= 16; cs *= 2) {
     int active = 0;
-    int rc = fused_active_clusters<kFusedThreads, kFusedUnroll,
-                                   kFusedLookahead, true>(cs, &active);
+    int rc = fused_active_clusters<kFusedReducers, kFusedQuantisers,
+                                   kFusedUnroll, kFusedDepth>(cs, &active);
     if (rc) return rc;
-    if ((uint64_t)active * (kFusedLookahead + 1) * max_size <= kFusedL2Budget)
-      return launch(cs, nullptr);
+    if ((uint64_t)active * (kFusedDepth + 1) * max_size <= kFusedL2Budget)
+      return launch_fused_form<kFusedReducers, kFusedQuantisers, kFusedUnroll,
+                               kFusedDepth>(a, cs, active, s);
   }
   return CASCADE_ERR_UNSUPPORTED;
 }

@@ -127,17 +127,21 @@ def test_copy_batch_ragged():
 
 
 @pytest.mark.parametrize("misalign", [0, 2, 8])
-def test_single_pass_compress_mixed_batch_vs_oracle(misalign):
-    # Batches whose largest block is 1-2 MiB take the single-pass cluster
-    # kernel.  64 blocks (several per cluster, so the look-ahead and the
-    # pair exchange run in steady state) of ragged sizes: odd, tiny, empty
-    # and not a multiple of the 16-byte groups; misaligned sources take the
-    # kernel's direct path.
-    rng = np.random.default_rng(40 + misalign)
-    sizes = [2 << 20, (2 << 20) - 2, (1 << 20) + 6, 0, 1, 100,
-             (3 << 19) + 3, 1 << 20]
+@pytest.mark.parametrize("top", [2 << 20, 512 << 10, 5 << 20],
+                         ids=["2MiB", "512KiB", "5MiB"])
+def test_single_pass_compress_mixed_batch_vs_oracle(misalign, top):
+    # Batches whose largest block is 512 KiB - 6 MiB take the single-pass
+    # cluster kernel (clusters of 8, 2 and 16 CTAs here).  Enough blocks
+    # that every cluster runs several (so the blocks between the reducer and
+    # quantiser warps and the pair exchange reach steady state), of ragged
+    # sizes: odd, tiny, empty and not a multiple of the 16-byte groups;
+    # misaligned sources take the kernel's direct path.
+    rng = np.random.default_rng(40 + misalign + top)
+    sizes = [top, top - 2, top // 2 + 6, 0, 1, 100, (3 * top) // 4 + 3,
+             top // 2]
     xs = []
-    for i in range(64):
+    count = {2 << 20: 64, 512 << 10: 400, 5 << 20: 40}[top]
+    for i in range(count):
         n = sizes[i % len(sizes)]
         if i % 3 == 0:      # KV-like values with outliers
             x = (rng.standard_normal(n // 2 + 1) * 3).astype(np.float16)
