@@ -732,9 +732,9 @@ int launch_dequantize(const uint64_t *d_srcs, const uint8_t *d_headers,
   if (n <= 0) return CASCADE_OK;
   const int tiles =
       (int)std::max<uint64_t>(1, div_up(max_out_size / 2, kTileElems));
-  // 8 CTAs per SM (2048 threads at 32 registers): more loads in flight for
-  // this latency-bound stream (5.7 vs 5.5 TB/s at 4 per SM).
-  const int grid = grid_for((uint64_t)n * tiles, 1, 8);
+  // 4 CTAs per SM: 4096 x 2 MiB blocks decode in 2.13 ms (0.93 of the HBM
+  // copy peak on 1.5 S) against 2.30 ms with 8 per SM and 2.15 with 12.
+  const int grid = grid_for((uint64_t)n * tiles, 1, 4);
   dequantize_kernel<<<grid, kThreads, 0, s>>>(d_srcs, d_headers, header_inline,
                                               d_out_sizes, n, tiles, d_dsts);
   count_launches(1);
