@@ -2011,6 +2011,28 @@ __global__ void shard_apply_kernel(int m, int n,
     atomicExch(err, CASCADE_ERR_INVALID);
 }
 
+// Held-slot requests: entry i claims digest i's key when block i stored
+// here and another rank owns the key, else takes no part (kNoSeq).
+__global__ void shard_held_kernel(int n, int world, uint32_t rank,
+                                  const uint64_t *__restrict__ digests,
+                                  const uint8_t *__restrict__ status,
+                                  const uint32_t *__restrict__ flags,
+                                  uint64_t *__restrict__ keys,
+                                  uint64_t *__restrict__ seqs,
+                                  uint32_t *__restrict__ hflags,
+                                  uint32_t *__restrict__ count) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const uint64_t k0 = digests[4 * (size_t)i], k1 = digests[4 * (size_t)i + 1];
+  const bool held = status[i] == CASCADE_PUT_STORED && (flags[i] & kTierHbm) &&
+                    owner_of(k0, world) != (int)rank;
+  keys[2 * (size_t)i] = k0;
+  keys[2 * (size_t)i + 1] = k1;
+  seqs[i] = held ? (uint64_t)i + 1 : kNoSeq;
+  hflags[i] = (flags[i] & 0xffffu) | kFlagHeld | (rank << 16);
+  if (held) atomicAdd(count, 1u);
+}
+
 // Relocation records into their owners' segments, after the batch's own.
 __global__ void shard_moves_kernel(int k, int world, uint32_t cap,
                                    const ShardRecord *__restrict__ moves,
@@ -2301,62 +2323,33 @@ static int shard_resolve(Store &st, const uint8_t *d_recv, size_t m,
 
 // With a DRAM tier, the blocks this rank stored for keys that other ranks
 // own get a held slot in this rank's index (kFlagHeld), so that demotion
-// here sees every payload in this rank's pool, in put order.
-static int shard_hold(Store &st, size_t n) {
-  if (!st.dram_tier) return CASCADE_OK;
-  cudaStream_t s = st.s;
-  CB_CUDA(cudaMemcpyAsync(st.sc.h_digests, st.sc.digests, 32 * n,
-                          cudaMemcpyDeviceToHost, s));
-  CB_CUDA(cudaMemcpyAsync(st.sc.h_hdr, st.sc.hdr, 8 * n,
-                          cudaMemcpyDeviceToHost, s));
-  CB_CUDA(cudaStreamSynchronize(s));
-  std::vector<size_t> held;
-  for (size_t i = 0; i < n; ++i)
-    if (st.sc.h_status[i] == CASCADE_PUT_STORED &&
-        (st.sc.h_flags[i] & kTierHbm) &&
-        owner_of(le64(st.sc.h_digests + 32 * i), st.shard_world) != st.shard_rank)
-      held.push_back(i);
-  if (held.empty()) return CASCADE_OK;
-  const size_t k = held.size();
+// here sees every payload in this rank's pool, in put order.  Queued on the
+// main stream after the batch's statuses are final; *d_count receives how
+// many (read after the caller's synchronisation, with oc.err).
+static int shard_hold(Store &st, size_t n, uint32_t *d_count) {
   Scratch &oc = st.oc;
-  int rc = ensure_scratch_of(st, oc, k);
-  if (!rc && st.claimed + k > st.nslots / 2) rc = grow_index(st);
+  int rc = ensure_scratch_of(st, oc, n);
+  if (!rc && st.claimed + n > st.nslots / 2) rc = grow_index(st);
   if (rc) return rc;
-  for (size_t j = 0; j < k; ++j) {
-    const size_t i = held[j];
-    oc.h_keys[2 * j] = le64(st.sc.h_digests + 32 * i);
-    oc.h_keys[2 * j + 1] = le64(st.sc.h_digests + 32 * i + 8);
-    oc.h_seqs[j] = j + 1;
-    oc.h_off[j] = st.sc.h_off[i];
-    oc.h_sizes[j] = st.sc.h_sizes[i];
-    oc.h_flags[j] = (st.sc.h_flags[i] & 0xffffu) | kFlagHeld |
-                    ((uint32_t)st.shard_rank << 16);
-    std::memcpy(oc.h_hdr + 8 * j, st.sc.h_hdr + 8 * i, 8);
-  }
-  CB_CUDA(cudaMemcpyAsync(oc.keys, oc.h_keys, 16 * k, cudaMemcpyHostToDevice, s));
-  CB_CUDA(cudaMemcpyAsync(oc.seqs, oc.h_seqs, 8 * k, cudaMemcpyHostToDevice, s));
-  CB_CUDA(cudaMemcpyAsync(oc.off, oc.h_off, 8 * k, cudaMemcpyHostToDevice, s));
-  CB_CUDA(cudaMemcpyAsync(oc.sizes, oc.h_sizes, 8 * k, cudaMemcpyHostToDevice, s));
-  CB_CUDA(cudaMemcpyAsync(oc.flags, oc.h_flags, 4 * k, cudaMemcpyHostToDevice, s));
-  CB_CUDA(cudaMemcpyAsync(oc.hdr, oc.h_hdr, 8 * k, cudaMemcpyHostToDevice, s));
+  cudaStream_t s = st.s;
+  CB_CUDA(cudaMemsetAsync(d_count, 0, sizeof(uint32_t), s));
   CB_CUDA(cudaMemsetAsync(oc.err, 0, sizeof(int), s));
+  shard_held_kernel<<<nblocks(n), 256, 0, s>>>(
+      (int)n, st.shard_world, (uint32_t)st.shard_rank,
+      reinterpret_cast<const uint64_t *>(st.sc.digests), st.sc.status,
+      st.sc.flags, oc.keys, oc.seqs, oc.flags, d_count);
+  count_launches(1);
+  CB_CUDA(cudaGetLastError());
   const uint64_t epoch = st.next_epoch;
-  st.next_epoch += k;
-  rc = launch_index_claim(st.slots, st.nslots - 1, oc.keys, 2, oc.seqs, (int)k,
+  st.next_epoch += n;
+  rc = launch_index_claim(st.slots, st.nslots - 1, oc.keys, 2, oc.seqs, (int)n,
                           oc.slot, oc.err, s);
-  if (!rc) rc = launch_index_resolve(st.slots, oc.slot, oc.seqs, (int)k,
+  if (!rc) rc = launch_index_resolve(st.slots, oc.slot, oc.seqs, (int)n,
                                      oc.status, s);
-  if (!rc) rc = launch_index_commit(st.slots, oc.slot, oc.status, oc.off,
-                                    oc.sizes, oc.flags, oc.hdr, epoch, (int)k, s);
-  if (rc) return rc;
-  CB_CUDA(cudaMemcpyAsync(oc.h_err, oc.err, sizeof(int), cudaMemcpyDeviceToHost, s));
-  CB_CUDA(cudaStreamSynchronize(s));
-  if (*oc.h_err) {
-    set_error("device index is full: raise index_slots");
-    return CASCADE_ERR_FULL;
-  }
-  st.claimed += k;
-  return CASCADE_OK;
+  if (!rc) rc = launch_index_commit(st.slots, oc.slot, oc.status, st.sc.off,
+                                    st.sc.sizes, oc.flags, st.sc.hdr, epoch,
+                                    (int)n, s);
+  return rc;
 }
 
 static int shard_end(Store &st, const uint8_t *d_back, size_t m, size_t n,
@@ -2385,12 +2378,26 @@ static int shard_end(Store &st, const uint8_t *d_back, size_t m, size_t n,
   int rc = launch_pool_free_unstored(st.d_pool, st.sc.req, st.sc.off,
                                      st.sc.status, (int)n, s);
   if (rc) return rc;
+  uint32_t *d_held = reinterpret_cast<uint32_t *>(st.shard_aux) + 256;  // after the cursors
+  if (st.dram_tier && (rc = shard_hold(st, n, d_held))) return rc;
   CB_CUDA(cudaMemcpyAsync(st.sc.h_status, st.sc.status, n,
                           cudaMemcpyDeviceToHost, s));
   CB_CUDA(cudaMemcpyAsync(st.sc.h_err, st.sc.err, sizeof(int),
                           cudaMemcpyDeviceToHost, s));
+  uint32_t held = 0;
+  if (st.dram_tier) {
+    CB_CUDA(cudaMemcpyAsync(&held, d_held, sizeof(held),
+                            cudaMemcpyDeviceToHost, s));
+    CB_CUDA(cudaMemcpyAsync(st.oc.h_err, st.oc.err, sizeof(int),
+                            cudaMemcpyDeviceToHost, s));
+  }
   CB_CUDA(cudaStreamSynchronize(s));
   st.shard_open = 0;
+  if (st.dram_tier && *st.oc.h_err) {
+    set_error("device index is full: raise index_slots");
+    return CASCADE_ERR_FULL;
+  }
+  st.claimed += held;
   CB_CHECK(*st.sc.h_err == 0, CASCADE_ERR_INVALID,
            "shard_put_end: a reply names no block of this batch");
   size_t missing = 0;
@@ -2402,7 +2409,6 @@ static int shard_end(Store &st, const uint8_t *d_back, size_t m, size_t n,
   const uint64_t claimed = st.claimed;
   tally_put(st, n);
   st.claimed = claimed;
-  if ((rc = shard_hold(st, n))) return rc;
   return finish_put(st, n, true, h_status, h_digests, n_stored);
 }
 
