@@ -2170,93 +2170,53 @@ static int shard_send_moves(Store &st, int world, size_t cap,
 }
 
 // The batch's descriptors are uploaded (and, with digests_ready, its hash is
-// under way on the hash stream): store it speculatively and write the
-// records.  Does not wait for the device.
+// under way on the hash stream): store it speculatively.  The records are
+// written by shard_records once the caller knows the exchange's segment
+// size.  Does not wait for the device.
 static int shard_begin_staged(Store &st, size_t n, uint64_t max_size,
-                              bool digests_ready, const uint8_t *h_prefix,
-                              int world, int rank, uint64_t seq_base,
-                              size_t cap, uint8_t *d_send) {
-  int rc;
+                              bool digests_ready, const uint8_t *h_prefix) {
   CB_CHECK(can_speculate(st, n), CASCADE_ERR_NOMEM,
            "sharded put: the HBM pool cannot hold the whole batch");
-  if ((rc = ensure_device_buf(st.shard_aux, st.oc_aux_cap,
-                              2048 + st.shard_moves.size() * sizeof(ShardRecord),
-                              st.s)))
-    return rc;
-  uint32_t *cursor = reinterpret_cast<uint32_t *>(st.shard_aux);
-  if ((rc = speculate_local(st, n, h_prefix, max_size, digests_ready)))
-    return rc;
-  cudaStream_t s = st.s;
-  CB_CUDA(cudaStreamWaitEvent(s, st.ev2, 0));
-  CB_CUDA(cudaMemsetAsync(cursor, 0, 256 * sizeof(uint32_t), s));
-  CB_CUDA(cudaMemsetAsync(st.sc.err, 0, sizeof(int), s));
-  shard_records_kernel<<<nblocks(n), 256, 0, s>>>(
-      (int)n, world, (uint32_t)rank, seq_base, (uint32_t)cap,
-      reinterpret_cast<const uint64_t *>(st.sc.digests), st.sc.off,
-      st.sc.sizes, st.sc.flags, st.sc.hdr, cursor,
-      reinterpret_cast<ShardRecord *>(d_send), st.sc.err);
-  count_launches(1);
-  CB_CUDA(cudaGetLastError());
-  if ((rc = shard_send_moves(st, world, cap, cursor, d_send))) return rc;
-  CB_CUDA(cudaMemcpyAsync(st.sc.h_off, st.sc.off, n * 8,
-                          cudaMemcpyDeviceToHost, s));
-  CB_CUDA(cudaMemcpyAsync(st.sc.h_err, st.sc.err, sizeof(int),
-                          cudaMemcpyDeviceToHost, s));
-  st.shard_rank = rank;
-  st.shard_world = world;
+  int rc = speculate_local(st, n, h_prefix, max_size, digests_ready);
+  if (rc) return rc;
   st.shard_open = n;
   return CASCADE_OK;
 }
 
-static int shard_check(const Store &st, size_t n, int world, int rank,
-                       size_t cap) {
+static int shard_check(const Store &st, int world, int rank) {
   CB_CHECK(world >= 1 && world <= 256 && rank >= 0 && rank < world,
            CASCADE_ERR_INVALID, "bad world/rank");
-  CB_CHECK(cap >= n && cap <= (size_t)INT32_MAX / (size_t)world,
-           CASCADE_ERR_INVALID,
-           "cap must be at least the batch size (and world * cap < 2^31)");
   CB_CHECK(st.hbm, CASCADE_ERR_UNSUPPORTED,
            "sharded puts need the HBM tier (use_gpu)");
   return CASCADE_OK;
 }
 
-// Fills the padded send buffer with unused entries on the main stream.
-static int fill_unused(Store &st, uint8_t *d_send, size_t bytes) {
-  CB_CUDA(cudaMemsetAsync(d_send, 0xff, bytes, st.s));
-  return CASCADE_OK;
-}
-
 static int shard_begin(Store &st, size_t n, const uint64_t *h_ptrs,
                        const uint64_t *h_sizes, const uint8_t *h_prefix,
-                       int world, int rank, uint64_t seq_base, size_t cap,
-                       uint8_t *d_send) {
-  int rc = shard_check(st, n, world, rank, cap);
-  if (!rc) rc = fill_unused(st, d_send, (size_t)world * cap * sizeof(ShardRecord));
-  if (rc || n == 0) {
-    st.shard_rank = rank;
-    st.shard_open = 0;
-    return rc;
-  }
+                       int world, int rank) {
+  st.shard_open = 0;
+  int rc = shard_check(st, world, rank);
+  if (rc) return rc;
+  st.shard_rank = rank;
+  st.shard_world = world;
+  if (n == 0) return CASCADE_OK;
   uint64_t max_size = 0;
   if ((rc = upload_batch(st, n, h_ptrs, h_sizes, nullptr, &max_size)))
     return rc;
-  return shard_begin_staged(st, n, max_size, false, h_prefix, world, rank,
-                            seq_base, cap, d_send);
+  return shard_begin_staged(st, n, max_size, false, h_prefix);
 }
 
 // Host blocks: staged to the device first.  Uniform pinned batches are
 // hashed stripe by stripe while they cross PCIe, as put_batch_host does.
 static int shard_begin_host(Store &st, size_t n, const uint8_t *const *blocks,
                             const uint64_t *sizes, const uint8_t *h_prefix,
-                            int world, int rank, uint64_t seq_base,
-                            size_t cap, uint8_t *d_send) {
-  int rc = shard_check(st, n, world, rank, cap);
-  if (!rc) rc = fill_unused(st, d_send, (size_t)world * cap * sizeof(ShardRecord));
-  if (rc || n == 0) {
-    st.shard_rank = rank;
-    st.shard_open = 0;
-    return rc;
-  }
+                            int world, int rank) {
+  st.shard_open = 0;
+  int rc = shard_check(st, world, rank);
+  if (rc) return rc;
+  st.shard_rank = rank;
+  st.shard_world = world;
+  if (n == 0) return CASCADE_OK;
   uint64_t need = 0;
   for (size_t i = 0; i < n; ++i)
     need += payload_bytes(sizes[i], q8_eligible(st, sizes[i], false));
@@ -2266,15 +2226,52 @@ static int shard_begin_host(Store &st, size_t n, const uint8_t *const *blocks,
   uint64_t max_size = 0;
   if ((rc = stage_host_striped(st, n, blocks, sizes, &taken, &max_size)))
     return rc;
-  if (taken)
-    return shard_begin_staged(st, n, max_size, true, h_prefix, world, rank,
-                              seq_base, cap, d_send);
+  if (taken) return shard_begin_staged(st, n, max_size, true, h_prefix);
   std::vector<uint64_t> ptrs;
   if ((rc = stage_host_blocks(st, n, blocks, sizes, ptrs))) return rc;
   if ((rc = upload_batch(st, n, ptrs.data(), sizes, nullptr, &max_size)))
     return rc;
-  return shard_begin_staged(st, n, max_size, false, h_prefix, world, rank,
-                            seq_base, cap, d_send);
+  return shard_begin_staged(st, n, max_size, false, h_prefix);
+}
+
+// The open batch's records (and shard_prepare's relocation records) into
+// d_send, `world` segments of `cap` entries, once its digests are done.
+// Sequence numbers order the batch as serial puts in (rank, block) order:
+// rank in the high half, block + 1 in the low half (claims last one batch).
+// Does not wait for the device.
+static int shard_records(Store &st, size_t cap, uint8_t *d_send) {
+  const size_t n = st.shard_open;
+  const int world = st.shard_world, rank = st.shard_rank;
+  CB_CHECK(cap >= n + st.shard_moves.size() &&
+               cap <= (size_t)INT32_MAX / (size_t)world,
+           CASCADE_ERR_INVALID,
+           "cap must cover the batch and its relocation records "
+           "(and world * cap < 2^31)");
+  cudaStream_t s = st.s;
+  CB_CUDA(cudaMemsetAsync(d_send, 0xff,
+                          (size_t)world * cap * sizeof(ShardRecord), s));
+  if (n == 0) return CASCADE_OK;
+  int rc = ensure_device_buf(st.shard_aux, st.oc_aux_cap,
+                             2048 + st.shard_moves.size() * sizeof(ShardRecord),
+                             s);
+  if (rc) return rc;
+  uint32_t *cursor = reinterpret_cast<uint32_t *>(st.shard_aux);
+  CB_CUDA(cudaStreamWaitEvent(s, st.ev2, 0));
+  CB_CUDA(cudaMemsetAsync(cursor, 0, 256 * sizeof(uint32_t), s));
+  CB_CUDA(cudaMemsetAsync(st.sc.err, 0, sizeof(int), s));
+  shard_records_kernel<<<nblocks(n), 256, 0, s>>>(
+      (int)n, world, (uint32_t)rank, ((uint64_t)rank << 32) + 1,
+      (uint32_t)cap, reinterpret_cast<const uint64_t *>(st.sc.digests),
+      st.sc.off, st.sc.sizes, st.sc.flags, st.sc.hdr, cursor,
+      reinterpret_cast<ShardRecord *>(d_send), st.sc.err);
+  count_launches(1);
+  CB_CUDA(cudaGetLastError());
+  if ((rc = shard_send_moves(st, world, cap, cursor, d_send))) return rc;
+  CB_CUDA(cudaMemcpyAsync(st.sc.h_off, st.sc.off, n * 8,
+                          cudaMemcpyDeviceToHost, s));
+  CB_CUDA(cudaMemcpyAsync(st.sc.h_err, st.sc.err, sizeof(int),
+                          cudaMemcpyDeviceToHost, s));
+  return CASCADE_OK;
 }
 
 // As owner: decides the received records and writes one reply per record.
@@ -2871,34 +2868,37 @@ extern "C" int cascade_shard_put_begin(cascade_store_t *s, size_t n,
                                        const uint64_t *h_ptrs,
                                        const uint64_t *h_sizes,
                                        const uint8_t *h_prefix, int world,
-                                       int rank, uint64_t seq_base, size_t cap,
-                                       uint8_t *d_send, void *stream) {
+                                       int rank, void *stream) {
   STORE_ENTRY(s);
-  CB_CHECK(d_send && (n == 0 || (h_ptrs && h_sizes)), CASCADE_ERR_INVALID,
+  CB_CHECK(n == 0 || (h_ptrs && h_sizes), CASCADE_ERR_INVALID,
            "null argument");
-  CB_CHECK(n <= (size_t)INT32_MAX, CASCADE_ERR_INVALID, "batch too large");
-  CB_CHECK(((uintptr_t)d_send & 15u) == 0, CASCADE_ERR_INVALID,
-           "d_send must be 16-byte aligned");
+  CB_CHECK(n <= (size_t)UINT32_MAX - 1, CASCADE_ERR_INVALID,
+           "batch too large");
   if (int rc = join_caller(st, stream)) return rc;
-  int rc = cb::shard_begin(st, n, h_ptrs, h_sizes, h_prefix, world, rank,
-                           seq_base, cap, d_send);
-  if (rc) return rc;
-  return cb::join_back(st, stream);
+  return cb::shard_begin(st, n, h_ptrs, h_sizes, h_prefix, world, rank);
 }
 
 extern "C" int cascade_shard_put_begin_host(
     cascade_store_t *s, size_t n, const uint8_t *const *h_blocks,
     const uint64_t *h_sizes, const uint8_t *h_prefix, int world, int rank,
-    uint64_t seq_base, size_t cap, uint8_t *d_send, void *stream) {
+    void *stream) {
   STORE_ENTRY(s);
-  CB_CHECK(d_send && (n == 0 || (h_blocks && h_sizes)), CASCADE_ERR_INVALID,
+  CB_CHECK(n == 0 || (h_blocks && h_sizes), CASCADE_ERR_INVALID,
            "null argument");
-  CB_CHECK(n <= (size_t)INT32_MAX, CASCADE_ERR_INVALID, "batch too large");
+  CB_CHECK(n <= (size_t)UINT32_MAX - 1, CASCADE_ERR_INVALID,
+           "batch too large");
+  if (int rc = join_caller(st, stream)) return rc;
+  return cb::shard_begin_host(st, n, h_blocks, h_sizes, h_prefix, world, rank);
+}
+
+extern "C" int cascade_shard_put_records(cascade_store_t *s, size_t cap,
+                                         uint8_t *d_send, void *stream) {
+  STORE_ENTRY(s);
+  CB_CHECK(d_send, CASCADE_ERR_INVALID, "null argument");
   CB_CHECK(((uintptr_t)d_send & 15u) == 0, CASCADE_ERR_INVALID,
            "d_send must be 16-byte aligned");
   if (int rc = join_caller(st, stream)) return rc;
-  int rc = cb::shard_begin_host(st, n, h_blocks, h_sizes, h_prefix, world,
-                                rank, seq_base, cap, d_send);
+  int rc = cb::shard_records(st, cap, d_send);
   if (rc) return rc;
   return cb::join_back(st, stream);
 }

@@ -8,16 +8,18 @@ has exactly one owner rank (the top bits of SHA-256 digest byte 0) and a
 batch is exact at once:
 
 1. every rank hashes its blocks and stores them speculatively in its own
-   HBM pool (``cascade_shard_put_begin``), writing one 64-byte record per
-   block into its owner rank's segment of a padded send buffer (``world``
-   segments of ``cap`` entries, ``cap`` the largest batch of any rank, which
-   one all-gather of the batch sizes tells every rank);
+   HBM pool (``cascade_shard_put_begin``); while the hash runs, one small
+   all-gather of the batch sizes gives ``cap``, the largest batch of any
+   rank, and ``cascade_shard_put_records`` then writes one 64-byte record
+   per block into its owner rank's segment of a padded send buffer
+   (``world`` segments of ``cap`` entries);
 2. the records go to their owners in one all-to-all with equal splits
    (NCCL on GPUs), with no host round trip for counts;
 3. each owner resolves the records it received against its slice of the
    index (``cascade_shard_resolve``): a key already stored is a dedup hit,
-   and among new keys the smallest global sequence number stores, which is
-   what serial puts in (rank, block) order would do;
+   and among new keys the smallest sequence number ((rank, block) packed in
+   64 bits) stores, which is what serial puts in (rank, block) order would
+   do;
 4. the 8-byte replies return in a second all-to-all and each rank frees the
    slots of its duplicates (``cascade_shard_put_end``).
 
@@ -56,9 +58,10 @@ _sz = ctypes.c_size_t
 _u64 = ctypes.c_uint64
 _int = ctypes.c_int
 _lib.register("cascade_shard_put_begin", _int,
-              [_vp, _sz, _vp, _vp, _vp, _int, _int, _u64, _sz, _vp, _vp])
+              [_vp, _sz, _vp, _vp, _vp, _int, _int, _vp])
 _lib.register("cascade_shard_put_begin_host", _int,
-              [_vp, _sz, _vp, _vp, _vp, _int, _int, _u64, _sz, _vp, _vp])
+              [_vp, _sz, _vp, _vp, _vp, _int, _int, _vp])
+_lib.register("cascade_shard_put_records", _int, [_vp, _sz, _vp, _vp])
 _lib.register("cascade_shard_resolve", _int, [_vp, _vp, _sz, _vp, _vp])
 _lib.register("cascade_shard_put_end", _int,
               [_vp, _vp, _sz, _sz, _vp, _vp, ctypes.POINTER(_u64), _vp])
@@ -160,34 +163,40 @@ class CudaShardOps:
             ctypes.byref(moves)))
         return int(moves.value)
 
-    def _begin(self, fn, desc, is_prefix, world, rank, seq_base, cap):
-        import torch
+    def _begin(self, fn, desc, is_prefix, world, rank):
         ptrs, sizes, keep = desc
         n = len(ptrs)
         pf = (np.array([1 if p else 0 for p in is_prefix], dtype=np.uint8)
               if is_prefix is not None else None)
-        send = torch.empty((world * cap, RECORD_BYTES), dtype=torch.uint8,
-                           device=self.device)
         self._keep = keep
+        self._n = 0
         check(fn(self.store._h, n, ptrs.ctypes.data if n else None,
                  sizes.ctypes.data if n else None,
                  pf.ctypes.data if pf is not None else None, world, rank,
-                 seq_base, cap, send.data_ptr(), self._stream()))
+                 self._stream()))
         self._n = n
-        return send
+        self._world = world
 
-    def begin(self, blocks, is_prefix, world, rank, seq_base, cap):
-        """Records for `world` segments of `cap` entries (device tensor)."""
-        return self._begin(_lib.load().cascade_shard_put_begin,
-                           self._describe(blocks), is_prefix, world, rank,
-                           seq_base, cap)
+    def begin(self, blocks, is_prefix, world, rank):
+        """Hashes and stores the batch speculatively (returns at once)."""
+        self._begin(_lib.load().cascade_shard_put_begin,
+                    self._describe(blocks), is_prefix, world, rank)
 
-    def begin_host(self, blocks, is_prefix, world, rank, seq_base, cap):
+    def begin_host(self, blocks, is_prefix, world, rank):
         """begin for host blocks: a list of uint8 numpy arrays, or one 2-D
         uint8 array (pinned rows are staged fastest)."""
-        return self._begin(_lib.load().cascade_shard_put_begin_host,
-                           self._describe_host(blocks), is_prefix, world,
-                           rank, seq_base, cap)
+        self._begin(_lib.load().cascade_shard_put_begin_host,
+                    self._describe_host(blocks), is_prefix, world, rank)
+
+    def records(self, cap):
+        """The batch's records for `world` segments of `cap` entries (a
+        device tensor, ready on the current stream)."""
+        import torch
+        send = torch.empty((self._world * cap, RECORD_BYTES),
+                           dtype=torch.uint8, device=self.device)
+        check(_lib.load().cascade_shard_put_records(
+            self.store._h, cap, send.data_ptr(), self._stream()))
+        return send
 
     def resolve(self, recv):
         import torch
@@ -298,7 +307,6 @@ class ShardedCascadeStore:
             self.store = CascadeStore(config)
             ops = CudaShardOps(self.store)
         self.ops = ops
-        self._next_seq = 1
         self._lock = threading.Lock()
         self._attached = False
         self._attach()
@@ -365,12 +373,12 @@ class ShardedCascadeStore:
             error, moves = None, 0
             try:    # room in this rank's pool; relocation records to send
                 moves = self.ops.prepare(blocks, host, self.world, self.rank)
+                begin = self.ops.begin_host if host else self.ops.begin
+                begin(blocks, is_prefix, self.world, self.rank)
             except Exception as e:       # noqa: BLE001 (re-raised below)
                 error = e
+            # while the hash runs: every rank's batch and relocation count
             sizes = self._sizes(n, moves)
-            counts = [c for c, _ in sizes]
-            seq_base = self._next_seq + sum(counts[:self.rank])
-            self._next_seq += sum(counts)
             cap = max(c + m for c, m in sizes)
             if cap == 0:
                 if error is not None:
@@ -380,9 +388,7 @@ class ShardedCascadeStore:
             send = None
             if error is None:
                 try:
-                    begin = self.ops.begin_host if host else self.ops.begin
-                    send = begin(blocks, is_prefix, self.world, self.rank,
-                                 seq_base, cap)
+                    send = self.ops.records(cap)
                 except Exception as e:   # noqa: BLE001
                     error = e
             if send is None:
@@ -468,4 +474,3 @@ class ShardedCascadeStore:
         import torch.distributed as dist
         dist.barrier(group=self.group)
         self.ops.store.clear()
-        self._next_seq = 1

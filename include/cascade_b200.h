@@ -258,27 +258,30 @@ int cascade_store_get_batch(cascade_store_t *s, size_t n,
 /* The reference keeps one replicated dedup set per node, synchronised  */
 /* by MPI_Allgatherv (DistributedStore::put / sync_metadata,            */
 /* distributed_backend.cpp:583-590, 1269-1324).  Here each key has one   */
-/* owner rank (the top bits of digest byte 0) and a batch is three      */
-/* calls around two all-to-all exchanges the caller runs (NCCL):         */
-/*   begin:   hash, store every block speculatively in this rank's HBM   */
-/*            pool, and write one 64-byte record per block into the      */
-/*            owner rank's segment of d_send;                            */
-/*   resolve: as owner, decide each received record (the smallest global */
-/*            sequence number of a new key stores; later ones and keys   */
+/* owner rank (the top bits of digest byte 0) and a batch is four calls */
+/* around two all-to-all exchanges the caller runs (NCCL):               */
+/*   begin:   hash and store every block speculatively in this rank's   */
+/*            HBM pool;                                                  */
+/*   records: once the hash is done, one 64-byte record per block into  */
+/*            the owner rank's segment of d_send;                        */
+/*   resolve: as owner, decide each received record (the first put of a */
+/*            new key in (rank, block) order stores; later ones and keys */
 /*            already stored are dedup hits) and write 8-byte replies;   */
 /*   end:     take the replies for this rank's blocks (in any order),    */
 /*            free the slots of duplicates and report per-block status.  */
 /* The exchange buffers are padded: world segments of cap entries each  */
 /* (segment r goes to / comes from rank r), cap the same on every rank   */
-/* and at least every rank's batch size, so both all-to-alls have equal */
-/* splits and no rank needs the others' counts.  Entries that carry     */
-/* nothing are all 0xff bytes.  begin and resolve do not wait for the   */
-/* device: their outputs are ready on `stream` when they return (the     */
-/* caller's exchange must be ordered after `stream`).  end is           */
-/* synchronous.  A rank must not run other operations on the store      */
-/* between begin and end.  Blocks are content-addressed; HBM must hold  */
-/* the whole batch (cascade_shard_put_prepare makes room with a DRAM    */
-/* tier). */
+/* and at least every rank's batch size plus its relocation records     */
+/* (cascade_shard_put_prepare), so both all-to-alls have equal splits   */
+/* and no rank needs the others' counts; a caller learns cap (one small */
+/* all-gather) while the hash runs, between begin and records.  Entries */
+/* that carry nothing are all 0xff bytes.  begin, records and resolve   */
+/* do not wait for the device: their outputs are ready on `stream` when */
+/* they return (the caller's exchange must be ordered after `stream`).  */
+/* end is synchronous.  A rank must not run other operations on the     */
+/* store between begin and end.  Blocks are content-addressed; HBM must */
+/* hold the whole batch (cascade_shard_put_prepare makes room with a    */
+/* DRAM tier). */
 #define CASCADE_SHARD_RECORD_BYTES 64
 #define CASCADE_SHARD_REPLY_BYTES 8
 
@@ -287,18 +290,15 @@ int cascade_store_get_batch(cascade_store_t *s, size_t n,
  * payloads to its DRAM tier (prefix blocks last; GPUBackend::evict_for_space,
  * gpu_backend.cu:467-487, as called from CascadeStore::put,
  * cascade_core.cpp:1100-1103), and sets *n_moves to the relocation records
- * the next begin adds to d_send: one per demoted payload whose key another
- * rank owns, so that the owner's entry follows it.  cap must then cover
- * every rank's batch plus its moves.  Without a DRAM tier it does nothing
- * (*n_moves = 0). */
+ * the next records call adds to d_send: one per demoted payload whose key
+ * another rank owns, so that the owner's entry follows it.  Without a DRAM
+ * tier it does nothing (*n_moves = 0). */
 int cascade_shard_put_prepare(cascade_store_t *s, size_t n,
                               const uint64_t *h_sizes, int world, int rank,
                               uint64_t *n_moves);
-/* d_send: world * cap records (16-byte aligned). */
 int cascade_shard_put_begin(cascade_store_t *s, size_t n,
                             const uint64_t *h_ptrs, const uint64_t *h_sizes,
                             const uint8_t *h_prefix, int world, int rank,
-                            uint64_t seq_base, size_t cap, uint8_t *d_send,
                             void *stream);
 /* begin for blocks in host memory (the sharded form of
  * cascade_store_put_batch_host): the blocks are copied to this rank's GPU
@@ -308,8 +308,10 @@ int cascade_shard_put_begin_host(cascade_store_t *s, size_t n,
                                  const uint8_t *const *h_blocks,
                                  const uint64_t *h_sizes,
                                  const uint8_t *h_prefix, int world, int rank,
-                                 uint64_t seq_base, size_t cap,
-                                 uint8_t *d_send, void *stream);
+                                 void *stream);
+/* d_send: world * cap records (16-byte aligned). */
+int cascade_shard_put_records(cascade_store_t *s, size_t cap, uint8_t *d_send,
+                              void *stream);
 /* m = world * cap received records; d_reply: m replies. */
 int cascade_shard_resolve(cascade_store_t *s, const uint8_t *d_recv,
                           size_t m, uint8_t *d_reply, void *stream);

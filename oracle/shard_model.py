@@ -64,8 +64,7 @@ class CpuShardOps:
         self.shared_dir = shared_dir
         self.store = None
 
-    def begin(self, blocks, is_prefix, world, rank, seq_base, cap):
-        import torch
+    def begin(self, blocks, is_prefix, world, rank):
         n = len(blocks)
         digests = [hashlib.sha256(np.ascontiguousarray(b).tobytes()).digest()
                    for b in blocks]
@@ -74,7 +73,7 @@ class CpuShardOps:
         for i, d in enumerate(digests):
             recs[i]["k0"] = int.from_bytes(d[:8], "little")
             recs[i]["k1"] = int.from_bytes(d[8:16], "little")
-            recs[i]["seq"] = seq_base + i
+            recs[i]["seq"] = (rank << 32) + i + 1
             recs[i]["offset"] = i
             recs[i]["size"] = len(blocks[i])
             recs[i]["holder"] = rank
@@ -82,10 +81,15 @@ class CpuShardOps:
             owners[i] = owner_of(d, world)
         self._digests = digests
         self._blocks = [np.ascontiguousarray(b) for b in blocks]
-        return torch.from_numpy(_padded(recs, owners, world, cap))
+        self._recs, self._owners, self._world = recs, owners, world
 
-    def begin_host(self, blocks, is_prefix, world, rank, seq_base, cap):
-        return self.begin(blocks, is_prefix, world, rank, seq_base, cap)
+    def begin_host(self, blocks, is_prefix, world, rank):
+        return self.begin(blocks, is_prefix, world, rank)
+
+    def records(self, cap):
+        import torch
+        return torch.from_numpy(_padded(self._recs, self._owners,
+                                        self._world, cap))
 
     def resolve(self, recv):
         import torch

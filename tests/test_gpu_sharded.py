@@ -263,3 +263,72 @@ def test_sharded_demotion_two_gpus(tmp_path, q8):
             assert got["sha"][i] in want[k], (rank, i)
     # both ranks read the same bytes for every block
     assert res[0][5]["sha"] == res[1][5]["sha"]
+
+
+def _single_main(rank, world, port, out_dir):
+    import datetime
+
+    import torch.distributed as dist
+
+    from cascade_b200 import cascade_cpp as cc
+    from cascade_b200.sharded import ShardedCascadeStore
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(0)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                            timeout=datetime.timedelta(seconds=60))
+    try:
+        cfg = cc.CascadeConfig()
+        cfg.gpu_capacity_bytes = 20 * 32768        # 20 INT8 blocks
+        cfg.shm_capacity_bytes = 64 << 20
+        cfg.dram_chunk_bytes = 4 << 20
+        cfg.kv_compression = True
+        cfg.gpu_q8 = True
+        store = ShardedCascadeStore(cfg)
+        res = []
+        for rnd in range(4):
+            blocks = torch.from_numpy(np.stack(_demote_blocks(0, rnd))).to(dev)
+            stored, status, _ = store.put_batch(blocks, return_status=True)
+            res.append({"stored": stored, "status": status.tolist()})
+        s = store.get_stats()
+        res.append({"gpu_used": s.gpu_used, "gpu_evictions": s.gpu_evictions})
+        ids = [hashlib.sha256(b.tobytes()).hexdigest()[:32]
+               for rnd in range(4) for b in _demote_blocks(0, rnd)]
+        outs = torch.zeros((len(ids), 65536), dtype=torch.uint8, device=dev)
+        found, sizes = store.get_batch(ids, outs)
+        res.append({"found": found.tolist(), "sizes": sizes.tolist(),
+                    "sha": [hashlib.sha256(o.cpu().numpy().tobytes())
+                            .hexdigest() for o in outs]})
+        store.close()
+        with open(os.path.join(out_dir, "s0.json"), "w") as f:
+            json.dump(res, f)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_sharded_protocol_one_rank_with_demotion(tmp_path):
+    """The whole sharded C path (prepare, begin, records, resolve, end,
+    lookup, reads from HBM and from the DRAM tier) on one GPU as a world of
+    one rank: a 20-block pool takes 4 rounds of 16 blocks, demoting before
+    each, and every block reads back as the oracle's compress ->
+    decompress; statuses equal serial puts."""
+    import torch.multiprocessing as mp
+
+    import oracle
+    mp.spawn(_single_main, args=(1, _free_port(), str(tmp_path)), nprocs=1,
+             join=True)
+    res = json.load(open(tmp_path / "s0.json"))
+    known = set()
+    for rnd in range(4):
+        assert res[rnd]["stored"] == 16
+        for b, s in zip(_demote_blocks(0, rnd), res[rnd]["status"]):
+            d = hashlib.sha256(b.tobytes()).digest()[:16]
+            assert (s != 0) == (d in known)
+            known.add(d)
+    assert res[4]["gpu_evictions"] > 0 and res[4]["gpu_used"] <= 20 * 32768
+    blocks = [b for rnd in range(4) for b in _demote_blocks(0, rnd)]
+    assert res[5]["found"] == [1] * len(blocks)
+    for i, b in enumerate(blocks):
+        want = oracle.kv_decompress(oracle.kv_compress(b), b.size)
+        assert res[5]["sha"][i] == hashlib.sha256(want.tobytes()).hexdigest(), i

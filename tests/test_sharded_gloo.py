@@ -196,6 +196,12 @@ def _failing_ops(fail_step, fail_batch, out_dir):
                 raise RuntimeError("injected begin failure")
             return super().begin(*a)
 
+        def records(self, cap):
+            if fail_step == "records" and self.batch == fail_batch:
+                self.batch += 1
+                raise RuntimeError("injected records failure")
+            return super().records(cap)
+
         def resolve(self, recv):
             if fail_step == "resolve" and self.batch == fail_batch:
                 self.batch += 1          # end() does not run for this batch
@@ -238,7 +244,7 @@ def _failure_main(rank, world, port, out_dir, fail_step):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("fail_step", ["begin", "resolve"])
+@pytest.mark.parametrize("fail_step", ["begin", "records", "resolve"])
 def test_sharded_put_survives_a_failing_rank(tmp_path, fail_step):
     """Rank 1 fails in its first batch: it raises after both exchanges, the
     other ranks finish that batch (their blocks that rank 1 owns come back
