@@ -727,7 +727,7 @@ def main_ours(args):
     chain_floor = {"gbps": floor_gbps, "frac": sha_gbps / floor_gbps,
                    "sm_mhz": mhz,
                    "basis": "each chain's consumer warp alone on a scheduler: "
-                            "64 rounds x (11 ALU + 5 IMAD) x 2 issue cycles "
+                            "64 rounds x 11 ALU (the leanest round: 11 ALU + 5 IMAD) x 2 issue cycles "
                             "= 1408 cycles per 64-byte chunk"}
     q_bytes = total * 1.5 + 8 * n          # read S, write S/2 + header
     q_gbps = q_bytes / (q_ms * 1e-3) / 1e9

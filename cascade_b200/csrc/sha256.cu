@@ -305,8 +305,10 @@ __global__ void __launch_bounds__(64 * kGroups)
         for (int u = 0; u < 4; ++u) {
           if (kRound == 0)
             sha::round_kw(a, b, cc, d, e, f, g, h, kv[u], one, neg_one);
-          else
+          else if (kRound == 1)
             sha::round_kw3(a, b, cc, d, e, f, g, h, kv[u], one, neg_one);
+          else
+            sha::round_kw9(a, b, cc, d, e, f, g, h, kv[u], one, neg_one);
         }
       }
     }
@@ -422,13 +424,13 @@ int launch_sha256_range(const uint64_t *d_ptrs, const uint64_t *d_sizes,
                         int n, uint8_t *d_digests, uint32_t *d_state,
                         uint64_t c_begin, uint64_t c_end, cudaStream_t s) {
   // Up to two producer/consumer pairs per SM, each warp has a scheduler to
-  // itself: the latency-tuned round (both recurrences three operations
-  // deep), all 64 rounds unrolled, and 8 chunks of loads in flight per lane
-  // (8192 chains: 610 GB/s against 523 for the other form).  Beyond that,
-  // warps share schedulers, the ALU pipe is the limit and the round with the
-  // fewest ALU instructions wins (12288 chains: 526 against 490).
+  // itself: the latency-tuned round (one IMAD on the e-recurrence), all 64
+  // rounds unrolled, and 8 chunks of loads in flight per lane (8192 chains:
+  // 610 GB/s against 523 for the other form).  Beyond that, warps share
+  // schedulers, the ALU pipe is the limit and the round with the fewest ALU
+  // instructions wins (12288 chains: 526 against 490).
   if (n <= 2 * 32 * sm_count())
-    return launch_sha256_pipelined<1, 4, 1, 64, 8>(
+    return launch_sha256_pipelined<1, 4, 2, 64, 8>(
         d_ptrs, d_sizes, n, d_digests, d_state, c_begin, c_end, s);
   return launch_sha256_pipelined<2, 3, 0, 16, 0>(d_ptrs, d_sizes, n, d_digests,
                                                  d_state, c_begin, c_end, s);

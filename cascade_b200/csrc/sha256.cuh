@@ -142,5 +142,27 @@ __device__ __forceinline__ void round_kw3(uint32_t &a, uint32_t &b,
   d = c; c = b; b = a; a = a_new;
 }
 
+// round_kw3 with Ch added to d + h + kw on the integer ALU and the sum
+// added to Sig1(e) by one IMAD: the e-recurrence carries one IMAD instead
+// of two (12 ALU + 4 IMAD instructions).  With the K+W ring, 4096 chains:
+// 1614 cycles per chunk against 1641 for round_kw3; from registers alone,
+// 1602 against 1682.
+//   e' = IMAD(Sig1(e), 1, Ch(e,f,g) + (d + (h + kw)))
+//   a' = IADD3(e', Sig0(a), Maj(a,b,c) - d)
+__device__ __forceinline__ void round_kw9(uint32_t &a, uint32_t &b,
+                                          uint32_t &c, uint32_t &d,
+                                          uint32_t &e, uint32_t &f,
+                                          uint32_t &g, uint32_t &h,
+                                          uint32_t kw, uint32_t one,
+                                          uint32_t neg_one) {
+  const uint32_t dhk = mad(d, one, mad(h, one, kw));
+  const uint32_t ch = (e & f) ^ (~e & g);
+  const uint32_t e_new = mad(Sig1(e), one, ch + dhk);
+  const uint32_t q = mad(d, neg_one, (a & b) | (c & (a | b)));
+  const uint32_t a_new = e_new + Sig0(a) + q;
+  h = g; g = f; f = e; e = e_new;
+  d = c; c = b; b = a; a = a_new;
+}
+
 }  // namespace sha
 }  // namespace cb

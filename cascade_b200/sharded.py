@@ -154,8 +154,12 @@ class CudaShardOps:
 
     def prepare(self, blocks, host, world, rank):
         """Room in this rank's pool for the batch (demoting to the DRAM
-        tier); returns the relocation records the next begin sends."""
-        _, sizes, _ = (self._describe_host if host else self._describe)(blocks)
+        tier); returns the relocation records the next begin sends.
+        Without a DRAM tier there is nothing to do."""
+        self._desc = (self._describe_host if host else self._describe)(blocks)
+        if not self.store._cfg.shm_capacity_bytes:
+            return 0
+        sizes = self._desc[1]
         n = len(sizes)
         moves = _u64(0)
         check(_lib.load().cascade_shard_put_prepare(
@@ -177,16 +181,23 @@ class CudaShardOps:
         self._n = n
         self._world = world
 
+    def _described(self, blocks, describe):
+        """prepare's description of these blocks, or a new one."""
+        desc, self._desc = getattr(self, "_desc", None), None
+        return desc if desc is not None else describe(blocks)
+
     def begin(self, blocks, is_prefix, world, rank):
         """Hashes and stores the batch speculatively (returns at once)."""
         self._begin(_lib.load().cascade_shard_put_begin,
-                    self._describe(blocks), is_prefix, world, rank)
+                    self._described(blocks, self._describe), is_prefix,
+                    world, rank)
 
     def begin_host(self, blocks, is_prefix, world, rank):
         """begin for host blocks: a list of uint8 numpy arrays, or one 2-D
         uint8 array (pinned rows are staged fastest)."""
         self._begin(_lib.load().cascade_shard_put_begin_host,
-                    self._describe_host(blocks), is_prefix, world, rank)
+                    self._described(blocks, self._describe_host), is_prefix,
+                    world, rank)
 
     def records(self, cap):
         """The batch's records for `world` segments of `cap` entries (a
