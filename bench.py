@@ -495,6 +495,82 @@ def section_dedup(ctx, args):
             "hits_exact": total_hits == expected}
 
 
+def section_capped(ctx, args):
+    """The llama3-70b shape with an HBM pool too small for it (SURVEY cfg5's
+    capped variant, scaled to fit a short run at every GPU count): 2048 x 5
+    MiB blocks per GPU, 30% Zipf(1.1) copies of a 256-block pool shared by
+    all GPUs, into 2 GiB of HBM per GPU (4 GiB at N > 1, where a sharded put
+    holds each slice in HBM while its keys resolve) over a DRAM tier, so
+    every step demotes to and places in the DRAM tier through the copy
+    streams.  Dedup hits must equal N - #distinct exactly."""
+    import numpy as np
+    from cascade_b200 import cascade_cpp as cc
+    from cascade_b200 import workloads
+    torch = ctx.torch
+    n, pool_n = 2048, 256
+    seq, _ = workloads.dedup_sequence(n, SEED + 77 + ctx.rank, pool=pool_n,
+                                      sessions=64, shared_frac=0.3)
+    geo = workloads.LLAMA3_70B
+    pool = workloads.kv_blocks_torch(pool_n, SEED + 77, ctx.dev, **geo)
+    uniq_n = int((seq >= pool_n).sum())
+    uniq = workloads.kv_blocks_torch(uniq_n, SEED + 2000 + ctx.rank, ctx.dev,
+                                     **geo)
+    rows = workloads.materialise(seq, pool, uniq)
+    del pool, uniq
+    torch.cuda.empty_cache()
+    bb = rows.shape[1]
+    cap = (2 << 30) if ctx.world == 1 else (4 << 30)
+    cfg = make_cfg(cc, ctx.local, cap, shm=16 << 30)
+    if ctx.world > 1:
+        from cascade_b200.sharded import ShardedCascadeStore
+        store = ShardedCascadeStore(cfg)
+        per = int(0.8 * cap // (bb // 2))
+        cuts = list(range(0, n, per)) + [n]
+
+        def put():
+            store.clear()
+            return sum(store.put_batch(rows[a:b])
+                       for a, b in zip(cuts[:-1], cuts[1:]))
+    else:
+        store = cc.CascadeStore(cfg)
+        cuts = [0, n]
+        ptrs = np.arange(n, dtype=np.uint64) * np.uint64(bb) + np.uint64(rows.data_ptr())
+        sizes = np.full(n, bb, np.uint64)
+
+        def put():
+            store.clear()
+            return store._put_batch_raw(n, ptrs, sizes, None, None, False,
+                                        ctx.stream)
+
+    ms, stored = ctx.timed(put, 2, 3)
+    assert stored == n, stored
+    st = store.get_stats()
+    store.close()
+    del rows
+    torch.cuda.empty_cache()
+    used = np.zeros(pool_n, np.int64)
+    used[np.unique(seq[seq < pool_n])] = 1
+    ev = ctx.gather_rows(torch.tensor(
+        np.concatenate([used, [uniq_n, int(st.dedup_hits), int(st.gpu_evictions),
+                               int(st.shm_used), int(st.gpu_used)]]),
+        dtype=torch.int64, device=ctx.dev))
+    distinct = int((ev[:, :pool_n].max(axis=0) > 0).sum()) + int(ev[:, pool_n].sum())
+    hits = int(ev[:, pool_n + 1].sum())
+    expected = ctx.world * n - distinct
+    assert hits == expected, (hits, expected)
+    return {"workload": "llama3-70b KV, capped HBM: 2048 x 5 MiB per GPU, "
+                        "30% Zipf(1.1) copies of a 256-block pool shared by "
+                        "all GPUs, every copy in its own buffer; "
+                        f"{cap >> 30} GiB HBM pool per GPU over a DRAM tier",
+            "gbps": ctx.world * n * bb / (ms * 1e-3) / 1e9, "ms_per_step": ms,
+            "dedup_hits": hits, "expected_hits": expected,
+            "hits_exact": hits == expected,
+            "gpu_evictions_per_step": int(ev[:, pool_n + 2].sum()),
+            "dram_tier_bytes_after_step": int(ev[:, pool_n + 3].sum()),
+            "hbm_bytes_after_step": int(ev[:, pool_n + 4].sum()),
+            "put_slices": len(cuts) - 1}
+
+
 def hbm_peak():
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
@@ -687,6 +763,7 @@ def main_ours(args):
         extra["sweep"] = section_sweep(ctx, args, peak_gbps.value)
     if not args.headline_only:
         extra["dedup"] = section_dedup(ctx, args)
+        extra["capped"] = section_capped(ctx, args)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
