@@ -116,6 +116,10 @@ def ref() -> Optional[ctypes.CDLL]:
         R.ref_store_create.argtypes = [ctypes.c_char_p, ctypes.c_size_t,
                                        ctypes.c_int, ctypes.c_int]
         R.ref_store_create.restype = ctypes.c_void_p
+        R.ref_store_create_gpu.argtypes = [ctypes.c_char_p, ctypes.c_size_t,
+                                           ctypes.c_size_t, ctypes.c_int,
+                                           ctypes.c_int, ctypes.c_int]
+        R.ref_store_create_gpu.restype = ctypes.c_void_p
         R.ref_store_destroy.argtypes = [ctypes.c_void_p]
         R.ref_store_clear.argtypes = [ctypes.c_void_p]
         R.ref_store_put.argtypes = [ctypes.c_void_p, ctypes.c_char_p, _u8p,
@@ -214,16 +218,22 @@ STAT_FIELDS = ("gpu_used", "shm_used", "gpu_hits", "shm_hits", "lustre_hits",
 
 
 class RefStore:
-    """The reference CascadeStore with use_gpu=False (CPU tiers only)."""
+    """The reference CascadeStore: use_gpu=False (CPU tiers only) unless
+    gpu_bytes is given, then with its GPU tier on device 0."""
 
     def __init__(self, shm_path: str, shm_bytes: int, kv_compression=False,
-                 dedup_enabled=True):
+                 dedup_enabled=True, gpu_bytes=0, semantic_eviction=True):
         self._R = ref()
         if self._R is None:
             raise FileNotFoundError(f"{REF_SO} missing: run `make -C oracle ref`")
-        self._h = self._R.ref_store_create(shm_path.encode(), shm_bytes,
-                                           int(kv_compression),
-                                           int(dedup_enabled))
+        if gpu_bytes:
+            self._h = self._R.ref_store_create_gpu(
+                shm_path.encode(), shm_bytes, gpu_bytes, int(kv_compression),
+                int(dedup_enabled), int(semantic_eviction))
+        else:
+            self._h = self._R.ref_store_create(shm_path.encode(), shm_bytes,
+                                               int(kv_compression),
+                                               int(dedup_enabled))
 
     def put(self, block_id: str, data: np.ndarray, is_prefix=False) -> bool:
         data = np.ascontiguousarray(data, dtype=np.uint8)

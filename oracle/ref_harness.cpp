@@ -79,6 +79,21 @@ void *ref_store_create(const char *shm_path, size_t shm_bytes,
   return new cascade::CascadeStore(cfg);
 }
 
+// The reference CascadeStore with its GPU tier on device 0 (GPUBackend:
+// cudaMalloc'd pool, copies only, no kernels), to pin the store model's
+// demotion counters.
+void *ref_store_create_gpu(const char *shm_path, size_t shm_bytes,
+                           size_t gpu_bytes, int kv_compression,
+                           int dedup_enabled, int semantic_eviction) {
+  auto cfg = cpu_only_config(shm_path, shm_bytes, kv_compression,
+                             dedup_enabled);
+  cfg.use_gpu = true;
+  cfg.gpu_capacity_bytes = gpu_bytes;
+  cfg.gpu_device_id = 0;
+  cfg.semantic_eviction = semantic_eviction != 0;
+  return new cascade::CascadeStore(cfg);
+}
+
 void ref_store_destroy(void *s) {
   delete static_cast<cascade::CascadeStore *>(s);
 }
