@@ -2061,8 +2061,9 @@ inline int nblocks(size_t n) { return (int)((n + 255) / 256); }
 // its whole batch in HBM until the keys resolve, so the room is made first.
 static int shard_prepare(Store &st, size_t n, const uint64_t *h_sizes,
                          int world, int rank, uint64_t *n_moves) {
-  *n_moves = 0;
-  st.shard_moves.clear();
+  // Relocation records that a failed put never sent stay pending: the
+  // owners' entries must still learn where those payloads went.
+  *n_moves = st.shard_moves.size();
   if (!st.hbm || !st.dram_tier || n == 0) return CASCADE_OK;
   uint64_t need = 0;
   for (size_t i = 0; i < n; ++i)
@@ -2250,23 +2251,26 @@ static int shard_records(Store &st, size_t cap, uint8_t *d_send) {
   cudaStream_t s = st.s;
   CB_CUDA(cudaMemsetAsync(d_send, 0xff,
                           (size_t)world * cap * sizeof(ShardRecord), s));
-  if (n == 0) return CASCADE_OK;
+  if (n == 0 && st.shard_moves.empty()) return CASCADE_OK;
   int rc = ensure_device_buf(st.shard_aux, st.oc_aux_cap,
                              2048 + st.shard_moves.size() * sizeof(ShardRecord),
                              s);
   if (rc) return rc;
   uint32_t *cursor = reinterpret_cast<uint32_t *>(st.shard_aux);
-  CB_CUDA(cudaStreamWaitEvent(s, st.ev2, 0));
   CB_CUDA(cudaMemsetAsync(cursor, 0, 256 * sizeof(uint32_t), s));
   CB_CUDA(cudaMemsetAsync(st.sc.err, 0, sizeof(int), s));
-  shard_records_kernel<<<nblocks(n), 256, 0, s>>>(
-      (int)n, world, (uint32_t)rank, ((uint64_t)rank << 32) + 1,
-      (uint32_t)cap, reinterpret_cast<const uint64_t *>(st.sc.digests),
-      st.sc.off, st.sc.sizes, st.sc.flags, st.sc.hdr, cursor,
-      reinterpret_cast<ShardRecord *>(d_send), st.sc.err);
-  count_launches(1);
-  CB_CUDA(cudaGetLastError());
+  if (n > 0) {
+    CB_CUDA(cudaStreamWaitEvent(s, st.ev2, 0));
+    shard_records_kernel<<<nblocks(n), 256, 0, s>>>(
+        (int)n, world, (uint32_t)rank, ((uint64_t)rank << 32) + 1,
+        (uint32_t)cap, reinterpret_cast<const uint64_t *>(st.sc.digests),
+        st.sc.off, st.sc.sizes, st.sc.flags, st.sc.hdr, cursor,
+        reinterpret_cast<ShardRecord *>(d_send), st.sc.err);
+    count_launches(1);
+    CB_CUDA(cudaGetLastError());
+  }
   if ((rc = shard_send_moves(st, world, cap, cursor, d_send))) return rc;
+  if (n == 0) return CASCADE_OK;
   CB_CUDA(cudaMemcpyAsync(st.sc.h_off, st.sc.off, n * 8,
                           cudaMemcpyDeviceToHost, s));
   CB_CUDA(cudaMemcpyAsync(st.sc.h_err, st.sc.err, sizeof(int),
