@@ -2062,8 +2062,12 @@ inline int nblocks(size_t n) { return (int)((n + 255) / 256); }
 static int shard_prepare(Store &st, size_t n, const uint64_t *h_sizes,
                          int world, int rank, uint64_t *n_moves) {
   // Relocation records that a failed put never sent stay pending: the
-  // owners' entries must still learn where those payloads went.
+  // owners' entries must still learn where those payloads went.  A records
+  // step after a begin that failed sends them alone.
   *n_moves = st.shard_moves.size();
+  st.shard_open = 0;
+  st.shard_world = world;
+  st.shard_rank = rank;
   if (!st.hbm || !st.dram_tier || n == 0) return CASCADE_OK;
   uint64_t need = 0;
   for (size_t i = 0; i < n; ++i)

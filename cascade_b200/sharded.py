@@ -154,9 +154,11 @@ class CudaShardOps:
 
     def prepare(self, blocks, host, world, rank):
         """Room in this rank's pool for the batch (demoting to the DRAM
-        tier); returns the relocation records the next begin sends.
-        Without a DRAM tier there is nothing to do."""
+        tier); returns how many relocation records the records step sends,
+        those a failed put left pending included.  Without a DRAM tier
+        there is nothing to do."""
         self._desc = (self._describe_host if host else self._describe)(blocks)
+        self._n, self._world = 0, world
         if not self.store._cfg.shm_capacity_bytes:
             return 0
         sizes = self._desc[1]
@@ -397,11 +399,12 @@ class ShardedCascadeStore:
                 empty = (0, np.zeros(0, np.uint8), np.zeros((0, 32), np.uint8))
                 return empty if return_status else 0
             send = None
-            if error is None:
+            if error is None or moves:
+                # after a failed begin: the relocation records alone
                 try:
                     send = self.ops.records(cap)
                 except Exception as e:   # noqa: BLE001
-                    error = e
+                    error = error or e
             if send is None:
                 send = unused(self.world * cap, RECORD_BYTES, dev)
             recv = torch.empty_like(send)

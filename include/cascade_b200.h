@@ -291,8 +291,10 @@ int cascade_store_get_batch(cascade_store_t *s, size_t n,
  * gpu_backend.cu:467-487, as called from CascadeStore::put,
  * cascade_core.cpp:1100-1103), and sets *n_moves to the relocation records
  * the next records call adds to d_send: one per demoted payload whose key
- * another rank owns, so that the owner's entry follows it.  Without a DRAM
- * tier it does nothing (*n_moves = 0). */
+ * another rank owns, so that the owner's entry follows it.  Records that a
+ * failed put never sent stay pending and count here too; when begin fails
+ * after prepare, a records call still sends them (the batch carries no
+ * blocks).  Without a DRAM tier it does nothing (*n_moves = 0). */
 int cascade_shard_put_prepare(cascade_store_t *s, size_t n,
                               const uint64_t *h_sizes, int world, int rank,
                               uint64_t *n_moves);

@@ -162,7 +162,7 @@ def _demote_blocks(rank, rnd):
     return list(own) + picks
 
 
-def _demote_main(rank, world, port, out_dir, q8):
+def _demote_main(rank, world, port, out_dir, q8, fail_round=None):
     import datetime
 
     import torch.distributed as dist
@@ -185,17 +185,41 @@ def _demote_main(rank, world, port, out_dir, q8):
         cfg.kv_compression = True
         cfg.gpu_q8 = q8
         store = ShardedCascadeStore(cfg)
+        moves = []
+        if fail_round is not None and rank == 1:
+            # host-side injection: rank 1's begin raises in one round, after
+            # its prepare demoted payloads whose keys rank 0 owns
+            prepare, begin = store.ops.prepare, store.ops.begin
+            state = {"rnd": 0}
+
+            def counted_prepare(*a):
+                m = prepare(*a)
+                moves.append(m)
+                return m
+
+            def failing_begin(*a):
+                if state["rnd"] == fail_round:
+                    raise RuntimeError("injected begin failure")
+                return begin(*a)
+            store.ops.prepare, store.ops.begin = counted_prepare, failing_begin
         res = []
         for rnd in range(4):
             blocks = torch.from_numpy(np.stack(_demote_blocks(rank, rnd))).to(dev)
-            stored, status, _ = store.put_batch(blocks, return_status=True)
-            res.append({"stored": stored, "status": status.tolist()})
+            try:
+                stored, status, _ = store.put_batch(blocks, return_status=True)
+                res.append({"stored": stored, "status": status.tolist()})
+            except RuntimeError as e:
+                res.append({"error": str(e)})
+            if fail_round is not None and rank == 1:
+                state["rnd"] += 1
         s = store.get_stats()
         res.append({"gpu_used": s.gpu_used, "gpu_evictions": s.gpu_evictions,
-                    "shm_used": s.shm_used})
+                    "shm_used": s.shm_used, "moves": moves})
         ids = []
         for r in range(world):
             for rnd in range(4):
+                if (r, rnd) == (1, fail_round):
+                    continue
                 for b in _demote_blocks(r, rnd):
                     ids.append(hashlib.sha256(b.tobytes()).hexdigest()[:32])
         outs = torch.zeros((len(ids), 65536), dtype=torch.uint8, device=dev)
@@ -263,6 +287,51 @@ def test_sharded_demotion_two_gpus(tmp_path, q8):
             assert got["sha"][i] in want[k], (rank, i)
     # both ranks read the same bytes for every block
     assert res[0][5]["sha"] == res[1][5]["sha"]
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < WORLD, reason="needs 2 GPUs")
+def test_sharded_demotion_survives_a_failed_begin(tmp_path):
+    """As the demotion test, but rank 1's begin raises in round 2, after its
+    prepare demoted payloads whose keys rank 0 owns.  Rank 1 still sends
+    those relocation records in the failed round's exchange, so rank 0's
+    entries follow the payloads to rank 1's DRAM tier before rank 1's later
+    puts reuse the freed HBM: every block that was put reads back as the
+    oracle's compress -> decompress of its bytes, on both ranks, and the
+    statuses equal serial puts without rank 1's failed batch."""
+    import torch.multiprocessing as mp
+
+    import oracle
+    fail_round = 2
+    mp.spawn(_demote_main, args=(WORLD, _free_port(), str(tmp_path), True,
+                                 fail_round), nprocs=WORLD, join=True)
+    res = [json.load(open(tmp_path / f"d{r}.json")) for r in range(WORLD)]
+    assert res[1][fail_round] == {"error": "injected begin failure"}
+    assert res[1][4]["moves"][fail_round] > 0
+    known = set()
+    puts = [(r, rnd) for rnd in range(4) for r in range(WORLD)
+            if (r, rnd) != (1, fail_round)]
+    for r, rnd in puts:
+        got = res[r][rnd]
+        assert got["stored"] == 16
+        for b, s in zip(_demote_blocks(r, rnd), got["status"]):
+            d = hashlib.sha256(b.tobytes()).digest()[:16]
+            assert (s != 0) == (d in known)
+            known.add(d)
+    want = {}
+    for r, rnd in puts:
+        for b in _demote_blocks(r, rnd):
+            k = hashlib.sha256(b.tobytes()).hexdigest()[:32]
+            want[k] = hashlib.sha256(np.ascontiguousarray(
+                oracle.kv_decompress(oracle.kv_compress(b), b.size))
+                .tobytes()).hexdigest()
+    ids = [hashlib.sha256(b.tobytes()).hexdigest()[:32]
+           for r in range(WORLD) for rnd in range(4)
+           if (r, rnd) != (1, fail_round) for b in _demote_blocks(r, rnd)]
+    for rank in range(WORLD):
+        got = res[rank][5]
+        assert got["found"] == [1] * len(ids)
+        for i, k in enumerate(ids):
+            assert got["sha"][i] == want[k], (rank, i)
 
 
 def _single_main(rank, world, port, out_dir):
