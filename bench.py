@@ -524,13 +524,13 @@ def section_capped(ctx, args):
     if ctx.world > 1:
         from cascade_b200.sharded import ShardedCascadeStore
         store = ShardedCascadeStore(cfg)
-        per = int(0.8 * cap // (bb // 2))
-        cuts = list(range(0, n, per)) + [n]
+        # the store puts the batch in slices that fit its pool, hashed in
+        # one launch first
+        cuts = store.ops.slices(rows, False)[0]
 
         def put():
             store.clear()
-            return sum(store.put_batch(rows[a:b])
-                       for a, b in zip(cuts[:-1], cuts[1:]))
+            return store.put_batch(rows)
     else:
         store = cc.CascadeStore(cfg)
         cuts = [0, n]
@@ -894,16 +894,14 @@ def run_extra(args):
     if ctx.world > 1:
         from cascade_b200.sharded import ShardedCascadeStore
         store = ShardedCascadeStore(cfg)
-        # A sharded put holds its whole batch in HBM while the keys resolve
-        # (demoting older payloads first), so a capped pool takes the step
-        # in slices that fit; every rank slices the same way.
-        per = max(1, int(0.8 * cap // (bb // 2))) if capped else n
-        cuts = list(range(0, n, per)) + [n]
+        # A sharded put holds a batch in HBM while the keys resolve
+        # (demoting older payloads first), so over a capped pool the store
+        # puts the step in slices that fit, hashed in one launch first.
+        cuts = store.ops.slices(rows, False)[0]
 
         def put():
             store.clear()
-            return sum(store.put_batch(rows[a:b])
-                       for a, b in zip(cuts[:-1], cuts[1:]))
+            return store.put_batch(rows)
     else:
         store = cc.CascadeStore(cfg)
         ptrs = np.arange(n, dtype=np.uint64) * np.uint64(bb) + np.uint64(rows.data_ptr())

@@ -1054,7 +1054,8 @@ static bool can_speculate(const Store &st, size_t n) {
 // hash on s2 (unless the caller did, `digests_ready`), allocate the slots
 // and write the payloads on the main stream.  ev2 marks the digests.
 static int speculate_local(Store &st, size_t n, const uint8_t *h_prefix,
-                           uint64_t max_size, bool digests_ready) {
+                           uint64_t max_size, bool digests_ready,
+                           bool beside_hash = true) {
   cudaStream_t s = st.s;
   bool any_q8 = false, any_raw = false;
   for (size_t i = 0; i < n; ++i) {
@@ -1100,7 +1101,7 @@ static int speculate_local(Store &st, size_t n, const uint8_t *h_prefix,
   // its SMs, an unused shared-memory request keeps them on the spare SMs,
   // so they take no issue slots from the serial chains.  With two hash
   // CTAs per SM they share the SMs (the spare SMs alone fall behind).
-  const size_t pad = sha256_neighbour_smem((int)n);
+  const size_t pad = beside_hash ? sha256_neighbour_smem((int)n) : 0;
   if (any_q8) {
     rc = launch_minmax(st.sc.ptrs, st.sc.eff_q8, (int)n, max_size, st.sc.mnmx,
                        s, pad);
@@ -2179,10 +2180,12 @@ static int shard_send_moves(Store &st, int world, size_t cap,
 // written by shard_records once the caller knows the exchange's segment
 // size.  Does not wait for the device.
 static int shard_begin_staged(Store &st, size_t n, uint64_t max_size,
-                              bool digests_ready, const uint8_t *h_prefix) {
+                              bool digests_ready, const uint8_t *h_prefix,
+                              bool beside_hash = true) {
   CB_CHECK(can_speculate(st, n), CASCADE_ERR_NOMEM,
            "sharded put: the HBM pool cannot hold the whole batch");
-  int rc = speculate_local(st, n, h_prefix, max_size, digests_ready);
+  int rc = speculate_local(st, n, h_prefix, max_size, digests_ready,
+                           beside_hash);
   if (rc) return rc;
   st.shard_open = n;
   return CASCADE_OK;
@@ -2209,6 +2212,55 @@ static int shard_begin(Store &st, size_t n, const uint64_t *h_ptrs,
   if ((rc = upload_batch(st, n, h_ptrs, h_sizes, nullptr, &max_size)))
     return rc;
   return shard_begin_staged(st, n, max_size, false, h_prefix);
+}
+
+// begin for a slice of a batch whose digests the caller already computed
+// on the device (one hash launch over the whole batch runs all its chains
+// at once; slices hashed one by one would each run only theirs).
+static int shard_begin_digests(Store &st, size_t n, const uint64_t *h_ptrs,
+                               const uint64_t *h_sizes,
+                               const uint8_t *h_prefix,
+                               const uint8_t *d_digests, int world, int rank) {
+  st.shard_open = 0;
+  int rc = shard_check(st, world, rank);
+  if (rc) return rc;
+  st.shard_rank = rank;
+  st.shard_world = world;
+  if (n == 0) return CASCADE_OK;
+  uint64_t max_size = 0;
+  if ((rc = upload_batch(st, n, h_ptrs, h_sizes, nullptr, &max_size)))
+    return rc;
+  CB_CUDA(cudaMemcpyAsync(st.sc.digests, d_digests, n * 32,
+                          cudaMemcpyDeviceToDevice, st.s));
+  CB_CUDA(cudaEventRecord(st.ev2, st.s));
+  return shard_begin_staged(st, n, max_size, true, h_prefix, false);
+}
+
+// Cut points of a sharded put: consecutive blocks whose payloads fill at
+// most 4/5 of the HBM pool form a slice (a sharded put holds its batch in
+// HBM until the keys resolve, and prepare demotes older payloads to the
+// DRAM tier to make room for each slice).  Without a DRAM tier nothing can
+// make room, so the batch stays one slice.  h_cuts gets n_slices + 1
+// entries (at most max(n, 1) + 1).
+static void shard_slices(const Store &st, size_t n, const uint64_t *h_sizes,
+                         uint64_t *h_cuts, uint64_t *n_slices) {
+  size_t k = 0;
+  h_cuts[k++] = 0;
+  if (st.hbm && st.dram_tier) {
+    const uint64_t budget = st.pool_cap / 5 * 4;
+    uint64_t acc = 0;
+    for (size_t i = 0; i < n; ++i) {
+      const uint64_t b =
+          payload_bytes(h_sizes[i], q8_eligible(st, h_sizes[i], false));
+      if (acc > 0 && acc + b > budget) {
+        h_cuts[k++] = i;
+        acc = 0;
+      }
+      acc += b;
+    }
+  }
+  h_cuts[k++] = n;
+  *n_slices = k - 1;
 }
 
 // Host blocks: staged to the device first.  Uniform pinned batches are
@@ -2884,6 +2936,32 @@ extern "C" int cascade_shard_put_begin(cascade_store_t *s, size_t n,
            "batch too large");
   if (int rc = join_caller(st, stream)) return rc;
   return cb::shard_begin(st, n, h_ptrs, h_sizes, h_prefix, world, rank);
+}
+
+extern "C" int cascade_shard_put_begin_digests(
+    cascade_store_t *s, size_t n, const uint64_t *h_ptrs,
+    const uint64_t *h_sizes, const uint8_t *h_prefix,
+    const uint8_t *d_digests, int world, int rank, void *stream) {
+  STORE_ENTRY(s);
+  CB_CHECK(n == 0 || (h_ptrs && h_sizes && d_digests), CASCADE_ERR_INVALID,
+           "null argument");
+  CB_CHECK(((uintptr_t)d_digests & 3u) == 0, CASCADE_ERR_INVALID,
+           "d_digests must be 4-byte aligned");
+  CB_CHECK(n <= (size_t)UINT32_MAX - 1, CASCADE_ERR_INVALID,
+           "batch too large");
+  if (int rc = join_caller(st, stream)) return rc;
+  return cb::shard_begin_digests(st, n, h_ptrs, h_sizes, h_prefix, d_digests,
+                                 world, rank);
+}
+
+extern "C" int cascade_shard_put_slices(cascade_store_t *s, size_t n,
+                                        const uint64_t *h_sizes,
+                                        uint64_t *h_cuts, uint64_t *n_slices) {
+  STORE_ENTRY(s);
+  CB_CHECK((n == 0 || h_sizes) && h_cuts && n_slices, CASCADE_ERR_INVALID,
+           "null argument");
+  cb::shard_slices(st, n, h_sizes, h_cuts, n_slices);
+  return CASCADE_OK;
 }
 
 extern "C" int cascade_shard_put_begin_host(

@@ -61,6 +61,10 @@ _lib.register("cascade_shard_put_begin", _int,
               [_vp, _sz, _vp, _vp, _vp, _int, _int, _vp])
 _lib.register("cascade_shard_put_begin_host", _int,
               [_vp, _sz, _vp, _vp, _vp, _int, _int, _vp])
+_lib.register("cascade_shard_put_begin_digests", _int,
+              [_vp, _sz, _vp, _vp, _vp, _vp, _int, _int, _vp])
+_lib.register("cascade_shard_put_slices", _int,
+              [_vp, _sz, _vp, _vp, ctypes.POINTER(_u64)])
 _lib.register("cascade_shard_put_records", _int, [_vp, _sz, _vp, _vp])
 _lib.register("cascade_shard_resolve", _int, [_vp, _vp, _sz, _vp, _vp])
 _lib.register("cascade_shard_put_end", _int,
@@ -169,30 +173,72 @@ class CudaShardOps:
             ctypes.byref(moves)))
         return int(moves.value)
 
-    def _begin(self, fn, desc, is_prefix, world, rank):
+    def _begin(self, fn, desc, is_prefix, world, rank, digests=None):
         ptrs, sizes, keep = desc
         n = len(ptrs)
         pf = (np.array([1 if p else 0 for p in is_prefix], dtype=np.uint8)
               if is_prefix is not None else None)
         self._keep = keep
         self._n = 0
+        extra = () if digests is None else (
+            digests.data_ptr() if n else None,)
         check(fn(self.store._h, n, ptrs.ctypes.data if n else None,
                  sizes.ctypes.data if n else None,
-                 pf.ctypes.data if pf is not None else None, world, rank,
-                 self._stream()))
+                 pf.ctypes.data if pf is not None else None, *extra, world,
+                 rank, self._stream()))
         self._n = n
         self._world = world
+
+    def slices(self, blocks, host):
+        """Cut points of a batch that is put in slices, each fitting the
+        HBM pool (over a DRAM tier), and the batch's description."""
+        desc = (self._describe_host if host else self._describe)(blocks)
+        sizes = desc[1]
+        n = len(sizes)
+        cuts = np.zeros(max(n, 1) + 1, np.uint64)
+        k = _u64(0)
+        check(_lib.load().cascade_shard_put_slices(
+            self.store._h, n, sizes.ctypes.data if n else None,
+            cuts.ctypes.data, ctypes.byref(k)))
+        return [int(c) for c in cuts[:k.value + 1]], desc
+
+    @staticmethod
+    def part(blocks, desc, a, b, host):
+        """Blocks a..b-1 of a batch that slices() described."""
+        if host:
+            return blocks[a:b]
+        return desc[0][a:b], desc[1][a:b]
+
+    def digests(self, desc):
+        """SHA-256 of a described device batch in one launch (all its
+        chains at once), as a (n, 32) uint8 tensor on this GPU."""
+        import torch
+        ptrs, sizes, _ = desc
+        n = len(ptrs)
+        d_ptrs = torch.from_numpy(ptrs.view(np.int64)).to(self.device)
+        d_sizes = torch.from_numpy(sizes.view(np.int64)).to(self.device)
+        out = torch.empty((n, 32), dtype=torch.uint8, device=self.device)
+        check(_lib.load().cascade_sha256_batch(
+            d_ptrs.data_ptr(), d_sizes.data_ptr(), n, out.data_ptr(),
+            self._stream()))
+        return out
 
     def _described(self, blocks, describe):
         """prepare's description of these blocks, or a new one."""
         desc, self._desc = getattr(self, "_desc", None), None
         return desc if desc is not None else describe(blocks)
 
-    def begin(self, blocks, is_prefix, world, rank):
-        """Hashes and stores the batch speculatively (returns at once)."""
-        self._begin(_lib.load().cascade_shard_put_begin,
-                    self._described(blocks, self._describe), is_prefix,
-                    world, rank)
+    def begin(self, blocks, is_prefix, world, rank, digests=None):
+        """Hashes (unless `digests` holds the batch's digests, a device
+        tensor) and stores the batch speculatively (returns at once)."""
+        if digests is None:
+            self._begin(_lib.load().cascade_shard_put_begin,
+                        self._described(blocks, self._describe), is_prefix,
+                        world, rank)
+        else:
+            self._begin(_lib.load().cascade_shard_put_begin_digests,
+                        self._described(blocks, self._describe), is_prefix,
+                        world, rank, digests)
 
     def begin_host(self, blocks, is_prefix, world, rank):
         """begin for host blocks: a list of uint8 numpy arrays, or one 2-D
@@ -360,68 +406,128 @@ class ShardedCascadeStore:
         size are copied to the GPU in stripes and hashed as they land."""
         return self._put(True, blocks, len(blocks), is_prefix, return_status)
 
-    def _sizes(self, n, extra=0):
-        """Collective: every rank's (batch size, extra records), in one
-        small all-gather."""
+    def _sizes(self, n, extra=0, more=0):
+        """Collective: every rank's (batch size, extra records, more slices
+        to come), in one small all-gather."""
         import torch
         import torch.distributed as dist
-        mine = torch.tensor([n, extra], dtype=torch.int64,
+        mine = torch.tensor([n, extra, more], dtype=torch.int64,
                             device=self.ops.device)
-        every = torch.zeros(2 * self.world, dtype=torch.int64,
+        every = torch.zeros(3 * self.world, dtype=torch.int64,
                             device=self.ops.device)
         dist.all_gather_into_tensor(every, mine, group=self.group)
         v = [int(x) for x in every.tolist()]
-        return list(zip(v[0::2], v[1::2]))
+        return list(zip(v[0::3], v[1::3], v[2::3]))
 
     def _put(self, host, blocks, n, is_prefix, return_status):
-        """The put exchange.  A rank whose own step fails still takes part
-        in both all-to-alls (sending entries that carry nothing, or failed
-        replies for the records it received) and raises afterwards, so its
-        peers never wait on it; their blocks owned by a failed rank come
-        back FAILED."""
-        import torch
-        import torch.distributed as dist
+        """A put in one or more rounds of the exchange.  A batch whose
+        payloads do not fit this rank's HBM pool (over a DRAM tier) goes in
+        slices that do, one round each; a device batch is hashed in one
+        launch first, so that all its chains run at once.  Every round's
+        size all-gather carries a flag for more slices to come, and the
+        ranks run rounds (with empty batches once theirs is done) until no
+        rank has more.  Keys resolve in (round, rank, block) order.
+
+        A rank whose own step fails still takes part in every exchange and
+        raises once the rounds are over, so its peers never wait on it."""
         with self._lock:
-            dev = self.ops.device
-            error, moves = None, 0
-            try:    # room in this rank's pool; relocation records to send
-                moves = self.ops.prepare(blocks, host, self.world, self.rank)
-                begin = self.ops.begin_host if host else self.ops.begin
-                begin(blocks, is_prefix, self.world, self.rank)
-            except Exception as e:       # noqa: BLE001 (re-raised below)
-                error = e
-            # while the hash runs: every rank's batch and relocation count
-            sizes = self._sizes(n, moves)
-            cap = max(c + m for c, m in sizes)
-            if cap == 0:
-                if error is not None:
-                    raise error
-                empty = (0, np.zeros(0, np.uint8), np.zeros((0, 32), np.uint8))
-                return empty if return_status else 0
-            send = None
-            if error is None or moves:
-                # after a failed begin: the relocation records alone
+            cuts, desc, digests = [0, n], None, None
+            if n and hasattr(self.ops, "slices"):
+                cuts, desc = self.ops.slices(blocks, host)
+            error = None
+            if len(cuts) > 2 and not host and hasattr(self.ops, "digests"):
                 try:
-                    send = self.ops.records(cap)
-                except Exception as e:   # noqa: BLE001
-                    error = error or e
-            if send is None:
-                send = unused(self.world * cap, RECORD_BYTES, dev)
-            recv = torch.empty_like(send)
-            dist.all_to_all_single(recv, send, group=self.group)
-            try:
-                reply = self.ops.resolve(recv)
-            except Exception as e:       # noqa: BLE001
-                error = error or e
-                reply = failed_replies(recv)
-            back = torch.empty_like(reply)
-            dist.all_to_all_single(back, reply, group=self.group)
+                    digests = self.ops.digests(desc)
+                except Exception as e:   # noqa: BLE001 (re-raised below)
+                    error = e
+            parts, k = [], 0
+            while True:
+                a, b = (cuts[k], cuts[k + 1]) if k + 1 < len(cuts) else (n, n)
+                if a == b:
+                    part = []            # this rank's slices are done
+                elif len(cuts) == 2:
+                    part = blocks
+                else:
+                    part = self.ops.part(blocks, desc, a, b, host)
+                more = error is None and k + 2 < len(cuts)
+                r, others, err = self._round(
+                    host, part, b - a,
+                    is_prefix[a:b] if is_prefix is not None else None,
+                    digests[a:b] if digests is not None else None, more,
+                    skip=error is not None)
+                error = error or err
+                if r is not None and a < b:
+                    parts.append(r)
+                k += 1
+                if not others:
+                    break
             if error is not None:
                 raise error
-            stored, status, digests = self.ops.end(back)
-        if return_status:
-            return stored, status, digests
-        return stored
+        stored = sum(p[0] for p in parts)
+        if not return_status:
+            return stored
+        if not parts:
+            return 0, np.zeros(0, np.uint8), np.zeros((0, 32), np.uint8)
+        return (stored, np.concatenate([p[1] for p in parts]),
+                np.concatenate([p[2] for p in parts]))
+
+    def _round(self, host, blocks, n, is_prefix, digests, more, skip=False):
+        """One round of the put exchange for this rank's `blocks` (none
+        with `skip`, after an earlier round failed here).  Returns (result
+        or None, whether any rank has more slices, this rank's error)."""
+        import torch
+        import torch.distributed as dist
+        dev = self.ops.device
+        error, moves = None, 0
+        if skip:
+            n = 0
+        else:
+            try:    # room in this rank's pool; relocation records to send
+                moves = self.ops.prepare(blocks, host, self.world, self.rank)
+                if host:
+                    self.ops.begin_host(blocks, is_prefix, self.world,
+                                        self.rank)
+                elif digests is not None:
+                    self.ops.begin(blocks, is_prefix, self.world, self.rank,
+                                   digests=digests)
+                else:
+                    self.ops.begin(blocks, is_prefix, self.world, self.rank)
+            except Exception as e:       # noqa: BLE001 (returned below)
+                error = e
+        # while the hash runs: every rank's batch, relocation count and
+        # whether it has more slices
+        sizes = self._sizes(n, moves, 1 if more else 0)
+        others = any(m for _, _, m in sizes)
+        cap = max(c + m for c, m, _ in sizes)
+        if cap == 0:
+            if error is not None or skip:
+                return None, others, error
+            return ((0, np.zeros(0, np.uint8), np.zeros((0, 32), np.uint8)),
+                    others, None)
+        send = None
+        if not skip and (error is None or moves):
+            # after a failed begin: the relocation records alone
+            try:
+                send = self.ops.records(cap)
+            except Exception as e:       # noqa: BLE001
+                error = error or e
+        if send is None:
+            send = unused(self.world * cap, RECORD_BYTES, dev)
+        recv = torch.empty_like(send)
+        dist.all_to_all_single(recv, send, group=self.group)
+        try:
+            reply = self.ops.resolve(recv)
+        except Exception as e:           # noqa: BLE001
+            error = error or e
+            reply = failed_replies(recv)
+        back = torch.empty_like(reply)
+        dist.all_to_all_single(back, reply, group=self.group)
+        if error is not None or skip:
+            return None, others, error
+        try:
+            return self.ops.end(back), others, None
+        except Exception as e:           # noqa: BLE001
+            return None, others, e
 
     def get_batch(self, ids, outs):
         """Collective: every rank reads its own list of blocks (any rank may
@@ -445,7 +551,7 @@ class ShardedCascadeStore:
             raise ValueError("one output per id")
         with self._lock:
             dev = self.ops.device
-            cap = max(c for c, _ in self._sizes(n_out))
+            cap = max(c for c, _, _ in self._sizes(n_out))
             if cap == 0:
                 return np.zeros(0, np.uint8), np.zeros(0, np.uint64)
             error = None

@@ -311,6 +311,29 @@ int cascade_shard_put_begin_host(cascade_store_t *s, size_t n,
                                  const uint64_t *h_sizes,
                                  const uint8_t *h_prefix, int world, int rank,
                                  void *stream);
+/* begin for blocks whose SHA-256 digests the caller already computed on
+ * this GPU (d_digests: n x 32 bytes, 4-byte aligned, e.g. from
+ * cascade_sha256_batch; ready on `stream`).  A batch larger than the HBM
+ * pool is put in slices (cascade_shard_put_slices); hashing the whole batch
+ * in one launch first runs all its chains at once, where slices hashed one
+ * by one would each run only theirs.  The payload kernels then have the
+ * whole GPU. */
+int cascade_shard_put_begin_digests(cascade_store_t *s, size_t n,
+                                    const uint64_t *h_ptrs,
+                                    const uint64_t *h_sizes,
+                                    const uint8_t *h_prefix,
+                                    const uint8_t *d_digests, int world,
+                                    int rank, void *stream);
+/* How to cut a batch of n blocks of h_sizes bytes into sharded puts that
+ * each fit this rank's HBM pool: consecutive blocks whose payloads fill at
+ * most 4/5 of the pool form a slice, and each slice's prepare demotes older
+ * payloads to the DRAM tier.  Without a DRAM tier the batch is one slice.
+ * h_cuts gets *n_slices + 1 ascending block indices from 0 to n (room for
+ * max(n, 1) + 1).  Every slice is a collective put of its own: ranks that
+ * have fewer slices put empty batches while the others finish. */
+int cascade_shard_put_slices(cascade_store_t *s, size_t n,
+                             const uint64_t *h_sizes, uint64_t *h_cuts,
+                             uint64_t *n_slices);
 /* d_send: world * cap records (16-byte aligned). */
 int cascade_shard_put_records(cascade_store_t *s, size_t cap, uint8_t *d_send,
                               void *stream);

@@ -52,8 +52,9 @@ def _padded(entries, owners, world, cap):
 
 
 class CpuShardOps:
-    def __init__(self, shared_dir=None):
+    def __init__(self, shared_dir=None, slice_blocks=None):
         import torch
+        self.slice_blocks = slice_blocks
         self.device = torch.device("cpu")
         self.index = {}        # this rank's key slice: key -> (seq, holder, size)
         self._digests = None
@@ -63,6 +64,18 @@ class CpuShardOps:
         self._get_keys = None
         self.shared_dir = shared_dir
         self.store = None
+
+    def slices(self, blocks, host):
+        """Cut points of a put: slices of `slice_blocks` blocks when set
+        (the stand-in for an HBM pool that holds that many), else one."""
+        n = len(blocks)
+        if not self.slice_blocks:
+            return [0, n], None
+        return list(range(0, n, self.slice_blocks)) + [n], None
+
+    @staticmethod
+    def part(blocks, desc, a, b, host):
+        return blocks[a:b]
 
     def begin(self, blocks, is_prefix, world, rank):
         n = len(blocks)

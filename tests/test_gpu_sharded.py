@@ -334,7 +334,117 @@ def test_sharded_demotion_survives_a_failed_begin(tmp_path):
             assert got["sha"][i] == want[k], (rank, i)
 
 
-def _single_main(rank, world, port, out_dir):
+def _sliced_main(rank, world, port, out_dir):
+    import datetime
+
+    import torch.distributed as dist
+
+    from cascade_b200 import cascade_cpp as cc
+    from cascade_b200.sharded import ShardedCascadeStore
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                            timeout=datetime.timedelta(seconds=60))
+    try:
+        cfg = cc.CascadeConfig()
+        cfg.gpu_device_id = rank
+        cfg.gpu_capacity_bytes = 20 * 32768        # 20 INT8 blocks per GPU
+        cfg.shm_capacity_bytes = 64 << 20
+        cfg.dram_chunk_bytes = 4 << 20
+        cfg.kv_compression = True
+        cfg.gpu_q8 = True
+        store = ShardedCascadeStore(cfg)
+        res = []
+        # rank 0: one batch of 48 blocks (three pools' worth of slices), then
+        # 16; rank 1: 16 blocks, then 48
+        plan = [[0, 1, 2], [3]] if rank == 0 else [[0], [1, 2, 3]]
+        for rnds in plan:
+            mine = [b for rnd in rnds for b in _demote_blocks(rank, rnd)]
+            blocks = torch.from_numpy(np.stack(mine)).to(dev)
+            cuts, _ = store.ops.slices(blocks, False)
+            stored, status, digests = store.put_batch(blocks,
+                                                      return_status=True)
+            res.append({"rnds": rnds, "cuts": cuts, "stored": stored,
+                        "status": status.tolist(),
+                        "digests": [bytes(d).hex() for d in digests]})
+        s = store.get_stats()
+        res.append({"gpu_used": s.gpu_used, "gpu_evictions": s.gpu_evictions})
+        ids = [hashlib.sha256(b.tobytes()).hexdigest()[:32]
+               for r in range(world) for rnd in range(4)
+               for b in _demote_blocks(r, rnd)]
+        outs = torch.zeros((len(ids), 65536), dtype=torch.uint8, device=dev)
+        found, sizes = store.get_batch(ids, outs)
+        res.append({"found": found.tolist(), "sizes": sizes.tolist(),
+                    "sha": [hashlib.sha256(o.cpu().numpy().tobytes())
+                            .hexdigest() for o in outs]})
+        store.close()
+        with open(os.path.join(out_dir, f"s{rank}.json"), "w") as f:
+            json.dump(res, f)
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < WORLD, reason="needs 2 GPUs")
+def test_sharded_put_of_batches_larger_than_the_pool(tmp_path):
+    """A batch of three pools' worth of blocks goes in slices that fit
+    (cascade_shard_put_slices), hashed once in one launch and put with the
+    digests (cascade_shard_put_begin_digests), one exchange round per
+    slice; the other rank puts empty batches until it is done.  Statuses
+    equal serial puts in (round, rank, block) order, digests are the
+    blocks' SHA-256, and every block reads back, from HBM or a DRAM tier,
+    as the oracle's compress -> decompress of its bytes."""
+    import torch.multiprocessing as mp
+
+    import oracle
+    mp.spawn(_sliced_main, args=(WORLD, _free_port(), str(tmp_path)),
+             nprocs=WORLD, join=True)
+    res = [json.load(open(tmp_path / f"s{r}.json")) for r in range(WORLD)]
+    assert res[0][0]["cuts"] == [0, 16, 32, 48] and res[1][0]["cuts"] == [0, 16]
+    known = set()
+    for put in range(2):
+        blocks = [[b for rnd in res[r][put]["rnds"]
+                   for b in _demote_blocks(r, rnd)] for r in range(WORLD)]
+        cuts = [res[r][put]["cuts"] for r in range(WORLD)]
+        want = [[None] * len(blocks[r]) for r in range(WORLD)]
+        for k in range(max(len(c) - 1 for c in cuts)):
+            for r in range(WORLD):
+                if k + 1 < len(cuts[r]):
+                    for i in range(cuts[r][k], cuts[r][k + 1]):
+                        d = hashlib.sha256(blocks[r][i].tobytes()).digest()[:16]
+                        want[r][i] = d in known
+                        known.add(d)
+        for r in range(WORLD):
+            got = res[r][put]
+            assert got["stored"] == len(blocks[r])
+            assert [s != 0 for s in got["status"]] == want[r]
+            assert got["digests"] == [hashlib.sha256(b.tobytes()).hexdigest()
+                                      for b in blocks[r]]
+    assert sum(r[2]["gpu_evictions"] for r in res) > 0
+    for r in res:
+        assert r[2]["gpu_used"] <= 20 * 32768
+    want = {}
+    for r in range(WORLD):
+        for rnd in range(4):
+            for b in _demote_blocks(r, rnd):
+                k = hashlib.sha256(b.tobytes()).hexdigest()[:32]
+                want[k] = hashlib.sha256(np.ascontiguousarray(
+                    oracle.kv_decompress(oracle.kv_compress(b), b.size))
+                    .tobytes()).hexdigest()
+    ids = [hashlib.sha256(b.tobytes()).hexdigest()[:32]
+           for r in range(WORLD) for rnd in range(4)
+           for b in _demote_blocks(r, rnd)]
+    for rank in range(WORLD):
+        got = res[rank][3]
+        assert got["found"] == [1] * len(ids)
+        assert got["sizes"] == [65536] * len(ids)
+        for i, k in enumerate(ids):
+            assert got["sha"][i] == want[k], (rank, i)
+
+
+def _single_main(rank, world, port, out_dir, sliced=False):
     import datetime
 
     import torch.distributed as dist
@@ -356,10 +466,24 @@ def _single_main(rank, world, port, out_dir):
         cfg.gpu_q8 = True
         store = ShardedCascadeStore(cfg)
         res = []
-        for rnd in range(4):
-            blocks = torch.from_numpy(np.stack(_demote_blocks(0, rnd))).to(dev)
-            stored, status, _ = store.put_batch(blocks, return_status=True)
-            res.append({"stored": stored, "status": status.tolist()})
+        if sliced:     # all four rounds' blocks in one batch of 4 slices
+            mine = [b for rnd in range(4) for b in _demote_blocks(0, rnd)]
+            blocks = torch.from_numpy(np.stack(mine)).to(dev)
+            assert store.ops.slices(blocks, False)[0] == [0, 16, 32, 48, 64]
+            stored, status, digests = store.put_batch(blocks,
+                                                      return_status=True)
+            assert stored == 64
+            assert [bytes(d) for d in digests] == [
+                hashlib.sha256(b.tobytes()).digest() for b in mine]
+            for rnd in range(4):
+                res.append({"stored": 16,
+                            "status": status[16 * rnd:16 * rnd + 16].tolist()})
+        else:
+            for rnd in range(4):
+                blocks = torch.from_numpy(
+                    np.stack(_demote_blocks(0, rnd))).to(dev)
+                stored, status, _ = store.put_batch(blocks, return_status=True)
+                res.append({"stored": stored, "status": status.tolist()})
         s = store.get_stats()
         res.append({"gpu_used": s.gpu_used, "gpu_evictions": s.gpu_evictions})
         ids = [hashlib.sha256(b.tobytes()).hexdigest()[:32]
@@ -376,17 +500,21 @@ def _single_main(rank, world, port, out_dir):
         dist.destroy_process_group()
 
 
-def test_sharded_protocol_one_rank_with_demotion(tmp_path):
+@pytest.mark.parametrize("sliced", [False, True],
+                         ids=["four-puts", "one-sliced-put"])
+def test_sharded_protocol_one_rank_with_demotion(tmp_path, sliced):
     """The whole sharded C path (prepare, begin, records, resolve, end,
     lookup, reads from HBM and from the DRAM tier) on one GPU as a world of
     one rank: a 20-block pool takes 4 rounds of 16 blocks, demoting before
     each, and every block reads back as the oracle's compress ->
-    decompress; statuses equal serial puts."""
+    decompress; statuses equal serial puts.  The rounds are four puts, or
+    one put of all 64 blocks that the store cuts into 4 slices, hashed in
+    one launch and put with those digests."""
     import torch.multiprocessing as mp
 
     import oracle
-    mp.spawn(_single_main, args=(1, _free_port(), str(tmp_path)), nprocs=1,
-             join=True)
+    mp.spawn(_single_main, args=(1, _free_port(), str(tmp_path), sliced),
+             nprocs=1, join=True)
     res = json.load(open(tmp_path / "s0.json"))
     known = set()
     for rnd in range(4):

@@ -305,3 +305,63 @@ def test_sharded_put_raises_when_a_rank_never_joins(tmp_path):
     got = json.load(open(tmp_path / "a0.json"))
     assert got["outcome"].startswith("raised"), got
     assert got["seconds"] < 30
+
+
+def _sliced_main(rank, world, port, out_dir, per):
+    import torch.distributed as dist
+    from cascade_b200.sharded import ShardedCascadeStore
+    from oracle.shard_model import CpuShardOps
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        store = ShardedCascadeStore(ops=CpuShardOps(shared_dir=out_dir,
+                                                    slice_blocks=per[rank]))
+        res = []
+        for batch in range(2):
+            put = store.put_batch if batch == 0 else store.put_batch_host
+            stored, status, digests = put(_blocks(rank, batch),
+                                          return_status=True)
+            res.append({"stored": stored, "status": status.tolist(),
+                        "digests": [bytes(d).hex() for d in digests]})
+        store.close()
+        with open(os.path.join(out_dir, f"s{rank}.json"), "w") as f:
+            json.dump(res, f)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_sharded_sliced_puts_resolve_round_by_round(tmp_path):
+    """Ranks whose batches do not fit their pools put them in slices, one
+    exchange round per slice, and ranks with fewer slices (or none) put
+    empty batches until the last rank is done: statuses equal serial puts
+    in (round, rank, block) order, digests come back in block order, and
+    the hit total is N - #distinct."""
+    world, per = 3, [7, 16, None]
+    mp.spawn(_sliced_main, args=(world, _free_port(), str(tmp_path), per),
+             nprocs=world, join=True)
+    res = [json.load(open(tmp_path / f"s{r}.json")) for r in range(world)]
+    known, n_total = set(), 0
+    for batch in range(2):
+        blocks = [_blocks(r, batch) for r in range(world)]
+        cuts = [list(range(0, len(blocks[r]), per[r] or len(blocks[r])))
+                + [len(blocks[r])] for r in range(world)]
+        want = [[None] * len(blocks[r]) for r in range(world)]
+        for k in range(max(len(c) - 1 for c in cuts)):
+            for r in range(world):
+                if k + 1 >= len(cuts[r]):
+                    continue
+                for i in range(cuts[r][k], cuts[r][k + 1]):
+                    d = hashlib.sha256(blocks[r][i].tobytes()).digest()[:16]
+                    want[r][i] = 1 if d in known else 0
+                    known.add(d)
+        for r in range(world):
+            got = res[r][batch]
+            assert got["stored"] == len(blocks[r])
+            assert [0 if s == STORED else 1 for s in got["status"]] == want[r]
+            assert got["digests"] == [
+                hashlib.sha256(b.tobytes()).hexdigest() for b in blocks[r]]
+            n_total += len(blocks[r])
+    hits = sum(1 for r in range(world) for b in range(2)
+               for s in res[r][b]["status"] if s != STORED)
+    assert hits == n_total - len(known)
