@@ -191,7 +191,11 @@ class CudaShardOps:
 
     def slices(self, blocks, host):
         """Cut points of a batch that is put in slices, each fitting the
-        HBM pool (over a DRAM tier), and the batch's description."""
+        HBM pool (over a DRAM tier), and the batch's description.  Without
+        a DRAM tier a batch is one slice."""
+        if not self.store._cfg.shm_capacity_bytes:
+            return [0, len(blocks[0]) if isinstance(blocks, tuple)
+                    else len(blocks)], None
         desc = (self._describe_host if host else self._describe)(blocks)
         sizes = desc[1]
         n = len(sizes)
