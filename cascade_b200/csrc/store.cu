@@ -2246,7 +2246,12 @@ static void shard_slices(const Store &st, size_t n, const uint64_t *h_sizes,
                          uint64_t *h_cuts, uint64_t *n_slices) {
   size_t k = 0;
   h_cuts[k++] = 0;
-  if (st.hbm && st.dram_tier) {
+  uint64_t need = 0;
+  for (size_t i = 0; i < n; ++i)
+    need += payload_bytes(h_sizes[i], q8_eligible(st, h_sizes[i], false));
+  // A batch that fits the pool's free space goes in one round: its payload
+  // kernels then run beside its own hash instead of after a whole-batch one.
+  if (st.hbm && st.dram_tier && st.gpu_used + need > st.pool_cap) {
     const uint64_t budget = st.pool_cap / 5 * 4;
     uint64_t acc = 0;
     for (size_t i = 0; i < n; ++i) {

@@ -98,6 +98,54 @@ int cascade_kv_decompress_batch(const uint64_t *d_src,
                                 const uint64_t *d_dst, size_t n,
                                 uint64_t max_out_size, void *stream);
 
+/* ------------------------------------------------------------------ */
+/* KV-cache wire format on the device.                                  */
+
+/* One layer's K or V tensor of one cache: element [h][s][d] is at
+ * ptr + (h * stride_head + s * stride_seq + d) * element size.  head_dim
+ * elements are contiguous; the strides (in elements) may be anything, so
+ * a [1, heads, seq, dim] tensor, a slice of a longer static cache and a
+ * [seq, heads, dim] tensor permuted to [heads, seq, dim] all describe
+ * themselves without a copy. */
+typedef struct {
+  uint64_t ptr;
+  int64_t stride_head;
+  int64_t stride_seq;
+} cascade_kv_tensor_t;
+
+#define CASCADE_KV_FP16 0
+#define CASCADE_KV_BF16 1
+#define CASCADE_KV_FP32 2
+
+/* Bytes of one wire block: the 18-byte "<IIIIH" header + 2 x layers x
+ * heads x seq x head_dim FP16 values (kv_manager.py:11-12, 43-63). */
+uint64_t cascade_kv_wire_bytes(uint32_t layers, uint32_t heads, uint32_t seq,
+                               uint32_t head_dim);
+
+/* kv_manager.serialize_kv_cache (inference_benchmark/kv_manager.py:43-63)
+ * on the device, for n caches of one shape in one launch.  d_src holds
+ * n x 2 x layers tensor descriptors (cache 0's K0, V0, K1, V1, ..., then
+ * cache 1's), elements of src_dtype (CASCADE_KV_*; BF16 and FP32 round to
+ * FP16 to nearest even, as the reference's .to(torch.float16) does).
+ * d_dst[i] receives cache i's wire block, cascade_kv_wire_bytes() bytes:
+ * the header (dtype id 0) then K0, V0, K1, ... as contiguous
+ * [heads][seq][head_dim] FP16, the reference's bytes exactly.  16-byte
+ * aligned outputs and head_dim a multiple of 8 take the vector path; any
+ * other alignment is handled element by element. */
+int cascade_kv_serialize_batch(const cascade_kv_tensor_t *d_src,
+                               int src_dtype, uint32_t layers, uint32_t heads,
+                               uint32_t seq, uint32_t head_dim,
+                               const uint64_t *d_dst, size_t n, void *stream);
+
+/* kv_manager.deserialize_kv_cache (kv_manager.py:66-95) on the device: n
+ * wire blocks d_src[i] of one shape (the caller has read the header) into
+ * n x 2 x layers FP16 tensors d_dst (same order as serialize). */
+int cascade_kv_deserialize_batch(const uint64_t *d_src, uint32_t layers,
+                                 uint32_t heads, uint32_t seq,
+                                 uint32_t head_dim,
+                                 const cascade_kv_tensor_t *d_dst, size_t n,
+                                 void *stream);
+
 /* n device-to-device block copies in one launch (the pool copy that
  * GPUBackend::put/get do with cudaMemcpyAsync, gpu_backend.cu:298-308,
  * 362-377). */
@@ -327,8 +375,8 @@ int cascade_shard_put_begin_digests(cascade_store_t *s, size_t n,
 /* How to cut a batch of n blocks of h_sizes bytes into sharded puts that
  * each fit this rank's HBM pool: consecutive blocks whose payloads fill at
  * most 4/5 of the pool form a slice, and each slice's prepare demotes older
- * payloads to the DRAM tier.  Without a DRAM tier the batch is one slice.
- * h_cuts gets *n_slices + 1 ascending block indices from 0 to n (room for
+ * payloads to the DRAM tier.  A batch that fits the pool's free space, or
+ * any batch without a DRAM tier, is one slice.  h_cuts gets *n_slices + 1 ascending block indices from 0 to n (room for
  * max(n, 1) + 1).  Every slice is a collective put of its own: ranks that
  * have fewer slices put empty batches while the others finish. */
 int cascade_shard_put_slices(cascade_store_t *s, size_t n,
