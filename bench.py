@@ -495,6 +495,77 @@ def section_dedup(ctx, args):
             "hits_exact": total_hits == expected}
 
 
+def section_kvwire(ctx, blocks, hbm, hbm_src):
+    """The KV-cache wire format (kv_manager.serialize_kv_cache /
+    deserialize_kv_cache) on the device for the headline's blocks: each
+    2 MiB block is read as 32 layers x (K, V) x [8 heads][16 tokens][128]
+    FP16 tensors, serialised into 18-byte-header wire blocks in one launch
+    and split back into the same memory in one launch.  Checked: every
+    header, the payload of a sample against its source bytes, and the
+    round trip byte for byte."""
+    import struct
+
+    import numpy as np
+    from cascade_b200 import _lib, kvwire
+    torch = ctx.torch
+    n, bb = blocks.shape
+    L, H, S, D = 32, 8, 16, 128
+    assert bb == kvwire.wire_bytes(L, H, S, D) - kvwire.HEADER_SIZE
+    T = H * S * D * 2
+    wb = kvwire.wire_bytes(L, H, S, D)
+    pitch = (wb + 255) // 256 * 256
+    wire = torch.empty((n, pitch), dtype=torch.uint8, device=ctx.dev)
+    # descriptors: tensor j of block b at blocks[b] + j * T, strides (S*D, D)
+    base = np.arange(n, dtype=np.int64)[:, None] * bb + blocks.data_ptr() \
+        + np.arange(2 * L, dtype=np.int64)[None, :] * T
+    desc = np.stack([base.reshape(-1), np.full(base.size, S * D, np.int64),
+                     np.full(base.size, D, np.int64)], axis=1)
+    d_desc = torch.from_numpy(np.ascontiguousarray(desc)).to(ctx.dev)
+    d_wire = (torch.arange(n, dtype=torch.int64, device=ctx.dev) * pitch
+              + wire.data_ptr())
+    sample = min(64, n)
+    keep = blocks[:sample].clone()
+
+    def ser():
+        _lib.call("cascade_kv_serialize_batch", d_desc.data_ptr(), 0, L, H, S,
+                  D, d_wire.data_ptr(), n, ctx.stream)
+
+    def de():
+        _lib.call("cascade_kv_deserialize_batch", d_wire.data_ptr(), L, H, S,
+                  D, d_desc.data_ptr(), n, ctx.stream)
+
+    ser_ms, _ = ctx.timed(ser, 2, 5)
+    head = struct.pack(kvwire.HEADER_FMT, L, H, S, D, 0)
+    heads_ok = bool((wire[:, :18].cpu().numpy()
+                     == np.frombuffer(head, np.uint8)).all())
+    payload_ok = bool(torch.equal(wire[:sample, 18:18 + bb], keep))
+    blocks[:sample].zero_()
+    de_ms, _ = ctx.timed(de, 2, 5)
+    torch.cuda.synchronize()
+    round_ok = bool(torch.equal(blocks[:sample], keep))
+    del wire, d_wire, d_desc, keep
+    torch.cuda.empty_cache()
+    alg = n * (2 * bb + 18)                  # read S, write S + 18 (and back)
+    return {
+        "workload": f"{n} KV caches of llama3-8b geometry ({L} layers x (K,V) "
+                    f"x [{H}][{S}][{D}] FP16, 2 MiB) <-> kv_manager wire "
+                    "blocks (18-byte <IIIIH header + payload)",
+        "serialize_gbps": n * bb / (ser_ms * 1e-3) / 1e9,
+        "serialize_ms": ser_ms,
+        "deserialize_gbps": n * bb / (de_ms * 1e-3) / 1e9,
+        "deserialize_ms": de_ms,
+        "unit": "GB/s of FP16 KV",
+        "roofline": {"bound": "hbm", "peak": hbm, "unit": "GB/s",
+                     "algorithmic_bytes": "2 x payload + 18 per block",
+                     "serialize_frac": alg / (ser_ms * 1e-3) / 1e9 / hbm,
+                     "deserialize_frac": alg / (de_ms * 1e-3) / 1e9 / hbm,
+                     "peak_source": hbm_src},
+        "headers_equal": heads_ok, "payload_equal_sample": payload_ok,
+        "round_trip_bit_exact_sample": round_ok,
+        "launches_per_call": 1,
+    }
+
+
 def section_capped(ctx, args):
     """The llama3-70b shape with an HBM pool too small for it (SURVEY cfg5's
     capped variant, scaled to fit a short run at every GPU count): 2048 x 5
@@ -761,6 +832,8 @@ def main_ours(args):
     if world == 1 and not args.headline_only:
         extra["cfg1"] = section_cfg1(ctx, args)
         extra["sweep"] = section_sweep(ctx, args, peak_gbps.value)
+        if args.layers == 32:
+            extra["kv_wire"] = section_kvwire(ctx, blocks, hbm, hbm_src)
     if not args.headline_only:
         extra["dedup"] = section_dedup(ctx, args)
         extra["capped"] = section_capped(ctx, args)
