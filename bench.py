@@ -798,6 +798,9 @@ def main_ours(args):
     del want
 
     # ---- e2e: host buffers through the public API, the same K steps
+    kvw = None
+    if world == 1 and not args.headline_only and args.layers == 32:
+        kvw = section_kvwire(ctx, blocks, hbm, hbm_src)
     del blocks, dptrs, dsizes, digests
     torch.cuda.empty_cache()
     host_np = host.numpy()
@@ -832,8 +835,8 @@ def main_ours(args):
     if world == 1 and not args.headline_only:
         extra["cfg1"] = section_cfg1(ctx, args)
         extra["sweep"] = section_sweep(ctx, args, peak_gbps.value)
-        if args.layers == 32:
-            extra["kv_wire"] = section_kvwire(ctx, blocks, hbm, hbm_src)
+        if kvw is not None:
+            extra["kv_wire"] = kvw
     if not args.headline_only:
         extra["dedup"] = section_dedup(ctx, args)
         extra["capped"] = section_capped(ctx, args)
