@@ -139,27 +139,46 @@ __device__ uint32_t load_elem(const cascade_kv_tensor_t *ts, uint32_t e,
   return to_f16<SRC>(load_raw<SRC>(elem_addr(t, c, SRC == 2 ? 4 : 2)));
 }
 
-// Payload unit q (elements 8q .. 8q+7) as four words of FP16 pairs.
+// Address of payload element e, the first of a unit that lies inside one
+// row (head_dim % 8 == 0 and e % 8 == 0).  A tensor laid out contiguously
+// as [heads][seq][dim] needs one division; any other strides need three.
+template <int ES>
+__device__ __forceinline__ uint64_t unit_addr(const cascade_kv_tensor_t *ts,
+                                              uint32_t e, const WireGeom &g) {
+  const uint32_t seg = fdiv(e, g.dE);
+  const uint32_t r = e - seg * g.E;
+  const cascade_kv_tensor_t *t = ts + seg;
+  const uint64_t ptr = __ldg(reinterpret_cast<const unsigned long long *>(&t->ptr));
+  const int64_t sh = __ldg(reinterpret_cast<const long long *>(&t->stride_head));
+  const int64_t ss = __ldg(reinterpret_cast<const long long *>(&t->stride_seq));
+  if (ss == (int64_t)g.D && sh == (int64_t)g.SD) return ptr + (uint64_t)r * ES;
+  const uint32_t h = fdiv(r, g.dSD);
+  const uint32_t r2 = r - h * g.SD;
+  const uint32_t s = fdiv(r2, g.dD);
+  const uint32_t d = r2 - s * g.D;
+  return ptr + (uint64_t)(((int64_t)h * sh + (int64_t)s * ss + (int64_t)d) * ES);
+}
+
+// Payload unit q (elements 8q .. 8q+7) as four words of FP16 pairs, from an
+// address unit_addr gave (16-byte aligned).
 template <int SRC>
-__device__ __forceinline__ uint4 load_unit(const cascade_kv_tensor_t *ts,
-                                           uint32_t q, const WireGeom &g) {
-  const uint32_t e = q * 8;
-  if (g.vec_ok && e + 8 <= g.N) {
-    const Coord c = coord(e, g);
-    const cascade_kv_tensor_t t = ts[c.seg];
-    const uint64_t a = elem_addr(t, c, SRC == 2 ? 4 : 2);
-    if ((a & 15u) == 0) {
-      if (SRC == 0) return ld16_stream(a);
-      if (SRC == 1) {
-        const uint4 r = ld16_stream(a);
-        return make_uint4(pack2<1>(r.x, r.x >> 16), pack2<1>(r.y, r.y >> 16),
-                          pack2<1>(r.z, r.z >> 16), pack2<1>(r.w, r.w >> 16));
-      }
-      const uint4 r0 = ld16_stream(a), r1 = ld16_stream(a + 16);
-      return make_uint4(pack2<2>(r0.x, r0.y), pack2<2>(r0.z, r0.w),
-                        pack2<2>(r1.x, r1.y), pack2<2>(r1.z, r1.w));
-    }
+__device__ __forceinline__ uint4 load_unit_at(uint64_t a) {
+  if (SRC == 0) return ld16_stream(a);
+  if (SRC == 1) {
+    const uint4 r = ld16_stream(a);
+    return make_uint4(pack2<1>(r.x, r.x >> 16), pack2<1>(r.y, r.y >> 16),
+                      pack2<1>(r.z, r.z >> 16), pack2<1>(r.w, r.w >> 16));
   }
+  const uint4 r0 = ld16_stream(a), r1 = ld16_stream(a + 16);
+  return make_uint4(pack2<2>(r0.x, r0.y), pack2<2>(r0.z, r0.w),
+                    pack2<2>(r1.x, r1.y), pack2<2>(r1.z, r1.w));
+}
+
+// Payload unit q element by element (0 past the end of the payload).
+template <int SRC>
+__device__ __noinline__ uint4 load_unit_slow(const cascade_kv_tensor_t *ts,
+                                             uint32_t q, const WireGeom &g) {
+  const uint32_t e = q * 8;
   uint32_t w[4];
 #pragma unroll
   for (int j = 0; j < 4; ++j)
@@ -168,47 +187,67 @@ __device__ __forceinline__ uint4 load_unit(const cascade_kv_tensor_t *ts,
   return make_uint4(w[0], w[1], w[2], w[3]);
 }
 
-__device__ __forceinline__ void store_bytes(uint8_t *p, const uint4 &v,
-                                            uint32_t nbytes) {
-  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-  for (uint32_t i = 0; i < nbytes; ++i) p[i] = (uint8_t)(w[i >> 2] >> (8 * (i & 3)));
+__device__ __noinline__ void store_bytes(uint8_t *p, uint4 v,
+                                         uint32_t nbytes) {
+  for (uint32_t i = 0; i < nbytes; ++i) {
+    const uint32_t w = i < 4 ? v.x : i < 8 ? v.y : i < 12 ? v.z : v.w;
+    p[i] = (uint8_t)(w >> (8 * (i & 3)));
+  }
 }
 
-// One work item = kWTile output vectors of one wire block.  Vector v = 0
-// is header bytes 0..15; vector v >= 1 is header/payload bytes 16v..16v+15
-// = the last 2 bytes of payload unit v-2 (the header's dtype id for v = 1)
-// and the first 14 of unit v-1.
+// One work item = kWTile output vectors of one wire block; warp w of the
+// CTA owns kWPer x 32 consecutive vectors, 32 per step.  Vector v = 0 is
+// header bytes 0..15; vector v >= 1 is wire bytes 16v..16v+15 = the last 2
+// bytes of payload unit v-2 (the header's dtype id for v = 1) and the first
+// 14 of unit v-1.  A lane takes unit v-2's last word from the lane before
+// it; lane 0 from lane 31 of the previous step, so only a warp's first
+// vector loads it on its own.
 template <int SRC>
-__global__ void __launch_bounds__(kWThreads)
+__global__ void __launch_bounds__(kWThreads, 3)
     kv_serialize_kernel(const cascade_kv_tensor_t *__restrict__ src,
                         const uint64_t *__restrict__ dst, int n, WireGeom g) {
+  constexpr int ES = SRC == 2 ? 4 : 2;
   const int lane = threadIdx.x & 31;
+  const uint32_t wofs = (threadIdx.x >> 5) * (kWPer * 32);
   const uint64_t items = (uint64_t)n * g.tiles;
   const uint64_t wire = kHeaderBytes + 2ull * g.N;
   for (uint64_t w = blockIdx.x; w < items; w += gridDim.x) {
     const int b = (int)(w / g.tiles);
-    const uint32_t vbase = (uint32_t)(w - (uint64_t)b * g.tiles) * kWTile;
-    if (vbase >= g.vecs) continue;          // uniform across the CTA
+    const uint32_t wbase =
+        (uint32_t)(w - (uint64_t)b * g.tiles) * kWTile + wofs;
+    if (wbase >= g.vecs) continue;          // uniform across the warp
     const cascade_kv_tensor_t *ts = src + (uint64_t)b * 2 * g.L;
     uint8_t *out = reinterpret_cast<uint8_t *>(dst[b]);
     const bool out_al = ((uintptr_t)out & 15u) == 0;
+    uint64_t addr[kWPer];
+#pragma unroll
+    for (int k = 0; k < kWPer; ++k) {       // addresses, then loads
+      const uint32_t q = wbase + k * 32 + lane - 1;   // unit of vector v
+      addr[k] = 0;
+      if (g.vec_ok && q < g.units && q * 8 + 8 <= g.N) {
+        addr[k] = unit_addr<ES>(ts, q * 8, g);
+        if (addr[k] & 15u) addr[k] = 0;
+      }
+    }
     uint4 cur[kWPer];
 #pragma unroll
-    for (int k = 0; k < kWPer; ++k) {       // all loads first
-      const uint32_t v = vbase + k * kWThreads + threadIdx.x;
+    for (int k = 0; k < kWPer; ++k) {
+      const uint32_t q = wbase + k * 32 + lane - 1;
       cur[k] = make_uint4(0, 0, 0, 0);      // v = 0: unit -1 = the dtype id
-      if (v >= 1 && v - 1 < g.units) cur[k] = load_unit<SRC>(ts, v - 1, g);
+      if (addr[k]) cur[k] = load_unit_at<SRC>(addr[k]);
+      else if (q < g.units) cur[k] = load_unit_slow<SRC>(ts, q, g);
     }
+    uint32_t carry = 0;                     // lane 0: word 3 of unit v-2
+    if (lane == 0 && wbase >= 2 && wbase - 2 < g.units)
+      carry = load_elem<SRC>(ts, (wbase - 2) * 8 + 6, g) |
+              (load_elem<SRC>(ts, (wbase - 2) * 8 + 7, g) << 16);
 #pragma unroll
     for (int k = 0; k < kWPer; ++k) {
-      const uint32_t v = vbase + k * kWThreads + threadIdx.x;
-      uint32_t prev = __shfl_up_sync(0xffffffffu, cur[k].w, 1);
-      if (lane == 0) {                      // lane 31 of the previous pass
-        prev = 0;                           // v = 1: dtype id 0 in bytes 16-17
-        if (v >= 2 && v - 2 < g.units)
-          prev = load_elem<SRC>(ts, (v - 2) * 8 + 6, g) |
-                 (load_elem<SRC>(ts, (v - 2) * 8 + 7, g) << 16);
-      }
+      const uint32_t v = wbase + k * 32 + lane;
+      const uint32_t up = __shfl_up_sync(0xffffffffu, cur[k].w, 1);
+      const uint32_t last = __shfl_sync(0xffffffffu, cur[k].w, 31);
+      const uint32_t prev = lane == 0 ? carry : up;
+      carry = last;
       if (v >= g.vecs) continue;
       const uint4 o =
           v == 0 ? make_uint4(g.L, g.H, g.S, g.D)
@@ -223,72 +262,102 @@ __global__ void __launch_bounds__(kWThreads)
   }
 }
 
-// One work item = kWTile payload units of one wire block.  Unit q is wire
-// bytes 18 + 16q .. 18 + 16q + 15 = bytes 2..15 of the block's 16-byte unit
-// q+1 and bytes 0..1 of unit q+2 (the next lane's first word).
-__global__ void __launch_bounds__(kWThreads)
+// Element-wise store of payload unit q (its first `cnt` elements).
+__device__ __noinline__ void store_unit_slow(const cascade_kv_tensor_t *ts,
+                                             uint32_t e, uint32_t cnt,
+                                             uint4 o, const WireGeom &g) {
+  for (uint32_t j = 0; j < cnt; ++j) {
+    const Coord cj = coord(e + j, g);
+    const cascade_kv_tensor_t tj = ts[cj.seg];
+    const uint64_t aj = elem_addr(tj, cj, 2);
+    const uint32_t w = j < 2 ? o.x : j < 4 ? o.y : j < 6 ? o.z : o.w;
+    const uint16_t h = (uint16_t)(w >> (16 * (j & 1)));
+    if ((aj & 1u) == 0) {
+      *reinterpret_cast<uint16_t *>(aj) = h;
+    } else {
+      reinterpret_cast<uint8_t *>(aj)[0] = (uint8_t)h;
+      reinterpret_cast<uint8_t *>(aj)[1] = (uint8_t)(h >> 8);
+    }
+  }
+}
+
+// Payload unit q read byte by byte from a wire block (0 past the end).
+__device__ __noinline__ uint4 wire_unit_slow(const uint8_t *in, uint32_t e,
+                                             const WireGeom &g) {
+  uint32_t wv[4] = {0, 0, 0, 0};
+#pragma unroll
+  for (uint32_t j = 0; j < 8; ++j) {
+    if (e + j < g.N) {
+      const uint8_t *p = in + kHeaderBytes + 2ull * (e + j);
+      wv[j >> 1] |= ((uint32_t)p[0] | ((uint32_t)p[1] << 8)) << (16 * (j & 1));
+    }
+  }
+  return make_uint4(wv[0], wv[1], wv[2], wv[3]);
+}
+
+// One work item = 256 x PER payload units of one wire block; warp w of the
+// CTA owns PER x 32 consecutive units, 32 per step.  Unit q is wire bytes
+// 18 + 16q .. 18 + 16q + 15 = bytes 2..15 of the block's 16-byte unit q+1
+// and bytes 0..1 of unit q+2, which the next lane loaded (lane 31: lane 0
+// of the next step; the warp's last unit loads it on its own).
+template <int PER>
+__global__ void __launch_bounds__(kWThreads, 3)
     kv_deserialize_kernel(const uint64_t *__restrict__ src,
                           const cascade_kv_tensor_t *__restrict__ dst, int n,
                           WireGeom g) {
   const int lane = threadIdx.x & 31;
+  const uint32_t wofs = (threadIdx.x >> 5) * (PER * 32);
   const uint64_t items = (uint64_t)n * g.tiles;
   for (uint64_t w = blockIdx.x; w < items; w += gridDim.x) {
     const int b = (int)(w / g.tiles);
-    const uint32_t qbase = (uint32_t)(w - (uint64_t)b * g.tiles) * kWTile;
-    if (qbase >= g.units) continue;         // uniform across the CTA
+    const uint32_t qbase =
+        (uint32_t)(w - (uint64_t)b * g.tiles) * (kWThreads * PER) + wofs;
+    if (qbase >= g.units) continue;         // uniform across the warp
     const cascade_kv_tensor_t *ts = dst + (uint64_t)b * 2 * g.L;
     const uint8_t *in = reinterpret_cast<const uint8_t *>(src[b]);
     const bool in_al = ((uintptr_t)in & 15u) == 0;
-    uint4 a[kWPer];
+    uint4 a[PER];
 #pragma unroll
-    for (int k = 0; k < kWPer; ++k) {
-      const uint32_t q = qbase + k * kWThreads + threadIdx.x;
+    for (int k = 0; k < PER; ++k) {         // source loads first
+      const uint32_t q = qbase + k * 32 + lane;
       a[k] = make_uint4(0, 0, 0, 0);
       if (in_al && q < g.units && q * 8 + 8 <= g.N)
         a[k] = ld16_stream((uint64_t)(in + 16ull * (q + 1)));
     }
+    uint64_t daddr[PER];
 #pragma unroll
-    for (int k = 0; k < kWPer; ++k) {
-      const uint32_t q = qbase + k * kWThreads + threadIdx.x;
+    for (int k = 0; k < PER; ++k) {       // then destination addresses
+      const uint32_t q = qbase + k * 32 + lane;
+      daddr[k] = 0;
+      if (g.vec_ok && q < g.units && q * 8 + 8 <= g.N) {
+        daddr[k] = unit_addr<2>(ts, q * 8, g);
+        if (daddr[k] & 15u) daddr[k] = 0;
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < PER; ++k) {
+      const uint32_t q = qbase + k * 32 + lane;
       uint32_t nxt = __shfl_down_sync(0xffffffffu, a[k].x, 1);
+      const uint32_t first_next =
+          __shfl_sync(0xffffffffu, k + 1 < PER ? a[k + 1 < PER ? k + 1 : k].x : 0u, 0);
+      if (lane == 31) nxt = first_next;
       if (q >= g.units) continue;
       const uint32_t e = q * 8;
       const bool full = e + 8 <= g.N;
       uint4 o;
       if (in_al && full) {
-        // The next lane loaded unit q+2 only if its own unit is full.
-        if (lane == 31 || (q + 1) * 8 + 8 > g.N)
+        // The neighbour loaded unit q+2 only if its own unit is full.
+        if ((lane == 31 && k + 1 == PER) || (q + 1) * 8 + 8 > g.N)
           nxt = *reinterpret_cast<const uint16_t *>(in + 16ull * (q + 2));
         o = make_uint4(fs16(a[k].x, a[k].y), fs16(a[k].y, a[k].z),
                        fs16(a[k].z, a[k].w), fs16(a[k].w, nxt));
       } else {
-        uint32_t wv[4] = {0, 0, 0, 0};
-        for (uint32_t j = 0; j < 8 && e + j < g.N; ++j) {
-          const uint8_t *p = in + kHeaderBytes + 2ull * (e + j);
-          wv[j >> 1] |= ((uint32_t)p[0] | ((uint32_t)p[1] << 8)) << (16 * (j & 1));
-        }
-        o = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+        o = wire_unit_slow(in, e, g);
       }
-      const Coord c = coord(e, g);
-      const cascade_kv_tensor_t t = ts[c.seg];
-      const uint64_t addr = elem_addr(t, c, 2);
-      if (g.vec_ok && full && (addr & 15u) == 0) {
-        *reinterpret_cast<uint4 *>(addr) = o;
-      } else {
-        const uint32_t wv[4] = {o.x, o.y, o.z, o.w};
-        for (uint32_t j = 0; j < 8 && e + j < g.N; ++j) {
-          const Coord cj = coord(e + j, g);
-          const cascade_kv_tensor_t tj = ts[cj.seg];
-          const uint64_t aj = elem_addr(tj, cj, 2);
-          const uint16_t h = (uint16_t)(wv[j >> 1] >> (16 * (j & 1)));
-          if ((aj & 1u) == 0) {
-            *reinterpret_cast<uint16_t *>(aj) = h;
-          } else {
-            reinterpret_cast<uint8_t *>(aj)[0] = (uint8_t)h;
-            reinterpret_cast<uint8_t *>(aj)[1] = (uint8_t)(h >> 8);
-          }
-        }
-      }
+      if (daddr[k])
+        *reinterpret_cast<uint4 *>(daddr[k]) = o;
+      else
+        store_unit_slow(ts, e, full ? 8 : g.N - e, o, g);
     }
   }
 }
@@ -345,7 +414,7 @@ extern "C" int cascade_kv_serialize_batch(const cascade_kv_tensor_t *d_src,
   CB_CHECK(d_src && d_dst, CASCADE_ERR_INVALID, "null pointer argument");
   g.tiles = (uint32_t)cb::div_up(g.vecs, cb::kWTile);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const int grid = cb::grid_for((uint64_t)n * g.tiles, 1, 4);
+  const int grid = cb::grid_for((uint64_t)n * g.tiles, 1, 3);
   switch (src_dtype) {
     case CASCADE_KV_FP16:
       cb::kv_serialize_kernel<0><<<grid, cb::kWThreads, 0, s>>>(d_src, d_dst,
@@ -376,11 +445,12 @@ extern "C" int cascade_kv_deserialize_batch(const uint64_t *d_src,
   if (rc != CASCADE_OK) return rc;
   if (n == 0) return CASCADE_OK;
   CB_CHECK(d_src && d_dst, CASCADE_ERR_INVALID, "null pointer argument");
-  g.tiles = (uint32_t)cb::div_up(g.units, cb::kWTile);
+  constexpr int kPer = 6;                 // units per thread per work item
+  g.tiles = (uint32_t)cb::div_up(g.units, cb::kWThreads * kPer);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const int grid = cb::grid_for((uint64_t)n * g.tiles, 1, 4);
-  cb::kv_deserialize_kernel<<<grid, cb::kWThreads, 0, s>>>(d_src, d_dst,
-                                                           (int)n, g);
+  const int grid = cb::grid_for((uint64_t)n * g.tiles, 1, 3);
+  cb::kv_deserialize_kernel<kPer><<<grid, cb::kWThreads, 0, s>>>(d_src, d_dst,
+                                                                 (int)n, g);
   cb::count_launches(1);
   CB_CUDA(cudaGetLastError());
   return CASCADE_OK;
