@@ -235,3 +235,46 @@ def deserialize_kv_cache(data, header=None) -> tuple:
     """kv_manager.deserialize_kv_cache on the device, for a CUDA uint8 wire
     block: a tuple of per-layer (K, V) FP16 tensors [1, heads, seq, dim]."""
     return deserialize_kv_caches([data], header=header)[0]
+
+
+def store_kv_caches(store, block_ids: Sequence, caches: Sequence,
+                    is_prefix=None):
+    """KVCacheStore.store (kv_manager.py:116-127) for a batch, without host
+    copies: the caches (one shape) are serialised in one launch and put
+    under their ids (prefix hashes) with one put_batch.  ``store``: a
+    CascadeStore.  Returns the per-block put status codes."""
+    if len(block_ids) != len(caches):
+        raise ValueError("one id per cache")
+    if not caches:
+        return []
+    rows = serialize_kv_caches(caches)
+    return store.put_batch(rows, keys=list(block_ids), is_prefix=is_prefix,
+                           return_status=True)[1]
+
+
+def load_kv_caches(store, block_ids: Sequence, layers: int, heads: int,
+                   seq: int, head_dim: int, device=None) -> list:
+    """KVCacheStore.load (kv_manager.py:135-156) for a batch of caches of a
+    known shape, without host copies: one get_batch into a staging buffer
+    on the GPU and one deserialize launch.  Returns, per id, the tuple of
+    (K, V) per layer, or None when the store does not hold that id with the
+    wire size of that shape."""
+    import torch
+    n = len(block_ids)
+    if n == 0:
+        return []
+    dev = torch.device(device if device is not None
+                       else f"cuda:{store._device}")
+    nbytes = wire_bytes(layers, heads, seq, head_dim)
+    pitch = -(-nbytes // ROW_ALIGN) * ROW_ALIGN
+    stage = torch.empty((n, pitch), dtype=torch.uint8, device=dev)
+    rows = [stage[i, :nbytes] for i in range(n)]
+    found, sizes = store.get_batch([store._key(b) for b in block_ids], rows)
+    hit = [i for i in range(n) if found[i] and int(sizes[i]) == nbytes]
+    out = [None] * n
+    if hit:
+        shape = (layers, heads, seq, head_dim, FP16_ID)
+        caches = deserialize_kv_caches([rows[i] for i in hit], header=shape)
+        for i, c in zip(hit, caches):
+            out[i] = c
+    return out

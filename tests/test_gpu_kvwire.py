@@ -202,3 +202,30 @@ def test_rejects_bad_shapes():
                                  b"\x02\0"), dtype=torch.uint8)
     with pytest.raises(ValueError):           # dtype id 2 is not written
         kvwire.deserialize_kv_cache(bad)
+
+
+def test_store_and_load_batches_of_caches():
+    """store_kv_caches / load_kv_caches: KVCacheStore.store / load for a
+    batch; a blob the reference's host path put reads back too."""
+    cfg = cc.CascadeConfig()
+    cfg.gpu_capacity_bytes = 64 << 20
+    cfg.shm_capacity_bytes = 16 << 20
+    store = cc.CascadeStore(cfg)
+    try:
+        shape = (4, 8, 13, 128)
+        caches = [_cache(40 + i, *shape) for i in range(5)]
+        st = kvwire.store_kv_caches(store, [f"p{i}" for i in range(5)], caches)
+        assert (np.asarray(st) == 0).all()
+        host = np.frombuffer(_oracle_bytes(caches[0]), np.uint8).copy()
+        assert store.put("from-host", host)
+        got = kvwire.load_kv_caches(store, ["p3", "missing", "from-host", "p0"],
+                                    *shape)
+        assert got[1] is None
+        for g, c in ((got[0], caches[3]), (got[2], caches[0]),
+                     (got[3], caches[0])):
+            for (k, v), (k0, v0) in zip(g, c):
+                assert torch.equal(k, k0) and torch.equal(v, v0)
+        # another shape under an id: not this wire size, so not loaded
+        assert kvwire.load_kv_caches(store, ["p1"], 4, 8, 12, 128) == [None]
+    finally:
+        store.close()
