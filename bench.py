@@ -543,6 +543,44 @@ def section_kvwire(ctx, blocks, hbm, hbm_src):
     de_ms, _ = ctx.timed(de, 2, 5)
     torch.cuda.synchronize()
     round_ok = bool(torch.equal(blocks[:sample], keep))
+
+    # KVCacheStore.load of the whole batch from a raw-format store: one
+    # cascade_store_get_kv_batch (lookup, then every wire block split
+    # straight out of the pool), against get_batch + deserialize.
+    from cascade_b200 import cascade_cpp as cc
+    # (2 MiB + 18 bytes rounds up to the pool's 2.25 MiB size class)
+    store = cc.CascadeStore(make_cfg(cc, ctx.local,
+                                     int(n * pitch * 1.13) + (256 << 20),
+                                     q8=False, shm=0, slots=1 << 15))
+    keys = np.random.default_rng(SEED).integers(
+        0, 256, (n, 16), dtype=np.uint8)
+    keys[:, 15] = 0x5a                       # clear of the reserved key region
+    wptrs = np.arange(n, dtype=np.uint64) * np.uint64(pitch) \
+        + np.uint64(wire.data_ptr())
+    st = store._put_batch_raw(n, wptrs, np.full(n, wb, np.uint64),
+                              [bytes(k) for k in keys], None, True,
+                              ctx.stream)[1]
+    assert (st == 0).all()
+    found = np.zeros(n, np.uint8)
+    nf = ctypes.c_uint64(0)
+    kflat = np.ascontiguousarray(keys).reshape(-1)
+
+    def load():
+        _lib.call("cascade_store_get_kv_batch", store._h, n,
+                  kflat.ctypes.data, L, H, S, D, d_desc.data_ptr(),
+                  found.ctypes.data, ctx.stream, ctypes.byref(nf))
+
+    blocks[:sample].zero_()
+    load_ms, _ = ctx.timed(load, 2, 5)
+    load_ok = bool(found.all()) and bool(torch.equal(blocks[:sample], keep))
+    caps = np.full(n, pitch, np.uint64)
+
+    def get_then_split():
+        store._get_batch_raw(n, kflat, wptrs, caps, ctx.stream)
+        de()
+
+    two_ms, _ = ctx.timed(get_then_split, 2, 5)
+    store.close()
     del wire, d_wire, d_desc, keep
     torch.cuda.empty_cache()
     alg = n * (2 * bb + 18)                  # read S, write S + 18 (and back)
@@ -563,6 +601,13 @@ def section_kvwire(ctx, blocks, hbm, hbm_src):
         "headers_equal": heads_ok, "payload_equal_sample": payload_ok,
         "round_trip_bit_exact_sample": round_ok,
         "launches_per_call": 1,
+        "load": {"what": "KVCacheStore.load of every cache from a raw HBM "
+                         "store: cascade_store_get_kv_batch (lookup + split "
+                         "straight out of the pool)",
+                 "gbps": n * bb / (load_ms * 1e-3) / 1e9, "ms": load_ms,
+                 "frac": alg / (load_ms * 1e-3) / 1e9 / hbm,
+                 "get_then_deserialize_ms": two_ms,
+                 "bit_exact_sample": load_ok},
     }
 
 

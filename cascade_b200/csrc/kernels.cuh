@@ -5,6 +5,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "cascade_b200.h"
+
 namespace cb {
 
 // Unused shared memory (bytes per CTA) that a kernel running beside a
@@ -62,6 +64,13 @@ int launch_dequantize(const uint64_t *d_srcs, const uint8_t *d_headers,
 int launch_copy(const uint64_t *d_srcs, const uint64_t *d_dsts,
                 const uint64_t *d_sizes, int n, uint64_t max_size,
                 cudaStream_t s, size_t smem_pad = 0);
+
+// kv_manager wire blocks d_src[i] (null: skipped) into 2 x layers FP16
+// tensors each (cascade_kv_deserialize_batch).
+int launch_kv_deserialize(const uint64_t *d_src, uint32_t layers,
+                          uint32_t heads, uint32_t seq, uint32_t head_dim,
+                          const cascade_kv_tensor_t *d_dst, int n,
+                          cudaStream_t s);
 
 // out[i] = in[i] + delta
 int launch_offset_ptrs(const uint64_t *d_in, uint64_t delta, uint64_t *d_out,

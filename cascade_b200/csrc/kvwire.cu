@@ -315,6 +315,7 @@ __global__ void __launch_bounds__(kWThreads, 3)
     if (qbase >= g.units) continue;         // uniform across the warp
     const cascade_kv_tensor_t *ts = dst + (uint64_t)b * 2 * g.L;
     const uint8_t *in = reinterpret_cast<const uint8_t *>(src[b]);
+    if (!in) continue;                      // a block this call skips
     const bool in_al = ((uintptr_t)in & 15u) == 0;
     uint4 a[PER];
 #pragma unroll
@@ -433,6 +434,26 @@ extern "C" int cascade_kv_serialize_batch(const cascade_kv_tensor_t *d_src,
   return CASCADE_OK;
 }
 
+namespace cb {
+
+int launch_kv_deserialize(const uint64_t *d_src, uint32_t layers,
+                          uint32_t heads, uint32_t seq, uint32_t head_dim,
+                          const cascade_kv_tensor_t *d_dst, int n,
+                          cudaStream_t s) {
+  WireGeom g;
+  int rc = make_geom(layers, heads, seq, head_dim, &g);
+  if (rc != CASCADE_OK || n <= 0) return rc;
+  constexpr int kPer = 6;                 // units per thread per work item
+  g.tiles = (uint32_t)div_up(g.units, kWThreads * kPer);
+  const int grid = grid_for((uint64_t)n * g.tiles, 1, 3);
+  kv_deserialize_kernel<kPer><<<grid, kWThreads, 0, s>>>(d_src, d_dst, n, g);
+  count_launches(1);
+  CB_CUDA(cudaGetLastError());
+  return CASCADE_OK;
+}
+
+}  // namespace cb
+
 extern "C" int cascade_kv_deserialize_batch(const uint64_t *d_src,
                                             uint32_t layers, uint32_t heads,
                                             uint32_t seq, uint32_t head_dim,
@@ -445,13 +466,6 @@ extern "C" int cascade_kv_deserialize_batch(const uint64_t *d_src,
   if (rc != CASCADE_OK) return rc;
   if (n == 0) return CASCADE_OK;
   CB_CHECK(d_src && d_dst, CASCADE_ERR_INVALID, "null pointer argument");
-  constexpr int kPer = 6;                 // units per thread per work item
-  g.tiles = (uint32_t)cb::div_up(g.units, cb::kWThreads * kPer);
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const int grid = cb::grid_for((uint64_t)n * g.tiles, 1, 3);
-  cb::kv_deserialize_kernel<kPer><<<grid, cb::kWThreads, 0, s>>>(d_src, d_dst,
-                                                                 (int)n, g);
-  cb::count_launches(1);
-  CB_CUDA(cudaGetLastError());
-  return CASCADE_OK;
+  return cb::launch_kv_deserialize(d_src, layers, heads, seq, head_dim, d_dst,
+                                   (int)n, static_cast<cudaStream_t>(stream));
 }

@@ -161,6 +161,10 @@ struct Store {
   size_t d_q8stage_cap = 0;
   uint8_t *d_evstage = nullptr;  // INT8 forms of blocks being demoted
   size_t d_evstage_cap = 0;
+  uint8_t *d_kvstage = nullptr;  // wire blocks a KV-cache get decodes first
+  size_t d_kvstage_cap = 0;
+  uint8_t *d_kvsrc = nullptr;    // wire-block addresses of a KV-cache get
+  size_t d_kvsrc_cap = 0;
   uint8_t *scan_d = nullptr;     // demotion-candidate histogram and list
   size_t scan_cap = 0;           // bytes
   // Copy streams between the device and the DRAM tier: [0] device to
@@ -1515,6 +1519,90 @@ static int get_batch_locked(Store &st, size_t n, const uint8_t *h_keys,
   return deliver_locked(st, n, out.data(), deliver.data());
 }
 
+// get_batch of blocks that hold kv_manager wire blocks of one shape, split
+// into the caller's K/V tensors.  Raw HBM hits are split straight out of
+// the pool (one pass over their bytes), before deliver_locked's promotions
+// can move anything; other hits (DRAM tier, INT8) are delivered into a
+// staging buffer first and split from there.  Blocks of another size are
+// reported not found and count neither hit nor miss, as a get into a
+// buffer too small for them does.
+static int get_kv_batch_locked(Store &st, size_t n, const uint8_t *h_keys,
+                               const uint32_t shape[4],
+                               const cascade_kv_tensor_t *d_dst,
+                               uint8_t *h_found, uint64_t *n_found) {
+  const uint64_t wb = cascade_kv_wire_bytes(shape[0], shape[1], shape[2],
+                                            shape[3]);
+  int rc = ensure_scratch(st, n);
+  if (!rc) rc = upload_keys(st, n, h_keys);
+  if (!rc) rc = lookup_locked(st, n, true);
+  if (rc) return rc;
+  for (size_t i = 0; i < n; ++i)
+    CB_CHECK(!(st.sc.h_info[i].found && (st.sc.h_info[i].flags & kFlagRemote)),
+             CASCADE_ERR_UNSUPPORTED,
+             "block is held by another rank of a sharded store: read it on "
+             "its holder");
+  const uint64_t pitch = (wb + 255) & ~uint64_t(255);
+  std::vector<uint64_t> direct(n, 0), staged(n, 0), out(n, 0);
+  std::vector<uint8_t> deliver(n, 0);
+  size_t nstage = 0, ndirect = 0;
+  uint64_t found = 0;
+  for (size_t i = 0; i < n; ++i) {
+    const LookupInfo &f = st.sc.h_info[i];
+    if (!f.found) {               // counted as a miss by deliver_locked
+      deliver[i] = 1;
+      h_found[i] = 0;
+      continue;
+    }
+    const bool q8 = (f.flags & kFlagQ8) != 0;
+    const uint64_t size = q8 ? 2 * (f.size / 2) : f.size;
+    h_found[i] = size == wb ? 1 : 0;
+    if (size != wb) continue;
+    ++found;
+    if ((f.flags & kTierHbm) && !q8) {
+      direct[i] = (uint64_t)(uintptr_t)st.pool + f.offset;
+      ++ndirect;
+      ++st.gpu_hits;
+    } else {
+      deliver[i] = 1;
+      out[i] = nstage++;          // staging slot, made an address below
+    }
+  }
+  if (n_found) *n_found = found;
+  cudaStream_t s = st.s;
+  if ((rc = ensure_device_buf(st.d_kvsrc, st.d_kvsrc_cap, 2 * n * 8, s)))
+    return rc;
+  uint64_t *d_direct = reinterpret_cast<uint64_t *>(st.d_kvsrc);
+  uint64_t *d_staged = d_direct + n;
+  if (ndirect) {
+    // Pageable source: the copy has read `direct` when the call returns.
+    CB_CUDA(cudaMemcpyAsync(d_direct, direct.data(), n * 8,
+                            cudaMemcpyHostToDevice, s));
+    if ((rc = launch_kv_deserialize(d_direct, shape[0], shape[1], shape[2],
+                                    shape[3], d_dst, (int)n, s)))
+      return rc;
+  }
+  if (nstage) {
+    if ((rc = ensure_device_buf(st.d_kvstage, st.d_kvstage_cap,
+                                nstage * pitch, s)))
+      return rc;
+    for (size_t i = 0; i < n; ++i)
+      if (deliver[i] && st.sc.h_info[i].found) {
+        out[i] = (uint64_t)(uintptr_t)st.d_kvstage + out[i] * pitch;
+        staged[i] = out[i];
+      }
+  }
+  // Misses and staged hits: counters, copies / decodes, promotions.
+  if ((rc = deliver_locked(st, n, out.data(), deliver.data()))) return rc;
+  if (nstage) {
+    CB_CUDA(cudaMemcpyAsync(d_staged, staged.data(), n * 8,
+                            cudaMemcpyHostToDevice, s));
+    if ((rc = launch_kv_deserialize(d_staged, shape[0], shape[1], shape[2],
+                                    shape[3], d_dst, (int)n, s)))
+      return rc;
+  }
+  return CASCADE_OK;
+}
+
 // ---------------------------------------------------------- index growth
 namespace {
 
@@ -1670,6 +1758,8 @@ static void destroy_store(Store *st) {
   if (st->h_stage) cudaFreeHost(st->h_stage);
   if (st->d_q8stage) cudaFree(st->d_q8stage);
   if (st->d_evstage) cudaFree(st->d_evstage);
+  if (st->d_kvstage) cudaFree(st->d_kvstage);
+  if (st->d_kvsrc) cudaFree(st->d_kvsrc);
   if (st->scan_d) cudaFree(st->scan_d);
   if (st->sha_state) cudaFree(st->sha_state);
   for (cudaEvent_t e : {st->ev, st->ev2, st->ev3, st->dma_start})
@@ -2927,6 +3017,26 @@ extern "C" int cascade_store_get_batch(cascade_store_t *s, size_t n,
   if (int rc = join_caller(st, stream)) return rc;
   return cb::get_batch_locked(st, n, h_keys, h_out_ptrs, h_out_caps, h_sizes,
                               h_found, n_found);
+}
+
+extern "C" int cascade_store_get_kv_batch(
+    cascade_store_t *s, size_t n, const uint8_t *h_keys, uint32_t layers,
+    uint32_t heads, uint32_t seq, uint32_t head_dim,
+    const cascade_kv_tensor_t *d_dst, uint8_t *h_found, void *stream,
+    uint64_t *n_found) {
+  STORE_ENTRY(s);
+  if (n_found) *n_found = 0;
+  if (n == 0) return CASCADE_OK;
+  CB_CHECK(h_keys && d_dst && h_found, CASCADE_ERR_INVALID, "null argument");
+  CB_CHECK(n <= (size_t)INT32_MAX, CASCADE_ERR_INVALID, "batch too large");
+  CB_CHECK(layers && heads && seq && head_dim, CASCADE_ERR_INVALID,
+           "layers, heads, seq_len and head_dim must be positive");
+  if (int rc = join_caller(st, stream)) return rc;
+  const uint32_t shape[4] = {layers, heads, seq, head_dim};
+  int rc = cb::get_kv_batch_locked(st, n, h_keys, shape, d_dst, h_found,
+                                   n_found);
+  if (rc) return rc;
+  return cb::join_back(st, stream);
 }
 
 extern "C" int cascade_shard_put_begin(cascade_store_t *s, size_t n,

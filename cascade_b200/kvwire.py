@@ -15,7 +15,10 @@ goes from `past_key_values` to the HBM pool and back without a host copy:
     past_key_values = kvwire.deserialize_kv_cache(buf[:size])
 
 The bytes are the reference's exactly, so blocks stored by the reference's
-host path and by this one read back through either.
+host path and by this one read back through either.  A store with
+kv_compression quantises a blob whole, header included (the reference's
+KVCompressor does the same), so a cache read back from INT8 storage is split
+by a shape the caller knows (load_kv_caches, or `header=`).
 """
 from __future__ import annotations
 
@@ -46,6 +49,9 @@ _lib.register("cascade_kv_serialize_batch", _int,
               [_vp, _int, _u32, _u32, _u32, _u32, _vp, _sz, _vp])
 _lib.register("cascade_kv_deserialize_batch", _int,
               [_vp, _u32, _u32, _u32, _u32, _vp, _sz, _vp])
+_lib.register("cascade_store_get_kv_batch", _int,
+              [_vp, _sz, _vp, _u32, _u32, _u32, _u32, _vp, _vp, _vp,
+               ctypes.POINTER(ctypes.c_uint64)])
 
 
 def wire_bytes(layers: int, heads: int, seq: int, head_dim: int) -> int:
@@ -253,28 +259,31 @@ def store_kv_caches(store, block_ids: Sequence, caches: Sequence,
 
 
 def load_kv_caches(store, block_ids: Sequence, layers: int, heads: int,
-                   seq: int, head_dim: int, device=None) -> list:
+                   seq: int, head_dim: int) -> list:
     """KVCacheStore.load (kv_manager.py:135-156) for a batch of caches of a
-    known shape, without host copies: one get_batch into a staging buffer
-    on the GPU and one deserialize launch.  Returns, per id, the tuple of
-    (K, V) per layer, or None when the store does not hold that id with the
-    wire size of that shape."""
+    known shape, without host copies, in one store call
+    (cascade_store_get_kv_batch): raw blocks in HBM are split straight out
+    of the pool into fresh per-layer tensors.  Returns, per id, the tuple of
+    (K, V) FP16 tensors [1, heads, seq, dim] per layer, or None when the
+    store does not hold that id with the wire size of that shape."""
+    import numpy as np
     import torch
     n = len(block_ids)
     if n == 0:
         return []
-    dev = torch.device(device if device is not None
-                       else f"cuda:{store._device}")
-    nbytes = wire_bytes(layers, heads, seq, head_dim)
-    pitch = -(-nbytes // ROW_ALIGN) * ROW_ALIGN
-    stage = torch.empty((n, pitch), dtype=torch.uint8, device=dev)
-    rows = [stage[i, :nbytes] for i in range(n)]
-    found, sizes = store.get_batch([store._key(b) for b in block_ids], rows)
-    hit = [i for i in range(n) if found[i] and int(sizes[i]) == nbytes]
-    out = [None] * n
-    if hit:
-        shape = (layers, heads, seq, head_dim, FP16_ID)
-        caches = deserialize_kv_caches([rows[i] for i in hit], header=shape)
-        for i, c in zip(hit, caches):
-            out[i] = c
-    return out
+    dev = torch.device(f"cuda:{store._device}")
+    L, H, S, D = layers, heads, seq, head_dim
+    outs = torch.empty((n, L, 2, 1, H, S, D), dtype=torch.float16,
+                       device=dev)
+    views = [outs[i, l, kv, 0] for i in range(n) for l in range(L)
+             for kv in range(2)]
+    dst = _descriptors(views, dev)
+    keys = np.frombuffer(b"".join(store._key(b) for b in block_ids),
+                         dtype=np.uint8).copy()
+    found = np.zeros(n, np.uint8)
+    nf = ctypes.c_uint64(0)
+    check(_lib.load().cascade_store_get_kv_batch(
+        store._h, n, keys.ctypes.data, L, H, S, D, dst.data_ptr(),
+        found.ctypes.data, _stream(dev), ctypes.byref(nf)))
+    return [tuple((outs[i, l, 0], outs[i, l, 1]) for l in range(L))
+            if found[i] else None for i in range(n)]

@@ -301,6 +301,23 @@ int cascade_store_get_batch(cascade_store_t *s, size_t n,
                             uint8_t *h_found, void *stream,
                             uint64_t *n_found);
 
+/* KVCacheStore.load (inference_benchmark/kv_manager.py:135-156) for n keys
+ * whose blocks are kv_manager wire blocks of one shape: get_batch and
+ * deserialize_kv_cache in one call, into the caller's 2 x layers FP16
+ * tensors per key (d_dst, as cascade_kv_deserialize_batch).  Raw blocks in
+ * HBM are split straight out of the pool, one pass over their bytes; DRAM
+ * or INT8 blocks are decoded into a staging buffer first (and promoted as
+ * get_batch promotes).  h_found[i] = 1 when key i holds a block of exactly
+ * cascade_kv_wire_bytes(); a block of another size is left alone and
+ * counts neither hit nor miss.  The split is ordered on `stream`; the
+ * lookup is synchronous. */
+int cascade_store_get_kv_batch(cascade_store_t *s, size_t n,
+                               const uint8_t *h_keys, uint32_t layers,
+                               uint32_t heads, uint32_t seq, uint32_t head_dim,
+                               const cascade_kv_tensor_t *d_dst,
+                               uint8_t *h_found, void *stream,
+                               uint64_t *n_found);
+
 /* ------------------------------------------------------------------ */
 /* Sharded dedup across the GPUs of one box (one rank per GPU).         */
 /* The reference keeps one replicated dedup set per node, synchronised  */

@@ -229,3 +229,48 @@ def test_store_and_load_batches_of_caches():
         assert kvwire.load_kv_caches(store, ["p1"], 4, 8, 12, 128) == [None]
     finally:
         store.close()
+
+
+def test_load_through_the_dram_tier_and_int8():
+    """load_kv_caches for blocks the fused pool path cannot split: raw
+    blocks demoted to the DRAM tier (exact), and INT8 blocks in HBM (equal
+    to what get + deserialize return)."""
+    shape = (4, 8, 16, 128)                      # 256 KiB + 18 per cache
+    caches = [_cache(70 + i, *shape) for i in range(6)]
+    ids = [f"c{i}" for i in range(6)]
+    cfg = cc.CascadeConfig()
+    cfg.gpu_capacity_bytes = 3 * (kvwire.wire_bytes(*shape) + 4096)
+    cfg.shm_capacity_bytes = 16 << 20
+    store = cc.CascadeStore(cfg)
+    try:
+        kvwire.store_kv_caches(store, ids, caches)
+        assert store.get_stats().gpu_evictions > 0
+        got = kvwire.load_kv_caches(store, ids, *shape)
+        for g, c in zip(got, caches):
+            for (k, v), (k0, v0) in zip(g, c):
+                assert torch.equal(k, k0) and torch.equal(v, v0)
+        s = store.get_stats()
+        assert s.gpu_hits + s.shm_hits == 6 and s.shm_hits > 0
+    finally:
+        store.close()
+    cfg = cc.CascadeConfig()
+    cfg.gpu_capacity_bytes = 64 << 20
+    cfg.shm_capacity_bytes = 16 << 20
+    cfg.kv_compression = True
+    cfg.gpu_q8 = True
+    store = cc.CascadeStore(cfg)
+    try:
+        kvwire.store_kv_caches(store, ids[:3], caches[:3])
+        got = kvwire.load_kv_caches(store, ids[:3], *shape)
+        buf = torch.empty(kvwire.wire_bytes(*shape), dtype=torch.uint8,
+                          device=DEV)
+        for i in range(3):
+            assert store.get(ids[i], buf)[0]
+            # INT8 storage quantises the header with the payload (as the
+            # reference's KVCompressor does): the shape comes from the caller
+            want = kvwire.deserialize_kv_cache(buf, header=shape + (0,))
+            for (k, v), (k0, v0) in zip(got[i], want):   # bits (NaNs too)
+                assert torch.equal(k.view(torch.int16), k0.view(torch.int16))
+                assert torch.equal(v.view(torch.int16), v0.view(torch.int16))
+    finally:
+        store.close()
