@@ -118,3 +118,28 @@ def test_cascade_package_helpers(callers):
     out = np.empty(x.size, np.uint8)
     assert store.get(bid, out) == (True, x.size)
     assert np.array_equal(out, x)
+
+
+def test_reference_store_device_load_and_back(callers):
+    """The reference's KVCacheStore.store (host serialisation) and this
+    library's device path on one store: kvwire.load_kv_caches reads what
+    the reference stored, and the reference's load reads what
+    kvwire.store_kv_caches stored."""
+    from cascade_b200 import kvwire
+    ca, kv, conf = callers["adapter"], callers["kv"], callers["config"]
+    adapter = ca.CascadeAdapter({"use_gpu": True, "gpu_capacity_gb": 0.25,
+                                 "shm_capacity_gb": 0.5})
+    assert adapter.initialize()
+    store = kv.KVCacheStore(adapter, conf.ModelConfig())
+    past = _kv_cache(11)
+    assert store.store("a" * 32, past)
+    got = kvwire.load_kv_caches(adapter.store, ["a" * 32], 4, 8, 37, 128)[0]
+    for (k0, v0), (k1, v1) in zip(past, got):
+        assert torch.equal(k0, k1) and torch.equal(v0, v1)
+    other = _kv_cache(12)
+    st = kvwire.store_kv_caches(adapter.store, ["b" * 32], [other])
+    assert int(st[0]) == 0
+    back = store.load("b" * 32, device=torch.device("cuda:0"))
+    for (k0, v0), (k1, v1) in zip(other, back):
+        assert torch.equal(k0, k1) and torch.equal(v0, v1)
+    adapter.close()
