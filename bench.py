@@ -849,7 +849,6 @@ def main_ours(args):
     del blocks, dptrs, dsizes, digests
     torch.cuda.empty_cache()
     host_np = host.numpy()
-    rows = [host_np[i] for i in range(n)]
     if world > 1:
         def e2e_step():
             sharded.clear()
@@ -857,7 +856,7 @@ def main_ours(args):
     else:
         def e2e_step():
             store.clear()
-            return store.put_batch_host(rows)
+            return store.put_batch_host(host_np)
 
     e2e_ms, got = ctx.timed(e2e_step, 1, args.steps)
     assert got == n
@@ -874,7 +873,7 @@ def main_ours(args):
     if world > 1:
         sharded.close()       # every rank unmaps the peers' pools first
     store.close()
-    del host, host_np, rows
+    del host, host_np
     torch.cuda.empty_cache()
     extra = {}
     if world == 1 and not args.headline_only:
@@ -962,8 +961,9 @@ def main_ours(args):
         "e2e": {"value": e2e_value, "unit": UNIT,
                 "h2d_bytes_per_step": total, "d2h_bytes_per_step": n * 33,
                 "steps": args.steps,
-                "api": ("CascadeStore.put_batch_host (pinned host blocks, "
-                        "striped H2D with hashing under the copy)")
+                "api": ("CascadeStore.put_batch_host (one 2-D pinned host "
+                        "array of blocks, striped H2D with hashing under the "
+                        "copy)")
                 if world == 1 else
                 ("ShardedCascadeStore.put_batch_host (pinned host blocks, "
                  "striped H2D with hashing under the copy, per rank)"),

@@ -343,11 +343,22 @@ class CascadeStore:
     def put_batch_host(self, blocks: Sequence, keys=None, is_prefix=None,
                        return_status: bool = False):
         """Stores host blocks (numpy uint8 arrays, pinned or not) in one call;
-        the library moves them to the GPU.  Same results as put_batch."""
-        arrs = [_host_u8(b) for b in blocks]
-        n = len(arrs)
-        ptrs = np.array([a.ctypes.data for a in arrs], dtype=np.uint64)
-        sizes = np.array([a.size for a in arrs], dtype=np.uint64)
+        the library moves them to the GPU.  Same results as put_batch.
+        ``blocks``: a sequence of arrays, or one 2-D uint8 array with a
+        block per row (described without a per-block Python step)."""
+        if (isinstance(blocks, np.ndarray) and blocks.ndim == 2
+                and blocks.dtype == np.uint8 and blocks.strides[1] == 1):
+            n = blocks.shape[0]
+            ptrs = (np.arange(n, dtype=np.uint64)
+                    * np.uint64(blocks.strides[0])
+                    + np.uint64(blocks.ctypes.data))
+            sizes = np.full(n, blocks.shape[1], np.uint64)
+            arrs = blocks                   # keeps the rows alive
+        else:
+            arrs = [_host_u8(b) for b in blocks]
+            n = len(arrs)
+            ptrs = np.array([a.ctypes.data for a in arrs], dtype=np.uint64)
+            sizes = np.array([a.size for a in arrs], dtype=np.uint64)
         kbuf = None
         if keys is not None:
             kbuf = np.frombuffer(b"".join(self._key(k) for k in keys),

@@ -288,11 +288,13 @@ def test_cuda_tensor_put_get_by_name():
     assert torch.equal(out, t)
 
 
+@pytest.mark.parametrize("form", ["rows", "2d"])
 @pytest.mark.parametrize("size", [1000, 65536 + 100, (2 << 20) + 100])
-def test_host_batch_striped_uniform_pinned(size):
+def test_host_batch_striped_uniform_pinned(size, form):
     """Equal-size blocks in one pinned array stream to the GPU in stripes
     while SHA-256 advances stripe by stripe; the result must equal hashing
-    whole blocks (OpenSSL) and store the same bytes."""
+    whole blocks (OpenSSL) and store the same bytes.  The blocks are passed
+    as a list of rows or as the 2-D array itself."""
     n = 24
     rng = np.random.default_rng(size)
     host = torch.from_numpy(rng.integers(0, 256, (n, size), dtype=np.uint8)).pin_memory()
@@ -300,7 +302,8 @@ def test_host_batch_striped_uniform_pinned(size):
     rows[5] = rows[2]                       # a duplicate inside the batch
     host.numpy()[5] = host.numpy()[2]
     st = make_store(use_gpu=True, gpu_cap=256 << 20)
-    stored, status, digests = st.put_batch_host(rows, return_status=True)
+    stored, status, digests = st.put_batch_host(
+        rows if form == "rows" else host.numpy(), return_status=True)
     assert stored == n
     assert status[5] == 2 and (np.delete(status, 5) == 0).all()
     for i in range(n):
