@@ -22,9 +22,8 @@
 // access ever leaves the tensors' and blocks' own bytes.
 #include <cuda_fp16.h>
 
-#include <cstring>
-
 #include "common.cuh"
+#include "kernels.cuh"
 
 namespace cb {
 
