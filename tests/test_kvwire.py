@@ -98,3 +98,22 @@ def test_serialize_refuses_host_tensors():
     kv = ((torch.zeros(1, 2, 3, 8, dtype=torch.float16),) * 2,)
     with pytest.raises(ValueError):
         kvwire.serialize_kv_cache(kv)
+
+
+def test_batch_helpers_check_arguments_without_a_gpu():
+    class NoStore:
+        _device = 0
+    assert kvwire.load_kv_caches(NoStore(), [], 1, 1, 1, 8) == []
+    assert kvwire.store_kv_caches(NoStore(), [], []) == []
+    assert kvwire.serialize_kv_caches([]) == []
+    assert kvwire.deserialize_kv_caches([]) == []
+    with pytest.raises(ValueError):
+        kvwire.store_kv_caches(NoStore(), ["a"], [])
+
+
+def test_read_header_of_host_bytes():
+    head = struct.pack("<IIIIH", 32, 8, 16, 128, 0) + b"\0" * 4
+    assert kvwire.read_header(np.frombuffer(head, np.uint8)) == (32, 8, 16,
+                                                                128, 0)
+    with pytest.raises(ValueError):
+        kvwire.read_header(np.zeros(5, np.uint8))
