@@ -557,13 +557,28 @@ def section_kvwire(ctx, blocks, hbm, hbm_src):
     keys[:, 15] = 0x5a                       # clear of the reserved key region
     wptrs = np.arange(n, dtype=np.uint64) * np.uint64(pitch) \
         + np.uint64(wire.data_ptr())
-    st = store._put_batch_raw(n, wptrs, np.full(n, wb, np.uint64),
-                              [bytes(k) for k in keys], None, True,
-                              ctx.stream)[1]
-    assert (st == 0).all()
+    klist = [bytes(k) for k in keys]
+    kflat = np.ascontiguousarray(keys).reshape(-1)
+    status = np.zeros(n, np.uint8)
+    nst = ctypes.c_uint64(0)
+
+    def put_fused():          # KVCacheStore.store: one store call
+        store.clear()
+        _lib.call("cascade_store_put_kv_batch", store._h, n,
+                  kflat.ctypes.data, L, H, S, D, d_desc.data_ptr(), 0, None,
+                  status.ctypes.data, ctx.stream, ctypes.byref(nst))
+
+    def put_two_step():       # serialise, then put_batch of the wire blocks
+        store.clear()
+        ser()
+        store._put_batch_raw(n, wptrs, np.full(n, wb, np.uint64), klist,
+                             None, False, ctx.stream)
+
+    two_put_ms, _ = ctx.timed(put_two_step, 1, 3)
+    put_ms, _ = ctx.timed(put_fused, 1, 3)
+    assert (status == 0).all() and nst.value == n
     found = np.zeros(n, np.uint8)
     nf = ctypes.c_uint64(0)
-    kflat = np.ascontiguousarray(keys).reshape(-1)
 
     def load():
         _lib.call("cascade_store_get_kv_batch", store._h, n,
@@ -601,6 +616,12 @@ def section_kvwire(ctx, blocks, hbm, hbm_src):
         "headers_equal": heads_ok, "payload_equal_sample": payload_ok,
         "round_trip_bit_exact_sample": round_ok,
         "launches_per_call": 1,
+        "store": {"what": "KVCacheStore.store of every cache into an "
+                          "emptied raw HBM store: cascade_store_put_kv_batch "
+                          "(each cache serialised straight into its pool "
+                          "slot, keyed index insert)",
+                  "gbps": n * bb / (put_ms * 1e-3) / 1e9, "ms": put_ms,
+                  "serialize_then_put_batch_ms": two_put_ms},
         "load": {"what": "KVCacheStore.load of every cache from a raw HBM "
                          "store: cascade_store_get_kv_batch (lookup + split "
                          "straight out of the pool)",

@@ -15,6 +15,7 @@ LIB_PATH = os.path.join(HERE, "libcascade_b200.so")
 HEADER_PATH = os.path.join(os.path.dirname(HERE), "include", "cascade_b200.h")
 
 CASCADE_OK = 0
+CASCADE_ERR_UNSUPPORTED = 6
 PUT_STORED, PUT_DUP_KNOWN, PUT_DUP_BATCH, PUT_FAILED = 0, 1, 2, 3
 
 _u8p = ctypes.POINTER(ctypes.c_uint8)

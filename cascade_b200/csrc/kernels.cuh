@@ -65,6 +65,13 @@ int launch_copy(const uint64_t *d_srcs, const uint64_t *d_dsts,
                 const uint64_t *d_sizes, int n, uint64_t max_size,
                 cudaStream_t s, size_t smem_pad = 0);
 
+// n caches' K/V tensors (2 x layers descriptors each) into kv_manager wire
+// blocks d_dst[i] (null: skipped) (cascade_kv_serialize_batch).
+int launch_kv_serialize(const cascade_kv_tensor_t *d_src, int src_dtype,
+                        uint32_t layers, uint32_t heads, uint32_t seq,
+                        uint32_t head_dim, const uint64_t *d_dst, int n,
+                        cudaStream_t s);
+
 // kv_manager wire blocks d_src[i] (null: skipped) into 2 x layers FP16
 // tensors each (cascade_kv_deserialize_batch).
 int launch_kv_deserialize(const uint64_t *d_src, uint32_t layers,

@@ -217,6 +217,7 @@ __global__ void __launch_bounds__(kWThreads, 3)
     if (wbase >= g.vecs) continue;          // uniform across the warp
     const cascade_kv_tensor_t *ts = src + (uint64_t)b * 2 * g.L;
     uint8_t *out = reinterpret_cast<uint8_t *>(dst[b]);
+    if (!out) continue;                     // a block this call skips
     const bool out_al = ((uintptr_t)out & 15u) == 0;
     uint64_t addr[kWPer];
 #pragma unroll
@@ -397,6 +398,36 @@ extern "C" uint64_t cascade_kv_wire_bytes(uint32_t layers, uint32_t heads,
   return 18ull + 4ull * layers * heads * seq * head_dim;
 }
 
+namespace cb {
+
+int launch_kv_serialize(const cascade_kv_tensor_t *d_src, int src_dtype,
+                        uint32_t layers, uint32_t heads, uint32_t seq,
+                        uint32_t head_dim, const uint64_t *d_dst, int n,
+                        cudaStream_t s) {
+  CB_CHECK(src_dtype >= CASCADE_KV_FP16 && src_dtype <= CASCADE_KV_FP32,
+           CASCADE_ERR_INVALID, "src_dtype must be FP16, BF16 or FP32");
+  WireGeom g;
+  int rc = make_geom(layers, heads, seq, head_dim, &g);
+  if (rc != CASCADE_OK || n <= 0) return rc;
+  g.tiles = (uint32_t)div_up(g.vecs, kWTile);
+  const int grid = grid_for((uint64_t)n * g.tiles, 1, 3);
+  switch (src_dtype) {
+    case CASCADE_KV_FP16:
+      kv_serialize_kernel<0><<<grid, kWThreads, 0, s>>>(d_src, d_dst, n, g);
+      break;
+    case CASCADE_KV_BF16:
+      kv_serialize_kernel<1><<<grid, kWThreads, 0, s>>>(d_src, d_dst, n, g);
+      break;
+    default:
+      kv_serialize_kernel<2><<<grid, kWThreads, 0, s>>>(d_src, d_dst, n, g);
+  }
+  count_launches(1);
+  CB_CUDA(cudaGetLastError());
+  return CASCADE_OK;
+}
+
+}  // namespace cb
+
 extern "C" int cascade_kv_serialize_batch(const cascade_kv_tensor_t *d_src,
                                           int src_dtype, uint32_t layers,
                                           uint32_t heads, uint32_t seq,
@@ -412,25 +443,9 @@ extern "C" int cascade_kv_serialize_batch(const cascade_kv_tensor_t *d_src,
   if (rc != CASCADE_OK) return rc;
   if (n == 0) return CASCADE_OK;
   CB_CHECK(d_src && d_dst, CASCADE_ERR_INVALID, "null pointer argument");
-  g.tiles = (uint32_t)cb::div_up(g.vecs, cb::kWTile);
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const int grid = cb::grid_for((uint64_t)n * g.tiles, 1, 3);
-  switch (src_dtype) {
-    case CASCADE_KV_FP16:
-      cb::kv_serialize_kernel<0><<<grid, cb::kWThreads, 0, s>>>(d_src, d_dst,
-                                                                (int)n, g);
-      break;
-    case CASCADE_KV_BF16:
-      cb::kv_serialize_kernel<1><<<grid, cb::kWThreads, 0, s>>>(d_src, d_dst,
-                                                                (int)n, g);
-      break;
-    default:
-      cb::kv_serialize_kernel<2><<<grid, cb::kWThreads, 0, s>>>(d_src, d_dst,
-                                                                (int)n, g);
-  }
-  cb::count_launches(1);
-  CB_CUDA(cudaGetLastError());
-  return CASCADE_OK;
+  return cb::launch_kv_serialize(d_src, src_dtype, layers, heads, seq,
+                                 head_dim, d_dst, (int)n,
+                                 static_cast<cudaStream_t>(stream));
 }
 
 namespace cb {

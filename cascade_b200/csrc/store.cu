@@ -1257,6 +1257,128 @@ static int put_batch_locked(Store &st, size_t n, const uint64_t *h_ptrs,
   return finish_put(st, n, h_keys == nullptr, h_status, h_digests, n_stored);
 }
 
+// KVCacheStore.store for a batch of keyed KV caches whose wire blocks all
+// fit the HBM pool as raw payloads: the speculative put's allocation and
+// index steps with the serialise kernel as the payload writer, so each
+// cache is written once, straight into its pool slot.  Blocks whose slot
+// could not be allocated (size-class rounding) are serialised into the
+// KV staging buffer and placed again by the tiered path, as put_uploaded
+// places them.  Returns CASCADE_ERR_UNSUPPORTED, having done nothing, when
+// the batch does not qualify (no HBM tier, INT8 payloads, or no room).
+static int put_kv_locked(Store &st, size_t n, const uint8_t *h_keys,
+                         const uint32_t shape[4],
+                         const cascade_kv_tensor_t *d_src, int src_dtype,
+                         const uint8_t *h_prefix, uint8_t *h_status,
+                         uint64_t *n_stored) {
+  const uint64_t wb = cascade_kv_wire_bytes(shape[0], shape[1], shape[2],
+                                            shape[3]);
+  CB_CHECK(st.hbm && !q8_eligible(st, wb, false), CASCADE_ERR_UNSUPPORTED,
+           "a fused KV put needs raw payloads in an HBM tier");
+  CB_CHECK(st.gpu_used + n * payload_bytes(wb, false) <= st.pool_cap,
+           CASCADE_ERR_UNSUPPORTED, "the HBM pool cannot take the whole batch");
+  cudaStream_t s = st.s;
+  std::vector<uint64_t> zeros(n, 0), sizes(n, wb);
+  uint64_t mx = 0;
+  int rc = upload_batch(st, n, zeros.data(), sizes.data(), h_keys, &mx);
+  if (rc) return rc;
+  st.demoted.clear();
+  for (size_t i = 0; i < n; ++i) {
+    st.sc.h_req[i] = payload_bytes(wb, false);
+    st.sc.h_off[i] = kInvalidOffset;
+    st.sc.h_dst[i] = 0;
+    st.sc.h_flags[i] = kTierHbm | ((h_prefix && h_prefix[i] &&
+                                    st.cfg.dedup_enabled) ? kFlagPrefix : 0);
+  }
+  if ((rc = ensure_stack(st, size_class(std::max<uint64_t>(st.sc.h_req[0], 1)))))
+    return rc;
+  if (st.claimed + n > st.nslots / 2 && (rc = grow_index(st))) return rc;
+  CB_CUDA(cudaMemcpyAsync(st.sc.req, st.sc.h_req, n * 8, cudaMemcpyHostToDevice, s));
+  CB_CUDA(cudaMemcpyAsync(st.sc.hoff, st.sc.h_off, n * 8, cudaMemcpyHostToDevice, s));
+  CB_CUDA(cudaMemcpyAsync(st.sc.hdst, st.sc.h_dst, n * 8, cudaMemcpyHostToDevice, s));
+  CB_CUDA(cudaMemcpyAsync(st.sc.flags, st.sc.h_flags, n * 4, cudaMemcpyHostToDevice, s));
+  if ((rc = launch_pool_alloc(st.d_pool, st.sc.req, (int)n, st.sc.off, s)))
+    return rc;
+  prepare_kernel<<<(int)((n + 255) / 256), 256, 0, s>>>(
+      (int)n, st.sc.req, st.sc.off, st.sc.hoff, st.sc.hdst, st.sc.flags,
+      st.sc.sizes, (uint64_t)(uintptr_t)st.pool, st.sc.dst, st.sc.eff_raw,
+      st.sc.eff_q8);
+  count_launches(1);
+  CB_CUDA(cudaGetLastError());
+  // The payloads: every cache serialised into its slot (dst 0: no slot).
+  if ((rc = launch_kv_serialize(d_src, src_dtype, shape[0], shape[1],
+                                shape[2], shape[3], st.sc.dst, (int)n, s)))
+    return rc;
+  // The keys decide who stores, first in the batch winning.
+  CB_CUDA(cudaMemsetAsync(st.sc.err, 0, sizeof(int), s));
+  const uint64_t epoch = st.next_epoch;
+  st.next_epoch += n;
+  rc = launch_index_claim(st.slots, st.nslots - 1, st.sc.keys, 2, st.sc.seqs,
+                          (int)n, st.sc.slot, st.sc.err, s);
+  if (!rc) rc = launch_index_resolve(st.slots, st.sc.slot, st.sc.seqs, (int)n,
+                                     st.sc.status, s);
+  if (!rc) rc = launch_index_commit(st.slots, st.sc.slot, st.sc.status,
+                                    st.sc.off, st.sc.sizes, st.sc.flags,
+                                    st.sc.hdr, epoch, (int)n, s);
+  if (!rc) rc = launch_index_finalize(st.slots, st.sc.slot, st.sc.off,
+                                      st.sc.status, (int)n, s);
+  if (!rc) rc = launch_pool_free_unstored(st.d_pool, st.sc.req, st.sc.off,
+                                          st.sc.status, (int)n, s);
+  if (rc) return rc;
+  CB_CUDA(cudaMemcpyAsync(st.sc.h_status, st.sc.status, n,
+                          cudaMemcpyDeviceToHost, s));
+  CB_CUDA(cudaMemcpyAsync(st.sc.h_off, st.sc.off, n * 8,
+                          cudaMemcpyDeviceToHost, s));
+  CB_CUDA(cudaMemcpyAsync(st.sc.h_err, st.sc.err, sizeof(int),
+                          cudaMemcpyDeviceToHost, s));
+  CB_CUDA(cudaStreamSynchronize(s));
+  if ((rc = check_device_err(st))) return rc;
+  // Blocks that got no slot: serialised into staging, then placed again.
+  std::vector<size_t> retry;
+  for (size_t i = 0; i < n; ++i)
+    if (st.sc.h_status[i] == CASCADE_PUT_FAILED &&
+        st.sc.h_off[i] == kInvalidOffset)
+      retry.push_back(i);
+  if (retry.empty()) {
+    tally_put(st, n);
+    return finish_put(st, n, false, h_status, nullptr, n_stored);
+  }
+  const uint64_t pitch = (wb + 255) & ~uint64_t(255);
+  const size_t m = retry.size();
+  if ((rc = ensure_device_buf(st.d_kvstage, st.d_kvstage_cap, m * pitch, s)) ||
+      (rc = ensure_device_buf(st.d_kvsrc, st.d_kvsrc_cap, n * 8, s)))
+    return rc;
+  std::vector<uint64_t> stage_dst(n, 0), ptrs(m), msizes(m, wb);
+  std::vector<uint8_t> keys(16 * m), pre(m);
+  for (size_t k = 0; k < m; ++k) {
+    const size_t i = retry[k];
+    stage_dst[i] = (uint64_t)(uintptr_t)st.d_kvstage + k * pitch;
+    ptrs[k] = stage_dst[i];
+    std::memcpy(keys.data() + 16 * k, h_keys + 16 * i, 16);
+    pre[k] = h_prefix ? h_prefix[i] : 0;
+    st.sc.h_status[i] = kRetry;
+  }
+  uint64_t *d_stage_dst = reinterpret_cast<uint64_t *>(st.d_kvsrc);
+  CB_CUDA(cudaMemcpyAsync(d_stage_dst, stage_dst.data(), n * 8,
+                          cudaMemcpyHostToDevice, s));
+  if ((rc = launch_kv_serialize(d_src, src_dtype, shape[0], shape[1],
+                                shape[2], shape[3], d_stage_dst, (int)n, s)))
+    return rc;
+  tally_put(st, n);
+  std::vector<uint8_t> status(st.sc.h_status, st.sc.h_status + n);
+  if ((rc = upload_batch(st, m, ptrs.data(), msizes.data(), keys.data(), &mx)))
+    return rc;
+  if ((rc = put_uploaded(st, m, false, pre.data(), mx, false, 1))) return rc;
+  for (size_t k = 0; k < m; ++k) status[retry[k]] = st.sc.h_status[k];
+  // Report the whole batch: statuses and the stored count.
+  uint64_t stored = 0;
+  for (size_t i = 0; i < n; ++i) {
+    if (h_status) h_status[i] = status[i];
+    stored += status[i] != CASCADE_PUT_FAILED ? 1 : 0;
+  }
+  if (n_stored) *n_stored = stored;
+  return CASCADE_OK;
+}
+
 // ----------------------------------------------------------------- get
 // Looks the keys up (touching LRU epochs when `touch`); infos land in
 // st.sc.h_info.  Keys must already be in st.sc.keys on the device.
@@ -3017,6 +3139,26 @@ extern "C" int cascade_store_get_batch(cascade_store_t *s, size_t n,
   if (int rc = join_caller(st, stream)) return rc;
   return cb::get_batch_locked(st, n, h_keys, h_out_ptrs, h_out_caps, h_sizes,
                               h_found, n_found);
+}
+
+extern "C" int cascade_store_put_kv_batch(
+    cascade_store_t *s, size_t n, const uint8_t *h_keys, uint32_t layers,
+    uint32_t heads, uint32_t seq, uint32_t head_dim,
+    const cascade_kv_tensor_t *d_src, int src_dtype, const uint8_t *h_prefix,
+    uint8_t *h_status, void *stream, uint64_t *n_stored) {
+  STORE_ENTRY(s);
+  if (n_stored) *n_stored = 0;
+  if (n == 0) return CASCADE_OK;
+  CB_CHECK(h_keys && d_src, CASCADE_ERR_INVALID, "null argument");
+  CB_CHECK(n <= (size_t)INT32_MAX, CASCADE_ERR_INVALID, "batch too large");
+  CB_CHECK(layers && heads && seq && head_dim, CASCADE_ERR_INVALID,
+           "layers, heads, seq_len and head_dim must be positive");
+  CB_CHECK(src_dtype >= CASCADE_KV_FP16 && src_dtype <= CASCADE_KV_FP32,
+           CASCADE_ERR_INVALID, "src_dtype must be FP16, BF16 or FP32");
+  if (int rc = join_caller(st, stream)) return rc;
+  const uint32_t shape[4] = {layers, heads, seq, head_dim};
+  return cb::put_kv_locked(st, n, h_keys, shape, d_src, src_dtype, h_prefix,
+                           h_status, n_stored);
 }
 
 extern "C" int cascade_store_get_kv_batch(

@@ -49,6 +49,9 @@ _lib.register("cascade_kv_serialize_batch", _int,
               [_vp, _int, _u32, _u32, _u32, _u32, _vp, _sz, _vp])
 _lib.register("cascade_kv_deserialize_batch", _int,
               [_vp, _u32, _u32, _u32, _u32, _vp, _sz, _vp])
+_lib.register("cascade_store_put_kv_batch", _int,
+              [_vp, _sz, _vp, _u32, _u32, _u32, _u32, _vp, _int, _vp, _vp,
+               _vp, ctypes.POINTER(ctypes.c_uint64)])
 _lib.register("cascade_store_get_kv_batch", _int,
               [_vp, _sz, _vp, _u32, _u32, _u32, _u32, _vp, _vp, _vp,
                ctypes.POINTER(ctypes.c_uint64)])
@@ -243,16 +246,46 @@ def deserialize_kv_cache(data, header=None) -> tuple:
     return deserialize_kv_caches([data], header=header)[0]
 
 
+def _sources(caches):
+    """(layers, heads, seq, head_dim, device, dtype, descriptor tensor) of a
+    batch of caches of one shape."""
+    per = [extract_kv_pairs(c) for c in caches]
+    geo = [_geometry(p) for p in per]
+    if any(g != geo[0] for g in geo):
+        raise ValueError("every cache must have one shape, dtype and device")
+    L, H, S, D, dev, dt = geo[0]
+    views = [_heads_seq_dim(t) for p in per for kv in p for t in kv]
+    return L, H, S, D, dev, dt, _descriptors(views, dev)
+
+
 def store_kv_caches(store, block_ids: Sequence, caches: Sequence,
                     is_prefix=None):
     """KVCacheStore.store (kv_manager.py:116-127) for a batch, without host
-    copies: the caches (one shape) are serialised in one launch and put
-    under their ids (prefix hashes) with one put_batch.  ``store``: a
-    CascadeStore.  Returns the per-block put status codes."""
+    copies.  ``store``: a CascadeStore.  When every wire block fits the HBM
+    pool as a raw payload, one store call (cascade_store_put_kv_batch)
+    serialises each cache straight into its pool slot; otherwise the caches
+    are serialised in one launch and put with put_batch.  Returns the
+    per-block put status codes."""
+    import numpy as np
     if len(block_ids) != len(caches):
         raise ValueError("one id per cache")
-    if not caches:
+    n = len(caches)
+    if n == 0:
         return []
+    L, H, S, D, dev, dt, src = _sources(caches)
+    keys = np.frombuffer(b"".join(store._key(b) for b in block_ids),
+                         dtype=np.uint8).copy()
+    pf = (np.array([1 if p else 0 for p in is_prefix], dtype=np.uint8)
+          if is_prefix is not None else None)
+    status = np.zeros(n, np.uint8)
+    nst = ctypes.c_uint64(0)
+    rc = _lib.load().cascade_store_put_kv_batch(
+        store._h, n, keys.ctypes.data, L, H, S, D, src.data_ptr(),
+        _dtype_code(dt), pf.ctypes.data if pf is not None else None,
+        status.ctypes.data, _stream(dev), ctypes.byref(nst))
+    if rc != _lib.CASCADE_ERR_UNSUPPORTED:
+        check(rc)
+        return status
     rows = serialize_kv_caches(caches)
     return store.put_batch(rows, keys=list(block_ids), is_prefix=is_prefix,
                            return_status=True)[1]

@@ -301,6 +301,23 @@ int cascade_store_get_batch(cascade_store_t *s, size_t n,
                             uint8_t *h_found, void *stream,
                             uint64_t *n_found);
 
+/* KVCacheStore.store (inference_benchmark/kv_manager.py:116-127) for n
+ * keyed KV caches of one shape (descriptors and src_dtype as
+ * cascade_kv_serialize_batch), when every wire block fits the HBM pool as a
+ * raw payload: each cache is serialised straight into its pool slot, with
+ * the statuses, dedup and counters of cascade_store_put_batch.  A block
+ * whose slot cannot be allocated (size-class rounding) is serialised into
+ * a staging buffer and placed in the next tier, as put_batch places it.
+ * Returns CASCADE_ERR_UNSUPPORTED, storing nothing, when the store has no
+ * HBM tier, keeps INT8 payloads in HBM, or lacks room for the batch: the
+ * caller then serialises and uses cascade_store_put_batch.  Synchronous. */
+int cascade_store_put_kv_batch(cascade_store_t *s, size_t n,
+                               const uint8_t *h_keys, uint32_t layers,
+                               uint32_t heads, uint32_t seq, uint32_t head_dim,
+                               const cascade_kv_tensor_t *d_src, int src_dtype,
+                               const uint8_t *h_prefix, uint8_t *h_status,
+                               void *stream, uint64_t *n_stored);
+
 /* KVCacheStore.load (inference_benchmark/kv_manager.py:135-156) for n keys
  * whose blocks are kv_manager wire blocks of one shape: get_batch and
  * deserialize_kv_cache in one call, into the caller's 2 x layers FP16

@@ -274,3 +274,46 @@ def test_load_through_the_dram_tier_and_int8():
                 assert torch.equal(v.view(torch.int16), v0.view(torch.int16))
     finally:
         store.close()
+
+
+def test_fused_put_dedup_and_slot_retry():
+    """cascade_store_put_kv_batch: first of a batch wins, a known id is a
+    dedup hit, and caches whose pool slot cannot be allocated (a pool sized
+    by bytes, 144 KiB size classes for 128 KiB + 18-byte blocks) are placed
+    in the DRAM tier through the staging buffer; every cache reads back."""
+    shape = (2, 8, 16, 128)
+    wb = kvwire.wire_bytes(*shape)
+    caches = [_cache(90 + i, *shape) for i in range(16)]
+    cfg = cc.CascadeConfig()
+    cfg.gpu_capacity_bytes = 16 * wb
+    cfg.shm_capacity_bytes = 16 << 20
+    store = cc.CascadeStore(cfg)
+    try:
+        ids = [f"k{i}" for i in range(16)]
+        st = kvwire.store_kv_caches(store, ids, caches)
+        assert (np.asarray(st) == 0).all()
+        s = store.get_stats()
+        assert s.shm_puts >= 1 and s.gpu_used + s.shm_used > 0
+        got = kvwire.load_kv_caches(store, ids, *shape)
+        for g, c in zip(got, caches):
+            for (k, v), (k0, v0) in zip(g, c):
+                assert torch.equal(k, k0) and torch.equal(v, v0)
+    finally:
+        store.close()
+    cfg = cc.CascadeConfig()
+    cfg.gpu_capacity_bytes = 64 << 20
+    cfg.shm_capacity_bytes = 0
+    store = cc.CascadeStore(cfg)
+    try:
+        st = kvwire.store_kv_caches(store, ["x", "y", "x"],
+                                    [caches[0], caches[1], caches[2]])
+        assert list(np.asarray(st)) == [0, 0, 2]
+        st = kvwire.store_kv_caches(store, ["y"], [caches[3]])
+        assert list(np.asarray(st)) == [1]
+        assert store.get_stats().dedup_hits == 2
+        got = kvwire.load_kv_caches(store, ["x", "y"], *shape)
+        for g, c in zip(got, (caches[0], caches[1])):
+            for (k, v), (k0, v0) in zip(g, c):
+                assert torch.equal(k, k0) and torch.equal(v, v0)
+    finally:
+        store.close()
