@@ -495,6 +495,50 @@ def section_dedup(ctx, args):
             "hits_exact": total_hits == expected}
 
 
+def reference_kv_manager_sample(ctx, blocks, wire, L, H, S, D, m=16):
+    """The reference's own serialize_kv_cache / deserialize_kv_cache
+    (inference_benchmark/kv_manager.py, the copy `make -C oracle callers`
+    stages byte for byte) on m of the caches, from and to the GPU as
+    KVCacheStore.store / load call them: per-cache time and whether its
+    bytes equal the device wire blocks."""
+    import importlib
+    import time
+    callers = os.path.join(ROOT, "baseline", "_ref", "callers")
+    if not os.path.exists(os.path.join(callers, "inference_benchmark",
+                                       "kv_manager.py")):
+        return {"unavailable": "the reference's callers are not staged "
+                               "(make -C oracle callers)"}
+    sys.path.insert(0, callers)
+    try:
+        kv = importlib.import_module("inference_benchmark.kv_manager")
+    finally:
+        sys.path.remove(callers)
+    T = H * S * D
+    rows = [blocks[i].view(ctx.torch.float16) for i in range(m)]
+    caches = [tuple((r[2 * l * T:(2 * l + 1) * T].view(1, H, S, D),
+                     r[(2 * l + 1) * T:(2 * l + 2) * T].view(1, H, S, D))
+                    for l in range(L)) for r in rows]
+    ctx.torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    blobs = [kv.serialize_kv_cache(c) for c in caches]
+    t1 = time.perf_counter()
+    for b in blobs:
+        kv.deserialize_kv_cache(b, device=ctx.dev)
+    ctx.torch.cuda.synchronize()
+    t2 = time.perf_counter()
+    wb = len(blobs[0])
+    equal = all(blobs[i] == bytes(wire[i, :wb].cpu().numpy())
+                for i in range(min(4, m)))
+    nbytes = m * (wb - 18)
+    return {"caches": m, "serialize_ms_per_cache": (t1 - t0) * 1e3 / m,
+            "deserialize_ms_per_cache": (t2 - t1) * 1e3 / m,
+            "serialize_gbps": nbytes / (t1 - t0) / 1e9,
+            "deserialize_gbps": nbytes / (t2 - t1) / 1e9,
+            "bytes_equal_device_wire": equal,
+            "what": "the reference's kv_manager functions (.cpu() + bytes "
+                    "join; numpy copies back to the GPU), host wall clock"}
+
+
 def section_kvwire(ctx, blocks, hbm, hbm_src):
     """The KV-cache wire format (kv_manager.serialize_kv_cache /
     deserialize_kv_cache) on the device for the headline's blocks: each
@@ -535,6 +579,7 @@ def section_kvwire(ctx, blocks, hbm, hbm_src):
                   D, d_desc.data_ptr(), n, ctx.stream)
 
     ser_ms, _ = ctx.timed(ser, 2, 5)
+    ref = reference_kv_manager_sample(ctx, blocks, wire, L, H, S, D)
     head = struct.pack(kvwire.HEADER_FMT, L, H, S, D, 0)
     heads_ok = bool((wire[:, :18].cpu().numpy()
                      == np.frombuffer(head, np.uint8)).all())
@@ -616,6 +661,7 @@ def section_kvwire(ctx, blocks, hbm, hbm_src):
         "headers_equal": heads_ok, "payload_equal_sample": payload_ok,
         "round_trip_bit_exact_sample": round_ok,
         "launches_per_call": 1,
+        "reference_kv_manager": ref,
         "store": {"what": "KVCacheStore.store of every cache into an "
                           "emptied raw HBM store: cascade_store_put_kv_batch "
                           "(each cache serialised straight into its pool "
