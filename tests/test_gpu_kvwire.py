@@ -317,3 +317,42 @@ def test_fused_put_dedup_and_slot_retry():
                 assert torch.equal(k, k0) and torch.equal(v, v0)
     finally:
         store.close()
+
+
+@pytest.mark.parametrize("dedup", [True, False])
+def test_fused_put_matches_put_batch(dedup):
+    """The one-call put and serialise + put_batch give the same statuses
+    and counters, with repeated ids, prefix flags and BF16 sources."""
+    shape = (3, 4, 9, 64)
+    caches = [_cache(200 + i, *shape, dtype=torch.bfloat16) for i in range(6)]
+    ids = ["a", "b", "a", "c", "b", "d"]
+    pre = [True, False, True, False, False, True]
+    results = []
+    for fused in (True, False):
+        cfg = cc.CascadeConfig()
+        cfg.gpu_capacity_bytes = 64 << 20
+        cfg.shm_capacity_bytes = 16 << 20
+        cfg.dedup_enabled = dedup
+        store = cc.CascadeStore(cfg)
+        try:
+            if fused:
+                st = kvwire.store_kv_caches(store, ids, caches, is_prefix=pre)
+            else:
+                rows = kvwire.serialize_kv_caches(caches)
+                st = store.put_batch(rows, keys=ids, is_prefix=pre,
+                                     return_status=True)[1]
+            s = store.get_stats()
+            got = kvwire.load_kv_caches(store, ["a", "b", "c", "d"], *shape)
+            counters = {f: getattr(s, f) for f in cc._STAT_FIELDS}
+            results.append((list(np.asarray(st)), counters, got))
+        finally:
+            store.close()
+    (st0, s0, g0), (st1, s1, g1) = results
+    assert st0 == st1 and s0 == s1
+    for a, b in zip(g0, g1):
+        for (k, v), (k0, v0) in zip(a, b):
+            assert torch.equal(k, k0) and torch.equal(v, v0)
+    # the stored caches are the first of each id, rounded to FP16
+    for g, c in zip(g0, (caches[0], caches[1], caches[3], caches[5])):
+        for (k, v), (k0, v0) in zip(g, c):
+            assert torch.equal(k, k0.half()) and torch.equal(v, v0.half())
