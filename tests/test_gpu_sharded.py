@@ -469,6 +469,10 @@ def _single_main(rank, world, port, out_dir, sliced=False):
         if sliced:     # all four rounds' blocks in one batch of 4 slices
             mine = [b for rnd in range(4) for b in _demote_blocks(0, rnd)]
             blocks = torch.from_numpy(np.stack(mine)).to(dev)
+            # a batch that fits the empty pool stays one round, even above
+            # the 4/5 that slices fill; one that does not fit is cut
+            assert store.ops.slices(blocks[:18], False)[0] == [0, 18]
+            assert store.ops.slices(blocks[:21], False)[0] == [0, 16, 21]
             assert store.ops.slices(blocks, False)[0] == [0, 16, 32, 48, 64]
             stored, status, digests = store.put_batch(blocks,
                                                       return_status=True)
